@@ -1,0 +1,411 @@
+#!/usr/bin/env python
+"""FM-head benchmark: latent xRT of one engine tick, 64 concurrent requests per GPU.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference] [--workload cfg2]
+
+A step is one FM-head tick for every request on the GPU: each request graduates
+its previous patch's 17 rows into its paged per-(layer, step) K/V cache and
+runs the 4 MeanFlow solver steps (prefixes of 17*U{0..120}
+rows, 16-row pages, seeded synthetic DiT).  xRT = requests * 16 frames * 0.04 s
+per tick / tick time (``scripts/bench_engine.py:25-27,133-143`` of the reference).
+Cache lengths are held fixed across timed ticks so every tick does the same
+work.  The K/V pool (~15 GB) and the weights (~465 MB) exceed the 126 MB L2, so
+no flush is needed between ticks.
+
+Multi-GPU (torchrun): one process per GPU, each with its own head and 64
+requests (weak scaling, no collective on the data path); time = max over ranks.
+
+``--impl reference`` times the reference's algorithm on the host CPU (the oracle
+restatement of the reference's cache path; the reference itself is Python with
+no GPU MeanFlow cache head) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+AUDIO_S_PER_PATCH = 16 * 0.04
+METRIC = "FM-head latent xRT (audio-s/s) at conc 64 per GPU"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4"])
+    ap.add_argument("--cpu-sample", type=int, default=8, help="requests in the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def workload_batch(name: str, rank: int):
+    from nanovllm_dots_b200 import synthetic as syn
+    b = syn.config_batch(name)
+    if rank:
+        # same distribution, an independent draw per rank
+        g = torch.Generator().manual_seed(1000 + rank)
+        hi = {"cfg1": 33, "cfg2": 121}.get(name)
+        if hi is not None:
+            pp = torch.randint(0, hi, (b.n,), generator=g).tolist()
+        else:
+            long_ = torch.rand(b.n, generator=g) < 0.25
+            pp = torch.where(long_, torch.randint(200, 321, (b.n,), generator=g),
+                             torch.randint(0, 61, (b.n,), generator=g)).tolist()
+        b = syn.make_batch(b.n, pp, seed=1000 + rank)
+    return b
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out = self.proc.communicate(timeout=5)[0]
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        if not self.proc or not getattr(self, "out", ""):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[2:6]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- #
+# CPU baseline (the oracle restatement of the reference cache path)            #
+# --------------------------------------------------------------------------- #
+def cpu_tick_seconds(weights, batch, idx):
+    from nanovllm_dots_b200 import synthetic as syn
+    from oracle import dit_oracle as O
+    cfg = syn.BASE
+    kvs = {}
+    for i in idx:
+        g = torch.Generator().manual_seed(99 + i)
+        P = batch.prefix_rows[i]
+        kvs[i] = torch.randn(cfg.nfe, cfg.layers, 2, P, cfg.heads, cfg.head_dim, generator=g) * 0.5
+    t0 = time.perf_counter()
+    O.tick_batch(weights, batch, kv_fn=lambda i: kvs[i], indices=idx)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(weights, batch, n_sample):
+    idx = list(range(min(n_sample, batch.n)))
+    secs = cpu_tick_seconds(weights, batch, idx)
+    mean_p = sum(batch.prefix_rows[i] for i in idx) / len(idx)
+    return {"value": round(len(idx) * AUDIO_S_PER_PATCH / secs, 4), "unit": "audio-s/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(idx)} request-ticks of the same workload (mean prefix {mean_p:.0f} "
+                      f"rows), fp32 eager torch on the host, {secs:.1f} s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from nanovllm_dots_b200 import synthetic as syn
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = syn.make_weights(syn.BASE)
+    b = workload_batch(args.workload, 0)
+    per_step = 2
+    times = []
+    for s in range(args.warmup + args.steps):
+        idx = [(s * per_step + j) % b.n for j in range(per_step)]
+        t = cpu_tick_seconds(w, b, idx)
+        if s >= args.warmup:
+            times.append(t)
+    tot = sum(times)
+    val = args.steps * per_step * AUDIO_S_PER_PATCH / tot
+    line = {"metric": METRIC, "value": round(val, 4), "unit": "audio-s/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000 * tot / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "requests_per_step": per_step,
+                       "note": "host-CPU run of the reference algorithm (cache path), bounded "
+                               "sample of the workload's requests per step"},
+            "cpu_baseline": {"value": round(val, 4), "unit": "audio-s/s",
+                             "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{per_step} request-ticks per step"},
+            "e2e": {"value": round(val, 4), "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- #
+# GPU arm                                                                      #
+# --------------------------------------------------------------------------- #
+def launches_per_tick(cfg, raw_ext=True):
+    per_step = 2 + cfg.layers * 8 + 2
+    return 3 + 1 + 1 + (2 if raw_ext else 0) + cfg.nfe * per_step
+
+
+def run_b200(args, rank, world):
+    from nanovllm_dots_b200 import _lib
+    from nanovllm_dots_b200 import synthetic as syn
+    from nanovllm_dots_b200.fm_head import B200FMHead, FMRequest
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = syn.BASE
+    b = workload_batch(args.workload, rank)
+    n = b.n
+    max_pages = max(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows)
+    num_pages = sum(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows) + 8
+    weights = syn.make_weights(cfg)
+    head = B200FMHead(weights, cfg, num_pages=num_pages, max_pages_per_req=max_pages,
+                      max_requests=n, device=dev)
+    # cached prefixes: N(0, 0.5^2) K/V drawn on the device straight into the pool
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    chunk = 1 << 28
+    flat = head.pool
+    for s in range(0, flat.numel(), chunk):
+        e = min(flat.numel(), s + chunk)
+        flat[s:e] = (torch.randn(e - s, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    rids = list(range(n))
+    for i in rids:
+        head.pages.ensure(i, b.prefix_rows[i])
+        head.requests[i] = FMRequest(i, b.prefix_rows[i])
+    cl, ne, bt = head.prepare(rids, [cfg.stride] * n)
+    d = lambda t: t.to(dev).contiguous()
+    noise, cond, ph, pl = d(b.noise), d(b.cond), d(b.prev_hidden), d(b.prev_latent)
+    out = torch.empty(n, cfg.latent_patch, cfg.latent_dim, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def tick():
+        head.launch(noise=noise, act_hidden=cond, ext_hidden=ph, ext_latent=pl, cache_len=cl,
+                    n_extend=ne, block_table=bt, out=out)
+
+    for _ in range(args.warmup):
+        tick()
+    torch.cuda.synchronize()
+    head.check_errors()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            tick()
+        e1.record(stream)
+        e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    head.check_errors()
+
+    # ---- end to end through the C ABI with host buffers (pinned), per-tick copies
+    pin = lambda t: t.contiguous().pin_memory()
+    h_noise, h_cond, h_ph, h_pl = pin(b.noise), pin(b.cond), pin(b.prev_hidden), pin(b.prev_latent)
+    h_cl, h_ne, h_bt = pin(cl.cpu()), pin(ne.cpu()), pin(bt.cpu())
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dn, dc, dph, dpl = [torch.empty_like(x) for x in (noise, cond, ph, pl)]
+    dcl, dne, dbt = torch.empty_like(cl), torch.empty_like(ne), torch.empty_like(bt)
+    h2d = sum(x.numel() * x.element_size() for x in (h_noise, h_cond, h_ph, h_pl, h_cl, h_ne, h_bt))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_tick():
+        for dst, src in ((dn, h_noise), (dc, h_cond), (dph, h_ph), (dpl, h_pl), (dcl, h_cl),
+                         (dne, h_ne), (dbt, h_bt)):
+            dst.copy_(src, non_blocking=True)
+        head.launch(noise=dn, act_hidden=dc, ext_hidden=dph, ext_latent=dpl, cache_len=dcl,
+                    n_extend=dne, block_table=dbt, out=out)
+        h_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_tick()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        e2e_tick()
+    f1.record(stream)
+    f1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+
+    # ---- per-kernel timing of the dominant kernels (same shapes, same stream)
+    hbm, tflops, peak_kind = load_peaks()
+    L = _lib.lib()
+    kern = {}
+    R = 2 * cfg.stride * n
+    ws = head.workspace
+    wsb = L.dfm_attention_workspace_size(n, max_pages, cfg.heads)
+    aws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    q = torch.randn(R, cfg.hidden, device=dev).to(torch.bfloat16)
+    ao = torch.empty_like(q)
+    planes = cfg.layers * cfg.nfe * 2
+
+    def attn_once():
+        _lib.check(L.dfm_paged_attention(q.data_ptr(), ao.data_ptr(), head.pool.data_ptr(),
+                                         num_pages, planes, cfg.heads, 0, 1, cl.data_ptr(),
+                                         ne.data_ptr(), bt.data_ptr(), max_pages, n,
+                                         aws.data_ptr(), wsb, _lib.c_void_p(stream.cuda_stream)),
+                   "dfm_paged_attention")
+
+    keys = sum(p + 2 * cfg.stride for p in b.prefix_rows)
+    attn_bytes = keys * cfg.heads * cfg.head_dim * 2 * 2 + 2 * R * cfg.hidden * 2
+    kern["attention"] = {"fn": attn_once, "bytes": attn_bytes, "per_tick": cfg.layers * cfg.nfe,
+                         "bound": "hbm"}
+    a_x = torch.randn(R, cfg.hidden, device=dev).to(torch.bfloat16)
+    a_u = torch.randn(R, cfg.ffn, device=dev).to(torch.bfloat16)
+    shapes = {"qkv": (a_x, head.w["qkv_w"][0], 3 * cfg.hidden, cfg.hidden, False),
+              "fc1": (a_x, head.w["fc1_w"][0], cfg.ffn, cfg.hidden, True),
+              "fc2": (a_u, head.w["fc2_w"][0], cfg.hidden, cfg.ffn, False),
+              "o_proj": (a_x, head.w["o_w"][0], cfg.hidden, cfg.hidden, False)}
+    for nm, (A, Wt, N, K, gelu) in shapes.items():
+        o_buf = torch.empty(R, N, device=dev, dtype=torch.bfloat16)
+
+        def f(A=A, Wt=Wt, N=N, K=K, gelu=gelu, o_buf=o_buf):
+            _lib.check(L.dfm_linear(A.data_ptr(), K, R, K, Wt.data_ptr(), K, N, None,
+                                    o_buf.data_ptr(), 0, int(gelu),
+                                    _lib.c_void_p(stream.cuda_stream)), "dfm_linear")
+        kern[nm] = {"fn": f, "flops": 2.0 * R * N * K, "per_tick": cfg.layers * cfg.nfe,
+                    "bound": "tensor"}
+    reps = 20
+    for nm, k in kern.items():
+        for _ in range(3):
+            k["fn"]()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(reps):
+            k["fn"]()
+        s1.record(stream)
+        s1.synchronize()
+        k["us"] = s0.elapsed_time(s1) * 1000 / reps
+    summary = {}
+    for nm, k in kern.items():
+        if k["bound"] == "hbm":
+            ach, peak, unit = k["bytes"] / (k["us"] * 1e-6) / 1e9, hbm, "GB/s"
+        else:
+            ach, peak, unit = k["flops"] / (k["us"] * 1e-6) / 1e12, tflops, "TFLOP/s"
+        summary[nm] = {"us": round(k["us"], 2), "achieved": round(ach, 1), "unit": unit,
+                       "frac": round(ach / peak, 4),
+                       "tick_share_est": round(k["us"] * k["per_tick"] / (ms * 1000), 4)}
+    dom = max(summary, key=lambda x: summary[x]["tick_share_est"])
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get(dom)
+    dk = kern[dom]
+    roof = {"kernel": dom, "bound": dk["bound"], "achieved": summary[dom]["achieved"],
+            "peak": hbm if dk["bound"] == "hbm" else tflops, "unit": summary[dom]["unit"],
+            "frac": summary[dom]["frac"], "traffic": traffic,
+            "algorithmic_per_launch": dk.get("bytes", dk.get("flops")),
+            "peak_source": f"{peak_kind} ({'hbm_gbs' if dk['bound'] == 'hbm' else 'bf16_tflops'})"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(weights, b, args.cpu_sample)
+
+    total_req = n * world
+    value = total_req * AUDIO_S_PER_PATCH / (ms / 1000)
+    e2e_val = total_req * AUDIO_S_PER_PATCH / (e2e_ms / 1000)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random-init DiT, N(0,1) inputs, N(0,0.5^2) cached K/V)",
+                "config": {"workload": args.workload, "requests_per_gpu": n,
+                           "mean_prefix_rows": round(sum(b.prefix_rows) / n, 1),
+                           "nfe": cfg.nfe, "layers": cfg.layers, "page_rows": cfg.page_rows,
+                           "l2": "inputs larger than L2 (K/V pool and weights), no flush",
+                           "parallelism": f"request-sharded x{world}"},
+                "e2e": {"value": round(e2e_val, 2), "unit": "audio-s/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "ms_per_step": round(e2e_ms, 4)},
+                "gpu_launches": launches_per_tick(cfg) * args.steps,
+                "roofline": roof, "kernels": summary, "clocks": clk.summary(),
+                "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    head.close()
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
+    try:
+        run_b200(args, rank, world)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

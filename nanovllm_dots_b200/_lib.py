@@ -1,0 +1,98 @@
+"""ctypes binding of ``libdfm.so`` (declarations in ``include/dfm.h``).
+
+The library is built in-tree by ``nanovllm_dots_b200.build``.  There is no
+fallback: if the shared object is missing or fails to load, every entry point
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_float, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libdfm.so")
+
+DFM_OK = 0
+DEVERR_BITS = {1: "timeout", 2: "page", 4: "len"}
+
+EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "dfm_read_error",
+           "dfm_destroy", "dfm_error_string", "dfm_linear", "dfm_attention_workspace_size",
+           "dfm_paged_attention")
+
+
+class DfmConfig(ctypes.Structure):
+    _fields_ = [("layers", c_int32), ("hidden", c_int32), ("heads", c_int32),
+                ("head_dim", c_int32), ("ffn", c_int32), ("latent_dim", c_int32),
+                ("latent_patch", c_int32), ("hidden_patch", c_int32), ("cond_dim", c_int32),
+                ("nfe", c_int32), ("page_rows", c_int32), ("num_pages", c_int32),
+                ("max_pages_per_req", c_int32), ("max_requests", c_int32), ("ln_eps", c_float),
+                ("precision", c_int32)]
+
+
+WEIGHT_FIELDS = ("input_w", "input_b", "temb_w1", "temb_b1", "temb_w2", "temb_b2", "demb_w1",
+                 "demb_b1", "demb_w2", "demb_b2", "ada_w", "ada_b", "qkv_w", "qk_norm", "o_w",
+                 "o_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "final_w", "final_b", "coord_w",
+                 "coord_b", "hidden_w", "hidden_b", "latent_w", "latent_b", "rope_inv_freq")
+
+
+class DfmWeights(ctypes.Structure):
+    _fields_ = [(f, c_void_p) for f in WEIGHT_FIELDS]
+
+
+class DfmBatch(ctypes.Structure):
+    _fields_ = [("n", c_int32), ("noise", c_void_p), ("act_hidden", c_void_p),
+                ("act_row", c_void_p), ("ext_hidden", c_void_p), ("ext_latent", c_void_p),
+                ("ext_rows", c_void_p), ("g_cond", c_void_p), ("cache_len", c_void_p),
+                ("n_extend", c_void_p), ("block_table", c_void_p), ("kv_pool", c_void_p),
+                ("out", c_void_p)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the FM-head library; raise if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"FM-head CUDA library not built: {LIB_PATH} is missing "
+                           "(run `python -m nanovllm_dots_b200.build`)")
+    L = ctypes.CDLL(LIB_PATH)
+    L.dfm_create.argtypes = [POINTER(DfmConfig), POINTER(DfmWeights), POINTER(c_void_p)]
+    L.dfm_create.restype = c_int32
+    L.dfm_workspace_size.argtypes = [c_void_p]
+    L.dfm_workspace_size.restype = c_size_t
+    L.dfm_pool_bytes.argtypes = [POINTER(DfmConfig)]
+    L.dfm_pool_bytes.restype = c_size_t
+    L.dfm_step.argtypes = [c_void_p, POINTER(DfmBatch), c_void_p, c_size_t, c_void_p]
+    L.dfm_step.restype = c_int32
+    L.dfm_read_error.argtypes = [c_void_p, c_void_p, c_void_p, POINTER(c_uint32)]
+    L.dfm_read_error.restype = c_int32
+    L.dfm_destroy.argtypes = [c_void_p]
+    L.dfm_destroy.restype = c_int32
+    L.dfm_error_string.argtypes = [c_int32]
+    L.dfm_error_string.restype = ctypes.c_char_p
+    L.dfm_linear.argtypes = [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_int32,
+                             c_void_p, c_void_p, c_int32, c_int32, c_void_p]
+    L.dfm_linear.restype = c_int32
+    L.dfm_attention_workspace_size.argtypes = [c_int32, c_int32, c_int32]
+    L.dfm_attention_workspace_size.restype = c_size_t
+    L.dfm_paged_attention.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                      c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32,
+                                      c_int32, c_void_p, c_size_t, c_void_p]
+    L.dfm_paged_attention.restype = c_int32
+    _lib = L
+    return L
+
+
+def check(rc: int, what: str) -> None:
+    if rc != DFM_OK:
+        msg = lib().dfm_error_string(rc).decode()
+        raise RuntimeError(f"{what} failed: {msg} (code {rc})")
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (None for None)."""
+    return None if t is None else t.data_ptr()

@@ -1,0 +1,543 @@
+// Host side of the FM-head C ABI (include/dfm.h): handle, workspace layout,
+// TMA descriptor encoding and the per-tick launch sequence.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "../../include/dfm.h"
+#include "attn.cuh"
+#include "ew.cuh"
+#include "gemm.cuh"
+
+using namespace dfm;
+
+namespace {
+
+constexpr int kH = 1024;
+constexpr int kStride = 17;      // hidden_patch + latent_patch
+constexpr int kSlot = 2 * kStride;  // graduating + active rows per request
+
+// ---------------------------------------------------------------- TMA encoding
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 K-major operand [rows, cols] with row stride ld elements, box
+// {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
+bool map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+            uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The K/V pool as a 5-D tensor [planes][pages][heads][16][64]; one box is one
+// (page, head) block of 16 rows x 64 dims.
+bool map_pool(CUtensorMap* m, const void* base, int num_pages, int heads, int planes) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  cuuint64_t dims[5] = {64, 16, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(num_pages),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[4] = {128, 2048, 2048ull * heads, 2048ull * heads * num_pages};
+  cuuint32_t box[5] = {64, 16, 1, 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- launches
+template <int BN, int ST, class Epi>
+cudaError_t gemm(const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K, const Epi& e,
+                 uint32_t* err, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  auto fn = gemm_bf16_tn<BN, ST, Epi>;
+  constexpr int smem = GemmShape<BN, ST>::SMEM;
+  cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (r != cudaSuccess) return r;
+  dim3 grid((M + GEMM_BM - 1) / GEMM_BM, N / BN);
+  fn<<<grid, GEMM_THREADS, smem, s>>>(a, b, M, K, e, err);
+  return cudaGetLastError();
+}
+
+constexpr RowMap kIdentity{1 << 30, 0, 0};
+
+EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMap m = kIdentity) {
+  EpiStore e;
+  e.out = out;
+  e.ldo = ldo;
+  e.out_f32 = f32 ? 1 : 0;
+  e.bias = bias;
+  e.gelu = gelu ? 1 : 0;
+  e.omap = m;
+  return e;
+}
+
+int attn_chunks(int max_pages) { return (max_pages * 16 + kSlot + ATT_CH - 1) / ATT_CH; }
+
+cudaError_t launch_attention(const CUtensorMap& pool_map, const AttnParams& p, cudaStream_t s) {
+  cudaError_t r = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       ATT_SMEM);
+  if (r != cudaSuccess) return r;
+  dim3 grid(p.n * p.MC, p.heads);
+  attn_kernel<<<grid, ATT_THREADS, ATT_SMEM, s>>>(pool_map, p);
+  r = cudaGetLastError();
+  if (r != cudaSuccess) return r;
+  const int warps = p.n * ATT_ROWS * p.heads;
+  attn_combine<<<(warps * 32 + 255) / 256, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- handle
+struct WsLayout {
+  size_t err, csilu, mod, emb1, xrows, h, xm, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
+      part_o, part_ml, total;
+};
+
+struct Handle {
+  DfmConfig c;
+  DfmWeights w;
+  int device;
+  int mod_w;  // adaLN output width
+  int mc;     // attention chunks per request
+  WsLayout ws;
+  CUtensorMap m_ada, m_in, m_final, m_coord, m_hid, m_lat;
+  CUtensorMap* m_qkv;
+  CUtensorMap* m_o;
+  CUtensorMap* m_fc1;
+  CUtensorMap* m_fc2;
+  // per-workspace/pool descriptors
+  const void* plan_ws = nullptr;
+  const void* plan_pool = nullptr;
+  CUtensorMap a_csilu, a_xrows, a_xm, a_ob, a_u, a_zb, a_xmf, a_act, a_exth, a_extl, pool;
+};
+
+WsLayout layout_for(const DfmConfig& c, int mc) {
+  WsLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 1023) & ~static_cast<size_t>(1023);
+    return o;
+  };
+  const size_t NR = c.max_requests, R = kSlot * NR, H = c.hidden;
+  const size_t modw = static_cast<size_t>(c.layers) * 6 * H + 2 * H;
+  L.err = take(256);
+  L.csilu = take(c.nfe * NR * H * 2);
+  L.mod = take(c.nfe * NR * modw * 4);
+  L.emb1 = take(2ull * c.nfe * H * 4);
+  L.xrows = take(R * H * 2);
+  L.h = take(R * H * 4);
+  L.xm = take(R * H * 2);
+  L.qb = take(R * H * 2);
+  L.ob = take(R * H * 2);
+  L.u = take(R * c.ffn * 2);
+  L.z = take(NR * c.latent_patch * c.latent_dim * 4);
+  L.zb = take(NR * c.latent_patch * c.latent_dim * 2);
+  L.xmf = take(NR * c.latent_patch * H * 2);
+  L.st_act = take(NR * c.cond_dim * 2);
+  L.st_exth = take(NR * c.cond_dim * 2);
+  L.st_extl = take(NR * c.latent_patch * c.latent_dim * 2);
+  L.part_o = take(NR * mc * c.heads * ATT_ROWS * 64 * 4);
+  L.part_ml = take(NR * mc * c.heads * ATT_ROWS * 2 * 4);
+  L.total = off;
+  return L;
+}
+
+int validate_config(const DfmConfig& c) {
+  if (c.hidden != kH || c.heads * c.head_dim != c.hidden || c.head_dim != 64) return DFM_ERR_UNSUPPORTED;
+  if (c.latent_patch != 16 || c.hidden_patch != 1 || c.latent_dim != 64) return DFM_ERR_UNSUPPORTED;
+  if (c.ffn % 256 != 0 || c.cond_dim % 64 != 0 || c.cond_dim <= 0) return DFM_ERR_UNSUPPORTED;
+  if (c.page_rows != 16 || c.precision != 0) return DFM_ERR_UNSUPPORTED;
+  if (c.nfe < 1 || c.nfe > EMB_MAX_STEPS) return DFM_ERR_UNSUPPORTED;
+  if (c.layers < 1 || c.num_pages < 1 || c.max_pages_per_req < 1 || c.max_requests < 1)
+    return DFM_ERR_INVALID_ARG;
+  if (static_cast<long long>(c.max_requests) * kSlot * c.ffn >= (1ll << 31)) return DFM_ERR_INVALID_ARG;
+  return DFM_OK;
+}
+
+bool ensure_plan(Handle* h, void* ws, void* pool) {
+  if (h->plan_ws == ws && h->plan_pool == pool) return true;
+  const DfmConfig& c = h->c;
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  const uint64_t NR = c.max_requests, R = kSlot * NR, H = c.hidden;
+  const uint64_t LP = NR * c.latent_patch;
+  bool ok = map_2d(&h->a_csilu, b + h->ws.csilu, c.nfe * NR, H, H, 128) &&
+            map_2d(&h->a_xrows, b + h->ws.xrows, R, H, H, 128) &&
+            map_2d(&h->a_xm, b + h->ws.xm, R, H, H, 128) &&
+            map_2d(&h->a_ob, b + h->ws.ob, R, H, H, 128) &&
+            map_2d(&h->a_u, b + h->ws.u, R, c.ffn, c.ffn, 128) &&
+            map_2d(&h->a_zb, b + h->ws.zb, LP, c.latent_dim, c.latent_dim, 128) &&
+            map_2d(&h->a_xmf, b + h->ws.xmf, LP, H, H, 128) &&
+            map_2d(&h->a_act, b + h->ws.st_act, NR, c.cond_dim, c.cond_dim, 128) &&
+            map_2d(&h->a_exth, b + h->ws.st_exth, NR, c.cond_dim, c.cond_dim, 128) &&
+            map_2d(&h->a_extl, b + h->ws.st_extl, LP, c.latent_dim, c.latent_dim, 128) &&
+            map_pool(&h->pool, pool, c.num_pages, c.heads, c.layers * c.nfe * 2);
+  if (!ok) {
+    h->plan_ws = h->plan_pool = nullptr;
+    return false;
+  }
+  // A workspace seen for the first time starts with a clear error word.
+  if (h->plan_ws != ws && cudaMemset(b + h->ws.err, 0, sizeof(uint32_t)) != cudaSuccess) return false;
+  h->plan_ws = ws;
+  h->plan_pool = pool;
+  return true;
+}
+
+#define CK(...)                                 \
+  do {                                          \
+    cudaError_t e_ = (__VA_ARGS__);             \
+    if (e_ != cudaSuccess) return DFM_ERR_CUDA; \
+  } while (0)
+
+}  // namespace
+
+extern "C" {
+
+const char* dfm_error_string(int code) {
+  switch (code) {
+    case DFM_OK: return "ok";
+    case DFM_ERR_INVALID_ARG: return "invalid argument";
+    case DFM_ERR_UNSUPPORTED: return "unsupported configuration";
+    case DFM_ERR_CUDA: return "CUDA error";
+    case DFM_ERR_WORKSPACE: return "workspace too small";
+    case DFM_ERR_DEVICE: return "device-side error";
+    default: return "unknown error";
+  }
+}
+
+size_t dfm_pool_bytes(const DfmConfig* c) {
+  if (!c) return 0;
+  return static_cast<size_t>(c->layers) * c->nfe * 2 * static_cast<size_t>(c->num_pages) *
+         c->heads * c->page_rows * c->head_dim * 2;
+}
+
+int dfm_create(const DfmConfig* cfg, const DfmWeights* w, void** out) {
+  if (!cfg || !w || !out) return DFM_ERR_INVALID_ARG;
+  *out = nullptr;
+  int rc = validate_config(*cfg);
+  if (rc != DFM_OK) return rc;
+  const void* req[] = {w->input_w, w->input_b, w->temb_w1, w->temb_b1, w->temb_w2, w->temb_b2,
+                       w->demb_w1, w->demb_b1, w->demb_w2, w->demb_b2, w->ada_w, w->ada_b,
+                       w->qkv_w, w->qk_norm, w->o_w, w->o_b, w->fc1_w, w->fc1_b, w->fc2_w,
+                       w->fc2_b, w->final_w, w->final_b, w->coord_w, w->coord_b, w->hidden_w,
+                       w->hidden_b, w->latent_w, w->latent_b, w->rope_inv_freq};
+  for (const void* p : req)
+    if (!p) return DFM_ERR_INVALID_ARG;
+  if (!encode_fn()) return DFM_ERR_CUDA;
+  Handle* h = new (std::nothrow) Handle();
+  if (!h) return DFM_ERR_CUDA;
+  h->c = *cfg;
+  h->w = *w;
+  if (cudaGetDevice(&h->device) != cudaSuccess) {
+    delete h;
+    return DFM_ERR_CUDA;
+  }
+  const DfmConfig& c = h->c;
+  const int H = c.hidden, L = c.layers;
+  h->mod_w = L * 6 * H + 2 * H;
+  h->mc = attn_chunks(c.max_pages_per_req);
+  h->ws = layout_for(c, h->mc);
+  h->m_qkv = new CUtensorMap[L];
+  h->m_o = new CUtensorMap[L];
+  h->m_fc1 = new CUtensorMap[L];
+  h->m_fc2 = new CUtensorMap[L];
+  auto bw = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  bool ok = map_2d(&h->m_ada, w->ada_w, h->mod_w, H, H, 256) &&
+            map_2d(&h->m_in, w->input_w, H, H, H, 128) &&
+            map_2d(&h->m_final, w->final_w, c.latent_dim, H, H, 64) &&
+            map_2d(&h->m_coord, w->coord_w, H, c.latent_dim, c.latent_dim, 128) &&
+            map_2d(&h->m_hid, w->hidden_w, H, c.cond_dim, c.cond_dim, 128) &&
+            map_2d(&h->m_lat, w->latent_w, H, c.latent_dim, c.latent_dim, 128);
+  for (int l = 0; ok && l < L; ++l) {
+    ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * 3 * H * H, 3 * H, H, H, 256) &&
+         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * H * H, H, H, H, 128) &&
+         map_2d(&h->m_fc1[l], bw(w->fc1_w) + static_cast<size_t>(l) * c.ffn * H, c.ffn, H, H, 256) &&
+         map_2d(&h->m_fc2[l], bw(w->fc2_w) + static_cast<size_t>(l) * H * c.ffn, H, c.ffn, c.ffn, 128);
+  }
+  if (!ok) {
+    dfm_destroy(h);
+    return DFM_ERR_CUDA;
+  }
+  *out = h;
+  return DFM_OK;
+}
+
+size_t dfm_workspace_size(void* handle) {
+  return handle ? static_cast<Handle*>(handle)->ws.total : 0;
+}
+
+int dfm_destroy(void* handle) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (!h) return DFM_ERR_INVALID_ARG;
+  delete[] h->m_qkv;
+  delete[] h->m_o;
+  delete[] h->m_fc1;
+  delete[] h->m_fc2;
+  delete h;
+  return DFM_OK;
+}
+
+int dfm_read_error(void* handle, void* workspace, void* stream, uint32_t* err_word) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (!h || !workspace || !err_word) return DFM_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  uint8_t* e = static_cast<uint8_t*>(workspace) + h->ws.err;
+  CK(cudaMemcpyAsync(&v, e, sizeof(v), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  CK(cudaMemsetAsync(e, 0, sizeof(uint32_t), s));
+  *err_word = v;
+  return DFM_OK;
+}
+
+int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_bytes,
+             void* stream) {
+  Handle* hd = static_cast<Handle*>(handle);
+  if (!hd || !b || !workspace) return DFM_ERR_INVALID_ARG;
+  const DfmConfig& c = hd->c;
+  const DfmWeights& w = hd->w;
+  const int n = b->n;
+  if (n < 1 || n > c.max_requests) return DFM_ERR_INVALID_ARG;
+  if (!b->noise || !b->out || !b->cache_len || !b->n_extend || !b->block_table || !b->kv_pool)
+    return DFM_ERR_INVALID_ARG;
+  if ((b->act_hidden == nullptr) == (b->act_row == nullptr)) return DFM_ERR_INVALID_ARG;
+  const bool ext_raw = b->ext_hidden != nullptr || b->ext_latent != nullptr;
+  if (ext_raw && (!b->ext_hidden || !b->ext_latent || b->ext_rows)) return DFM_ERR_INVALID_ARG;
+  if (workspace_bytes < hd->ws.total) return DFM_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return DFM_ERR_INVALID_ARG;
+  int dev = -1;
+  CK(cudaGetDevice(&dev));
+  if (dev != hd->device) return DFM_ERR_INVALID_ARG;
+  if (!ensure_plan(hd, workspace, b->kv_pool)) return DFM_ERR_CUDA;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws + hd->ws.err);
+  const int H = c.hidden, L = c.layers, NFE = c.nfe, LD = c.latent_dim, LPAT = c.latent_patch;
+  const int R = kSlot * n, RL = LPAT * n;
+  const size_t modw = hd->mod_w;
+  auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
+  auto f32 = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
+  auto W = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+
+  // ---- stage inputs into fixed workspace slots (fixed TMA descriptors)
+  if (b->act_hidden)
+    CK(cudaMemcpyAsync(ws + hd->ws.st_act, b->act_hidden, static_cast<size_t>(n) * c.cond_dim * 2,
+                       cudaMemcpyDeviceToDevice, s));
+  if (ext_raw) {
+    CK(cudaMemcpyAsync(ws + hd->ws.st_exth, b->ext_hidden, static_cast<size_t>(n) * c.cond_dim * 2,
+                       cudaMemcpyDeviceToDevice, s));
+    CK(cudaMemcpyAsync(ws + hd->ws.st_extl, b->ext_latent, static_cast<size_t>(RL) * LD * 2,
+                       cudaMemcpyDeviceToDevice, s));
+  }
+  {
+    const int cnt = RL * LD;
+    init_z_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(b->noise), cnt,
+                                                    f32(hd->ws.z), bf(hd->ws.zb));
+    CK(cudaGetLastError());
+  }
+
+  // ---- condition and adaLN modulation for every step (one GEMM)
+  TimeGrid grid{};
+  for (int k = 0; k < NFE; ++k) {
+    // linspace(0, 1, nfe + 1) as the reference builds it (batched_fm.py:113-116)
+    const float t0 = static_cast<float>(k) / NFE, t1 = static_cast<float>(k + 1) / NFE;
+    grid.t[k] = __bfloat162float(__float2bfloat16(t0));
+    grid.dt[k] = __bfloat162float(__float2bfloat16(t1)) - grid.t[k];
+  }
+  embed1_kernel<<<(2 * H * 32 + 255) / 256, 256, 0, s>>>(W(w.temb_w1), w.temb_b1, W(w.demb_w1),
+                                                         w.demb_b1, grid, NFE, H, f32(hd->ws.emb1));
+  CK(cudaGetLastError());
+  embed2_kernel<<<(H * 32 + 255) / 256, 256, 0, s>>>(
+      W(w.temb_w2), w.temb_b2, W(w.demb_w2), w.demb_b2, f32(hd->ws.emb1),
+      static_cast<const __nv_bfloat16*>(b->g_cond), n, NFE, H, bf(hd->ws.csilu));
+  CK(cudaGetLastError());
+  CK(gemm<256, 4>(hd->a_csilu, hd->m_ada, NFE * n, static_cast<int>(modw), H,
+                  store(f32(hd->ws.mod), static_cast<int>(modw), true, w.ada_b, false), err, s));
+
+  // ---- DiT-input rows: [graduating 17 | active hidden | active latents 16] per request
+  __nv_bfloat16* xrows = bf(hd->ws.xrows);
+  if (b->act_hidden) {
+    CK(gemm<128, 6>(hd->a_act, hd->m_hid, n, H, c.cond_dim,
+                    store(xrows, H, false, w.hidden_b, false, RowMap{1, kSlot, kStride}), err, s));
+  } else {
+    CK(cudaMemcpy2DAsync(xrows + static_cast<size_t>(kStride) * H, kSlot * H * 2, b->act_row, H * 2,
+                         H * 2, n, cudaMemcpyDeviceToDevice, s));
+  }
+  if (ext_raw) {
+    CK(gemm<128, 6>(hd->a_exth, hd->m_hid, n, H, c.cond_dim,
+                    store(xrows, H, false, w.hidden_b, false, RowMap{1, kSlot, 0}), err, s));
+    CK(gemm<128, 6>(hd->a_extl, hd->m_lat, RL, H, LD,
+                    store(xrows, H, false, w.latent_b, false, RowMap{LPAT, kSlot, 1}), err, s));
+  } else if (b->ext_rows) {
+    CK(cudaMemcpy2DAsync(xrows, kSlot * H * 2, b->ext_rows, kStride * H * 2, kStride * H * 2, n,
+                         cudaMemcpyDeviceToDevice, s));
+  } else {
+    CK(cudaMemset2DAsync(xrows, kSlot * H * 2, 0, kStride * H * 2, n, s));
+  }
+
+  const size_t plane_elems = static_cast<size_t>(c.num_pages) * c.heads * 16 * 64;
+  AttnParams ap{};
+  ap.q = bf(hd->ws.qb);
+  ap.out = bf(hd->ws.ob);
+  ap.part_o = f32(hd->ws.part_o);
+  ap.part_ml = f32(hd->ws.part_ml);
+  ap.cache_len = b->cache_len;
+  ap.n_ext = b->n_extend;
+  ap.block_table = b->block_table;
+  ap.n = n;
+  ap.max_pages = c.max_pages_per_req;
+  ap.num_pages = c.num_pages;
+  ap.heads = c.heads;
+  ap.H = H;
+  ap.MC = hd->mc;
+  ap.ext_slots = kStride;
+  ap.err = err;
+
+  float* hbuf = f32(hd->ws.h);
+  __nv_bfloat16* xm = bf(hd->ws.xm);
+  for (int k = 0; k < NFE; ++k) {
+    const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;
+    // active latent rows = coordinate_proj(z) (batched_fm.py:117-119)
+    CK(gemm<128, 6>(hd->a_zb, hd->m_coord, RL, H, LD,
+                    store(xrows, H, false, w.coord_b, false, RowMap{LPAT, kSlot, kStride + 1}), err, s));
+    CK(gemm<128, 6>(hd->a_xrows, hd->m_in, R, H, H, store(hbuf, H, true, w.input_b, false), err, s));
+    for (int l = 0; l < L; ++l) {
+      const float* mb = mod_k + static_cast<size_t>(l) * 6 * H;
+      ln_mod_kernel<<<(R * 32 + 255) / 256, 256, 0, s>>>(hbuf, R, kIdentity, mb, mb + H,
+                                                         static_cast<int>(modw), kSlot, xm, c.ln_eps);
+      CK(cudaGetLastError());
+      EpiQKV eq;
+      eq.q_out = bf(hd->ws.qb);
+      eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
+      eq.plane_elems = plane_elems;
+      eq.plane_k = (l * NFE + k) * 2;
+      eq.plane_v = eq.plane_k + 1;
+      eq.cache_len = b->cache_len;
+      eq.n_ext = b->n_extend;
+      eq.block_table = b->block_table;
+      eq.max_pages = c.max_pages_per_req;
+      eq.num_pages = c.num_pages;
+      eq.heads = c.heads;
+      eq.H = H;
+      eq.slot = kSlot;
+      eq.ext_slots = kStride;
+      eq.qk_norm = w.qk_norm + static_cast<size_t>(l) * 4 * c.head_dim;
+      eq.inv_freq = w.rope_inv_freq;
+      eq.eps = c.ln_eps;
+      eq.err = err;
+      CK(gemm<256, 4>(hd->a_xm, hd->m_qkv[l], R, 3 * H, H, eq, err, s));
+      ap.plane_k = eq.plane_k;
+      ap.plane_v = eq.plane_v;
+      CK(launch_attention(hd->pool, ap, s));
+      EpiResid ea{hbuf, H, w.o_b + static_cast<size_t>(l) * H, mb + 2 * H, static_cast<int>(modw), kSlot};
+      CK(gemm<128, 6>(hd->a_ob, hd->m_o[l], R, H, H, ea, err, s));
+      ln_mod_kernel<<<(R * 32 + 255) / 256, 256, 0, s>>>(hbuf, R, kIdentity, mb + 3 * H, mb + 4 * H,
+                                                         static_cast<int>(modw), kSlot, xm, c.ln_eps);
+      CK(cudaGetLastError());
+      CK(gemm<256, 4>(hd->a_xm, hd->m_fc1[l], R, c.ffn, H,
+                      store(bf(hd->ws.u), c.ffn, false, w.fc1_b + static_cast<size_t>(l) * c.ffn, true),
+                      err, s));
+      EpiResid ef{hbuf, H, w.fc2_b + static_cast<size_t>(l) * H, mb + 5 * H, static_cast<int>(modw), kSlot};
+      CK(gemm<128, 6>(hd->a_u, hd->m_fc2[l], R, H, c.ffn, ef, err, s));
+    }
+    // final layer on the 16 latent rows of each request, then z += dt * v
+    const float* mf = mod_k + static_cast<size_t>(L) * 6 * H;
+    ln_mod_kernel<<<(RL * 32 + 255) / 256, 256, 0, s>>>(hbuf, RL, RowMap{LPAT, kSlot, kStride + 1}, mf,
+                                                        mf + H, static_cast<int>(modw), LPAT,
+                                                        bf(hd->ws.xmf), c.ln_eps);
+    CK(cudaGetLastError());
+    EpiSolver es;
+    es.z = f32(hd->ws.z);
+    es.zb = k == NFE - 1 ? static_cast<__nv_bfloat16*>(b->out) : bf(hd->ws.zb);
+    es.bias = w.final_b;
+    es.dt = grid.dt[k];
+    CK(gemm<64, 8>(hd->a_xmf, hd->m_final, RL, LD, H, es, err, s));
+  }
+  return DFM_OK;
+}
+
+// ---------------------------------------------------------------- ops
+int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* Wt, int64_t ldw,
+               int32_t N, const float* bias, void* out, int32_t out_f32, int32_t gelu, void* stream) {
+  if (!A || !Wt || !out || M < 1 || K < 64 || K % 64 || N < 64 || N % 64) return DFM_ERR_INVALID_ARG;
+  if (lda < K || ldw < K || (lda * 2) % 16 || (ldw * 2) % 16) return DFM_ERR_INVALID_ARG;
+  if (out_f32 && N % 4) return DFM_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ma, mw;
+  const int bn = N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 64);
+  if (!map_2d(&ma, A, M, K, lda, 128) || !map_2d(&mw, Wt, N, K, ldw, bn)) return DFM_ERR_CUDA;
+  EpiStore e = store(out, N, out_f32 != 0, bias, gelu != 0);
+  if (bias == nullptr) e.bias = nullptr;
+  cudaError_t r;
+  if (bn == 256) r = gemm<256, 4>(ma, mw, M, N, K, e, nullptr, s);
+  else if (bn == 128) r = gemm<128, 6>(ma, mw, M, N, K, e, nullptr, s);
+  else r = gemm<64, 8>(ma, mw, M, N, K, e, nullptr, s);
+  return r == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
+}
+
+size_t dfm_attention_workspace_size(int32_t n, int32_t max_pages, int32_t heads) {
+  if (n < 1 || max_pages < 1 || heads < 1) return 0;
+  const size_t mc = attn_chunks(max_pages);
+  const size_t a = (static_cast<size_t>(n) * mc * heads * ATT_ROWS * 64 * 4 + 1023) & ~static_cast<size_t>(1023);
+  return 1024 + a + static_cast<size_t>(n) * mc * heads * ATT_ROWS * 2 * 4;
+}
+
+int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t num_pages,
+                        int32_t num_planes, int32_t heads, int32_t plane_k, int32_t plane_v,
+                        const int32_t* cache_len, const int32_t* n_extend, const int32_t* block_table,
+                        int32_t max_pages, int32_t n, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (!q || !out || !kv_pool || !cache_len || !n_extend || !block_table || !workspace)
+    return DFM_ERR_INVALID_ARG;
+  if (n < 1 || heads < 1 || num_pages < 1 || max_pages < 1 || plane_k < 0 || plane_v < 0 ||
+      plane_k >= num_planes || plane_v >= num_planes)
+    return DFM_ERR_INVALID_ARG;
+  if (workspace_bytes < dfm_attention_workspace_size(n, max_pages, heads)) return DFM_ERR_WORKSPACE;
+  CUtensorMap pm;
+  if (!map_pool(&pm, kv_pool, num_pages, heads, num_planes)) return DFM_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int mc = attn_chunks(max_pages);
+  AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.err = reinterpret_cast<uint32_t*>(ws);
+  p.part_o = reinterpret_cast<float*>(ws + 1024);
+  p.part_ml = reinterpret_cast<float*>(
+      ws + 1024 + ((static_cast<size_t>(n) * mc * heads * ATT_ROWS * 64 * 4 + 1023) & ~static_cast<size_t>(1023)));
+  p.cache_len = cache_len;
+  p.n_ext = n_extend;
+  p.block_table = block_table;
+  p.n = n;
+  p.max_pages = max_pages;
+  p.num_pages = num_pages;
+  p.heads = heads;
+  p.H = heads * 64;
+  p.MC = mc;
+  p.plane_k = plane_k;
+  p.plane_v = plane_v;
+  p.ext_slots = kStride;
+  return launch_attention(pm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
+}
+
+}  // extern "C"

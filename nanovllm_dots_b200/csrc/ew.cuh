@@ -1,0 +1,159 @@
+// Row-wise kernels of the FM head: adaLN LayerNorm + modulate, the timestep /
+// duration embedders, and solver-state initialisation.
+#pragma once
+
+#include "common.cuh"
+
+namespace dfm {
+
+// out[r] = LN(h[in_map(r)]) * (1 + scale[req]) + shift[req], req = r / rows_per_req,
+// LayerNorm without affine over H = 1024 (``native/dit.py:70-71,19-20``).
+// One warp per row; h is the fp32 residual stream, out the bf16 GEMM operand.
+__global__ void __launch_bounds__(256)
+    ln_mod_kernel(const float* __restrict__ h, int M, RowMap in_map, const float* __restrict__ shift,
+                  const float* __restrict__ scale, int mod_ld, int rows_per_req,
+                  __nv_bfloat16* __restrict__ out, float eps) {
+  constexpr int H = 1024;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= M) return;
+  const float* hr = h + static_cast<size_t>(in_map(r)) * H;
+  float4 x[8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    x[j] = *reinterpret_cast<const float4*>(hr + j * 128 + lane * 4);
+    s += x[j].x + x[j].y + x[j].z + x[j].w;
+  }
+  const float mean = warp_sum(s) * (1.0f / H);
+  float v = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float a = x[j].x - mean, b = x[j].y - mean, c = x[j].z - mean, d = x[j].w - mean;
+    v += a * a + b * b + c * c + d * d;
+  }
+  const float rstd = rsqrtf(warp_sum(v) * (1.0f / H) + eps);
+  const size_t req = static_cast<size_t>(r / rows_per_req);
+  const float* sh = shift + req * mod_ld;
+  const float* sc = scale + req * mod_ld;
+  __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int col = j * 128 + lane * 4;
+    const float4 a = *reinterpret_cast<const float4*>(sh + col);
+    const float4 b = *reinterpret_cast<const float4*>(sc + col);
+    const float y0 = (x[j].x - mean) * rstd * (1.f + b.x) + a.x;
+    const float y1 = (x[j].y - mean) * rstd * (1.f + b.y) + a.y;
+    const float y2 = (x[j].z - mean) * rstd * (1.f + b.z) + a.z;
+    const float y3 = (x[j].w - mean) * rstd * (1.f + b.w) + a.w;
+    *reinterpret_cast<uint2*>(o + col) = make_uint2(pack_bf16(y0, y1), pack_bf16(y2, y3));
+  }
+}
+
+constexpr int EMB_MAX_STEPS = 8;
+struct TimeGrid {
+  float t[EMB_MAX_STEPS];   // timesteps seen by the DiT
+  float dt[EMB_MAX_STEPS];  // durations seen by the duration embedder
+};
+
+// Sinusoidal embedding component idx of 256: cos(t f_i) for idx < 128, sin for
+// idx >= 128, f_i = exp(-ln(10000) * i / 128) (``native/dit.py:33-42``).
+DFM_DEV float sinusoid(float t, int idx) {
+  const int i = idx & 127;
+  const float f = expf(-9.210340371976184f * static_cast<float>(i) / 128.0f);
+  const float a = t * f;
+  return idx < 128 ? cosf(a) : sinf(a);
+}
+
+// First embedder layer for both embedders and every step:
+// out1[e][k][j] = silu(W1_e[j, :] . emb(x_{e,k}) + b1_e[j]); e = 0 time, 1 duration.
+// One warp per (e, j); the 256-wide dot product is 8 bf16 per lane.
+__global__ void __launch_bounds__(256)
+    embed1_kernel(const __nv_bfloat16* __restrict__ w_t, const float* __restrict__ b_t,
+                  const __nv_bfloat16* __restrict__ w_d, const float* __restrict__ b_d,
+                  TimeGrid grid, int nfe, int H, float* __restrict__ out1) {
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= 2 * H) return;
+  const int e = wid / H, j = wid - e * H;
+  const __nv_bfloat16* w = (e == 0 ? w_t : w_d) + static_cast<size_t>(j) * 256 + lane * 8;
+  const uint4 wv = *reinterpret_cast<const uint4*>(w);
+  const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+  float wf[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) wf[q] = __bfloat162float(wp[q]);
+  const float bias = (e == 0 ? b_t : b_d)[j];
+#pragma unroll 1
+  for (int k = 0; k < nfe; ++k) {
+    const float x = e == 0 ? grid.t[k] : grid.dt[k];
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc += wf[q] * sinusoid(x, lane * 8 + q);
+    acc = warp_sum(acc);
+    if (lane == 0) out1[(static_cast<size_t>(e) * nfe + k) * H + j] = silu(acc + bias);
+  }
+}
+
+// Second embedder layer, the condition sum and the adaLN input:
+// c_k[j] = (W2_t[j].out1[0][k] + b2_t[j]) + (W2_d[j].out1[1][k] + b2_d[j])
+// csilu[(k*n + i), j] = bf16(silu(c_k[j] + g_cond[i][j]))    (``native/dit.py:137-143``;
+// adaLN_modulation = SiLU -> Linear, ``dit.py:75-79``).  One warp per j.
+__global__ void __launch_bounds__(256)
+    embed2_kernel(const __nv_bfloat16* __restrict__ w_t, const float* __restrict__ b_t,
+                  const __nv_bfloat16* __restrict__ w_d, const float* __restrict__ b_d,
+                  const float* __restrict__ out1, const __nv_bfloat16* __restrict__ g_cond, int n,
+                  int nfe, int H, __nv_bfloat16* __restrict__ csilu) {
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (j >= H) return;
+  float ck[EMB_MAX_STEPS];
+#pragma unroll
+  for (int k = 0; k < EMB_MAX_STEPS; ++k) ck[k] = 0.f;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const __nv_bfloat16* w = (e == 0 ? w_t : w_d) + static_cast<size_t>(j) * H;
+    float acc[EMB_MAX_STEPS];
+#pragma unroll
+    for (int k = 0; k < EMB_MAX_STEPS; ++k) acc[k] = 0.f;
+#pragma unroll 1
+    for (int c = lane * 8; c < H; c += 256) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+      const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+      for (int k = 0; k < EMB_MAX_STEPS; ++k) {
+        if (k >= nfe) break;
+        const float* x = out1 + (static_cast<size_t>(e) * nfe + k) * H + c;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[k] += __bfloat162float(wp[q]) * x[q];
+      }
+    }
+    const float bias = (e == 0 ? b_t : b_d)[j];
+#pragma unroll
+    for (int k = 0; k < EMB_MAX_STEPS; ++k) {
+      if (k >= nfe) break;
+      ck[k] += warp_sum(acc[k]) + bias;
+    }
+  }
+  // lanes stride over the (k, i) pairs
+  for (int idx = lane; idx < nfe * n; idx += 32) {
+    const int k = idx / n, i = idx - k * n;
+    float c = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < EMB_MAX_STEPS; ++kk)
+      if (kk == k) c = ck[kk];
+    if (g_cond) c += __bfloat162float(g_cond[static_cast<size_t>(i) * H + j]);
+    csilu[static_cast<size_t>(idx) * H + j] = __float2bfloat16(silu(c));
+  }
+}
+
+// z = float(noise), zb = noise (the solver state and its bf16 GEMM copy).
+__global__ void init_z_kernel(const __nv_bfloat16* __restrict__ noise, int count,
+                              float* __restrict__ z, __nv_bfloat16* __restrict__ zb) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= count) return;
+  const __nv_bfloat16 v = noise[idx];
+  z[idx] = __bfloat162float(v);
+  zb[idx] = v;
+}
+
+}  // namespace dfm

@@ -1,0 +1,281 @@
+"""Host-side mirror of the reference's FM-head interface, over the C ABI.
+
+``B200FMHead`` is the batched counterpart of the reference's per-request KV
+cache heads (``CachedFMHead`` / ``FlashCachedFMHead``,
+``nanovllm_dots/models/dots/cached_fm.py:200-309``,
+``flash_cached_fm.py:81-360``): it owns the packed weights, the paged K/V
+pool and every request's page list, and one ``tick`` call decodes the next
+latent patch of every in-flight request (``decode_patch`` of each head, for all
+of them at once).  Errors raise ``RuntimeError``, as the reference engine does
+(``engine.py:487-506,661-666``).
+
+PyTorch is used only for device memory and streams; all arithmetic runs in the
+CUDA library.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import torch
+
+from . import _lib
+from .synthetic import BASE, FMConfig
+
+
+# --------------------------------------------------------------------------- #
+# Weights                                                                      #
+# --------------------------------------------------------------------------- #
+def pack_weights(sd: dict[str, torch.Tensor], cfg: FMConfig, device) -> dict[str, torch.Tensor]:
+    """Pack reference-named weights into the C-ABI layout (bf16 matrices, fp32
+    vectors) on ``device``.  Keys follow the reference state dict
+    (``native/dit.py`` module names plus ``coordinate_proj``, ``hidden_proj``,
+    ``latent_proj``)."""
+    L = cfg.layers
+    bf = lambda t: t.detach().to(device=device, dtype=torch.bfloat16).contiguous()
+    f32 = lambda t: t.detach().to(device=device, dtype=torch.float32).contiguous()
+    blk = lambda l, n: sd[f"blocks.{l}.{n}"]
+    out = {
+        "input_w": bf(sd["input_layer.weight"]), "input_b": f32(sd["input_layer.bias"]),
+        "temb_w1": bf(sd["time_embedder.mlp.0.weight"]), "temb_b1": f32(sd["time_embedder.mlp.0.bias"]),
+        "temb_w2": bf(sd["time_embedder.mlp.2.weight"]), "temb_b2": f32(sd["time_embedder.mlp.2.bias"]),
+        "demb_w1": bf(sd["duration_embedder.mlp.0.weight"]),
+        "demb_b1": f32(sd["duration_embedder.mlp.0.bias"]),
+        "demb_w2": bf(sd["duration_embedder.mlp.2.weight"]),
+        "demb_b2": f32(sd["duration_embedder.mlp.2.bias"]),
+        "ada_w": bf(torch.cat([blk(l, "adaLN_modulation.1.weight") for l in range(L)]
+                              + [sd["output_layer.adaLN_modulation.1.weight"]])),
+        "ada_b": f32(torch.cat([blk(l, "adaLN_modulation.1.bias") for l in range(L)]
+                               + [sd["output_layer.adaLN_modulation.1.bias"]])),
+        "qkv_w": bf(torch.stack([torch.cat([blk(l, "attn.q_proj.weight"), blk(l, "attn.k_proj.weight"),
+                                            blk(l, "attn.v_proj.weight")]) for l in range(L)])),
+        "qk_norm": f32(torch.stack([torch.stack([blk(l, "attn.q_norm.weight"), blk(l, "attn.q_norm.bias"),
+                                                 blk(l, "attn.k_norm.weight"), blk(l, "attn.k_norm.bias")])
+                                    for l in range(L)])),
+        "o_w": bf(torch.stack([blk(l, "attn.o_proj.weight") for l in range(L)])),
+        "o_b": f32(torch.stack([blk(l, "attn.o_proj.bias") for l in range(L)])),
+        "fc1_w": bf(torch.stack([blk(l, "ffn.fc1.weight") for l in range(L)])),
+        "fc1_b": f32(torch.stack([blk(l, "ffn.fc1.bias") for l in range(L)])),
+        "fc2_w": bf(torch.stack([blk(l, "ffn.fc2.weight") for l in range(L)])),
+        "fc2_b": f32(torch.stack([blk(l, "ffn.fc2.bias") for l in range(L)])),
+        "final_w": bf(sd["output_layer.linear.weight"]), "final_b": f32(sd["output_layer.linear.bias"]),
+        "coord_w": bf(sd["coordinate_proj.weight"]), "coord_b": f32(sd["coordinate_proj.bias"]),
+        "hidden_w": bf(sd["hidden_proj.weight"]), "hidden_b": f32(sd["hidden_proj.bias"]),
+        "latent_w": bf(sd["latent_proj.weight"]), "latent_b": f32(sd["latent_proj.bias"]),
+    }
+    # RotaryEmbedding.inv_freq exactly as the reference builds it (layers.py:105-110)
+    dh = cfg.head_dim
+    out["rope_inv_freq"] = f32(1.0 / (cfg.rotary_theta ** (torch.arange(0, dh, 2).float() / dh)))
+    return out
+
+
+def abi_config(cfg: FMConfig, num_pages: int, max_pages_per_req: int, max_requests: int):
+    return _lib.DfmConfig(cfg.layers, cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn, cfg.latent_dim,
+                          cfg.latent_patch, cfg.hidden_patch, cfg.cond_dim, cfg.nfe, cfg.page_rows,
+                          num_pages, max_pages_per_req, max_requests, cfg.ln_eps, 0)
+
+
+# --------------------------------------------------------------------------- #
+# Pages                                                                        #
+# --------------------------------------------------------------------------- #
+class PageAllocator:
+    """Free list of K/V pool pages and each request's page list (host side).
+
+    A page holds ``page_rows`` consecutive cache positions of one request for
+    every (layer, step, K|V) plane.  This is the FM counterpart of the LLM
+    engine's block manager (``nanovllm_dots/engine/block_manager.py:90``)
+    without prefix sharing (FM cache contents depend on the request's g_cond).
+    """
+
+    def __init__(self, num_pages: int, page_rows: int, max_pages_per_req: int):
+        self.num_pages = num_pages
+        self.page_rows = page_rows
+        self.max_pages_per_req = max_pages_per_req
+        self.free = list(range(num_pages - 1, -1, -1))
+        self.pages: dict[object, list[int]] = {}
+
+    def ensure(self, rid, rows: int) -> list[int]:
+        """Grow request rid's page list to cover ``rows`` positions."""
+        need = math.ceil(rows / self.page_rows)
+        if need > self.max_pages_per_req:
+            raise RuntimeError(f"request {rid!r}: {rows} FM cache rows exceed the block-table "
+                               f"capacity ({self.max_pages_per_req} pages of {self.page_rows})")
+        have = self.pages.setdefault(rid, [])
+        while len(have) < need:
+            if not self.free:
+                raise RuntimeError("FM K/V pool exhausted: no free pages "
+                                   f"({self.num_pages} pages total)")
+            have.append(self.free.pop())
+        return have
+
+    def release(self, rid) -> None:
+        for p in self.pages.pop(rid, []):
+            self.free.append(p)
+
+    def used(self) -> int:
+        return self.num_pages - len(self.free)
+
+
+@dataclasses.dataclass
+class FMRequest:
+    """Per-request FM state kept by the head: rows already cached."""
+    rid: object
+    cache_len: int = 0
+
+
+# --------------------------------------------------------------------------- #
+# Head                                                                         #
+# --------------------------------------------------------------------------- #
+class B200FMHead:
+    """Batched MeanFlow FM head over the paged per-(layer, step) K/V cache.
+
+    ``tick`` is one engine step for all in-flight requests: it extends each
+    request's cache by the rows that graduated since its previous tick and runs
+    the NFE solver steps on the active rows (hidden row + latent patch),
+    returning the next latent patch of every request.
+    """
+
+    def __init__(self, weights: dict[str, torch.Tensor], cfg: FMConfig = BASE, *,
+                 num_pages: int, max_pages_per_req: int, max_requests: int,
+                 device: torch.device | str = "cuda"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("B200FMHead runs on a CUDA device only (no CPU path)")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.L = _lib.lib()
+        self.w = pack_weights(weights, cfg, self.device)
+        self.acfg = abi_config(cfg, num_pages, max_pages_per_req, max_requests)
+        wstruct = _lib.DfmWeights(*[_lib.ptr(self.w[f]) for f in _lib.WEIGHT_FIELDS])
+        h = _lib.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(self.L.dfm_create(self.acfg, wstruct, h), "dfm_create")
+        self.handle = h
+        self.ws_bytes = int(self.L.dfm_workspace_size(h))
+        self.workspace = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=self.device)
+        pool_bytes = int(self.L.dfm_pool_bytes(self.acfg))
+        self.pool = torch.zeros(pool_bytes // 2, dtype=torch.bfloat16, device=self.device)
+        self.pages = PageAllocator(num_pages, cfg.page_rows, max_pages_per_req)
+        self.max_requests = max_requests
+        self.max_pages_per_req = max_pages_per_req
+        self.requests: dict[object, FMRequest] = {}
+
+    # ------------------------------------------------------------- pool views
+    def pool_view(self) -> torch.Tensor:
+        """The pool as [layers, nfe, 2, pages, heads, page_rows, head_dim]."""
+        c = self.cfg
+        return self.pool.view(c.layers, c.nfe, 2, self.acfg.num_pages, c.heads, c.page_rows,
+                              c.head_dim)
+
+    def write_prefix(self, rid, kv: torch.Tensor) -> None:
+        """Install a request's cached prefix K/V (bf16 [nfe, layers, 2, P, heads,
+        head_dim]) into its pages; the request's cache_len becomes P.  This is
+        the bulk-prefill entry (``flash_cached_fm.py:279-313`` builds the same
+        state by running the prefix through the DiT)."""
+        c = self.cfg
+        P = kv.shape[3]
+        req = self.requests.setdefault(rid, FMRequest(rid))
+        pages = self.pages.ensure(rid, P)
+        if P:
+            npg = math.ceil(P / c.page_rows)
+            planes = c.layers * c.nfe * 2
+            kvd = kv.to(self.device, torch.bfloat16).permute(1, 0, 2, 3, 4, 5)  # [L, nfe, 2, P, h, d]
+            kvd = kvd.reshape(planes, P, c.heads, c.head_dim)
+            if npg * c.page_rows != P:
+                kvd = torch.cat([kvd, kvd.new_zeros(planes, npg * c.page_rows - P, c.heads,
+                                                    c.head_dim)], dim=1)
+            blocks = kvd.view(planes, npg, c.page_rows, c.heads, c.head_dim).transpose(2, 3)
+            view = self.pool.view(planes, self.acfg.num_pages, c.heads, c.page_rows, c.head_dim)
+            idx = torch.tensor(pages[:npg], dtype=torch.long, device=self.device)
+            view[:, idx] = blocks
+        req.cache_len = P
+
+    def release(self, rid) -> None:
+        """Free a finished request's pages (``engine.py:460-473`` cancel/finish)."""
+        self.pages.release(rid)
+        self.requests.pop(rid, None)
+
+    # ------------------------------------------------------------- ticks
+    def prepare(self, rids, n_extend) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Host bookkeeping for one tick: allocate pages for the graduating and
+        active rows, build (cache_len, n_extend, block_table) device tensors."""
+        c = self.cfg
+        n = len(rids)
+        if not 1 <= n <= self.max_requests:
+            raise RuntimeError(f"tick with {n} requests (max {self.max_requests})")
+        bt = torch.full((n, self.max_pages_per_req), -1, dtype=torch.int32)
+        cl = torch.empty(n, dtype=torch.int32)
+        for i, (rid, ne) in enumerate(zip(rids, n_extend)):
+            if not 0 <= ne <= c.stride:
+                raise RuntimeError(f"request {rid!r}: n_extend={ne} outside [0, {c.stride}]")
+            req = self.requests.setdefault(rid, FMRequest(rid))
+            pages = self.pages.ensure(rid, req.cache_len + ne + c.stride)
+            bt[i, : len(pages)] = torch.tensor(pages, dtype=torch.int32)
+            cl[i] = req.cache_len
+        ne_t = torch.tensor(list(n_extend), dtype=torch.int32)
+        dev = self.device
+        return (cl.to(dev, non_blocking=True), ne_t.to(dev, non_blocking=True),
+                bt.to(dev, non_blocking=True))
+
+    def launch(self, *, noise, cache_len, n_extend, block_table, out, act_hidden=None,
+               act_row=None, ext_hidden=None, ext_latent=None, ext_rows=None, g_cond=None,
+               stream=None) -> None:
+        """One ``dfm_step`` on device tensors (no host bookkeeping)."""
+        for name, t in (("noise", noise), ("out", out), ("act_hidden", act_hidden),
+                        ("act_row", act_row), ("ext_hidden", ext_hidden),
+                        ("ext_latent", ext_latent), ("ext_rows", ext_rows), ("g_cond", g_cond)):
+            if t is not None:
+                if t.dtype != torch.bfloat16 or t.device != self.device or not t.is_contiguous():
+                    raise RuntimeError(f"{name}: expected a contiguous bf16 tensor on {self.device}")
+        n = noise.shape[0]
+        b = _lib.DfmBatch(n, _lib.ptr(noise), _lib.ptr(act_hidden), _lib.ptr(act_row),
+                          _lib.ptr(ext_hidden), _lib.ptr(ext_latent), _lib.ptr(ext_rows),
+                          _lib.ptr(g_cond), _lib.ptr(cache_len), _lib.ptr(n_extend),
+                          _lib.ptr(block_table), _lib.ptr(self.pool), _lib.ptr(out))
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _lib.check(self.L.dfm_step(self.handle, b, _lib.ptr(self.workspace), self.ws_bytes,
+                                   _lib.c_void_p(s.cuda_stream)), "dfm_step")
+
+    def tick(self, rids, *, noise, act_hidden=None, act_row=None, ext_hidden=None,
+             ext_latent=None, ext_rows=None, n_extend=None, g_cond=None) -> torch.Tensor:
+        """Decode the next latent patch of every request in ``rids``.
+
+        Inputs are device tensors with one leading row per request.  Each
+        request graduates ``n_extend[i]`` rows (default: stride, or 0 when no
+        graduating inputs are given) into its cache.  Returns bf16
+        [n, latent_patch, latent_dim]."""
+        c = self.cfg
+        n = len(rids)
+        if n_extend is None:
+            has_ext = ext_hidden is not None or ext_rows is not None
+            n_extend = [c.stride if has_ext else 0] * n
+        cl, ne, bt = self.prepare(rids, n_extend)
+        out = torch.empty(n, c.latent_patch, c.latent_dim, dtype=torch.bfloat16, device=self.device)
+        self.launch(noise=noise, cache_len=cl, n_extend=ne, block_table=bt, out=out,
+                    act_hidden=act_hidden, act_row=act_row, ext_hidden=ext_hidden,
+                    ext_latent=ext_latent, ext_rows=ext_rows, g_cond=g_cond)
+        for rid, e in zip(rids, n_extend):
+            self.requests[rid].cache_len += int(e)
+        return out
+
+    def check_errors(self) -> None:
+        """Synchronise and raise if any kernel reported a device-side error."""
+        v = _lib.c_uint32(0)
+        s = torch.cuda.current_stream(self.device)
+        _lib.check(self.L.dfm_read_error(self.handle, _lib.ptr(self.workspace),
+                                         _lib.c_void_p(s.cuda_stream), v), "dfm_read_error")
+        if v.value:
+            names = [nm for bit, nm in _lib.DEVERR_BITS.items() if v.value & bit]
+            raise RuntimeError(f"FM head device error: {', '.join(names)} (0x{v.value:x})")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.L.dfm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

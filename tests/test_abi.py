@@ -1,0 +1,88 @@
+"""The C-ABI library builds, loads without a GPU and exports every entry point
+``include/dfm.h`` declares; host-side bookkeeping that needs no GPU."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from nanovllm_dots_b200 import _lib, build
+from nanovllm_dots_b200.fm_head import PageAllocator, abi_config, pack_weights
+from nanovllm_dots_b200.synthetic import BASE
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "dfm.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(dfm_\w+)\s*\(", src, re.M)))
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    path = build.build()
+    L = ctypes.CDLL(path)
+    decl = declared_functions()
+    assert decl, "no declarations parsed from dfm.h"
+    for name in decl:
+        assert hasattr(L, name), f"{name} declared in dfm.h but not exported"
+    assert set(decl) == set(_lib.EXPORTS)
+
+
+def test_struct_layouts_match_header():
+    src = open(HEADER).read()
+    body = src[src.index("typedef struct DfmWeights"):src.index("} DfmWeights;")]
+    n_ptr = len(re.findall(r"const (?:void|float)\*\s+\w+", body))
+    assert n_ptr == len(_lib.WEIGHT_FIELDS)
+    assert ctypes.sizeof(_lib.DfmConfig) == 16 * 4
+    assert ctypes.sizeof(_lib.DfmBatch) == 8 + 12 * 8
+
+
+def test_pool_bytes_and_error_strings():
+    L = _lib.lib()
+    cfg = abi_config(BASE, num_pages=10, max_pages_per_req=4, max_requests=2)
+    assert L.dfm_pool_bytes(cfg) == 12 * 4 * 2 * 10 * 16 * 16 * 64 * 2
+    assert L.dfm_error_string(0) == b"ok"
+    assert L.dfm_error_string(4) == b"workspace too small"
+
+
+def test_create_rejects_bad_configs_without_a_gpu():
+    L = _lib.lib()
+    w = _lib.DfmWeights()
+    h = ctypes.c_void_p()
+    bad = abi_config(BASE, num_pages=10, max_pages_per_req=4, max_requests=2)
+    bad.hidden = 768
+    assert L.dfm_create(bad, w, h) == 2          # unsupported width
+    good = abi_config(BASE, num_pages=10, max_pages_per_req=4, max_requests=2)
+    assert L.dfm_create(good, w, h) == 1         # null weight pointers
+    assert L.dfm_step(None, None, None, 0, None) == 1
+    assert L.dfm_linear(None, 64, 1, 64, None, 64, 64, None, None, 0, 0, None) == 1
+
+
+def test_page_allocator():
+    pa = PageAllocator(num_pages=5, page_rows=16, max_pages_per_req=3)
+    assert pa.ensure("a", 17) == [0, 1]
+    assert pa.ensure("b", 1) == [2]
+    assert pa.ensure("a", 48) == [0, 1, 3]
+    with pytest.raises(RuntimeError, match="block-table"):
+        pa.ensure("a", 49)
+    with pytest.raises(RuntimeError, match="exhausted"):
+        pa.ensure("b", 48)
+    pa.release("a")
+    assert pa.used() == 2 and sorted(pa.free) == [0, 1, 3]
+
+
+def test_pack_weights_layout(weights):
+    p = pack_weights(weights, BASE, "cpu")
+    H, L, F = BASE.hidden, BASE.layers, BASE.ffn
+    assert p["ada_w"].shape == (L * 6 * H + 2 * H, H) and p["ada_w"].dtype == torch.bfloat16
+    assert p["qkv_w"].shape == (L, 3 * H, H)
+    assert torch.equal(p["qkv_w"][3, H:2 * H].float(), weights["blocks.3.attn.k_proj.weight"])
+    assert torch.equal(p["ada_w"][L * 6 * H:].float(), weights["output_layer.adaLN_modulation.1.weight"])
+    assert p["qk_norm"].shape == (L, 4, 64)
+    assert p["fc2_w"].shape == (L, H, F)
+    assert p["rope_inv_freq"].shape == (32,)
+    for f in _lib.WEIGHT_FIELDS:
+        assert f in p
