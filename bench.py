@@ -45,9 +45,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "prof"],
+                    help="prof = the first 16 requests of cfg2 (a few GB, for ncu captures)")
     ap.add_argument("--cpu-sample", type=int, default=8, help="requests in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-tick", action="store_true",
+                    help="run one eager tick inside cudaProfilerStart/Stop (for ncu "
+                         "--profile-from-start off) and exit")
     return ap.parse_args()
 
 
@@ -62,6 +66,9 @@ def load_peaks():
 
 def workload_batch(name: str, rank: int):
     from nanovllm_dots_b200 import synthetic as syn
+    if name == "prof":
+        full = syn.config_batch("cfg2")
+        return syn.make_batch(16, [p // 17 for p in full.prefix_rows[:16]], seed=2)
     b = syn.config_batch(name)
     if rank:
         # same distribution, an independent draw per rank
@@ -226,9 +233,42 @@ def run_b200(args, rank, world):
     out = torch.empty(n, cfg.latent_patch, cfg.latent_dim, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def tick():
+    def eager_tick():
         head.launch(noise=noise, act_hidden=cond, ext_hidden=ph, ext_latent=pl, cache_len=cl,
                     n_extend=ne, block_table=bt, out=out)
+
+    for _ in range(2):
+        eager_tick()
+    torch.cuda.synchronize()
+    head.check_errors()
+    if args.profile_tick:
+        torch.cuda.cudart().cudaProfilerStart()
+        eager_tick()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        head.check_errors()
+        if rank == 0:
+            print(json.dumps({"profile_tick": True, "workload": args.workload, "requests": n,
+                              "launches": launches_per_tick(cfg)}), flush=True)
+        head.close()
+        return
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(3):
+        eager_tick()
+    ev1.record(stream)
+    ev1.synchronize()
+    eager_ms = ev0.elapsed_time(ev1) / 3
+
+    # the tick as one CUDA graph over static buffers (the serving configuration)
+    tg = head.graph(n, raw_inputs=True)
+    for k, v in (("noise", noise), ("act_hidden", cond), ("ext_hidden", ph), ("ext_latent", pl),
+                 ("cache_len", cl), ("n_extend", ne), ("block_table", bt)):
+        tg.inputs[k].copy_(v)
+    torch.cuda.synchronize()
+
+    def tick():
+        tg.replay()
 
     for _ in range(args.warmup):
         tick()
@@ -265,18 +305,18 @@ def run_b200(args, rank, world):
     h_noise, h_cond, h_ph, h_pl = pin(b.noise), pin(b.cond), pin(b.prev_hidden), pin(b.prev_latent)
     h_cl, h_ne, h_bt = pin(cl.cpu()), pin(ne.cpu()), pin(bt.cpu())
     h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    dn, dc, dph, dpl = [torch.empty_like(x) for x in (noise, cond, ph, pl)]
-    dcl, dne, dbt = torch.empty_like(cl), torch.empty_like(ne), torch.empty_like(bt)
     h2d = sum(x.numel() * x.element_size() for x in (h_noise, h_cond, h_ph, h_pl, h_cl, h_ne, h_bt))
     d2h = h_out.numel() * h_out.element_size()
+    pairs = [(tg.inputs[k], v) for k, v in (("noise", h_noise), ("act_hidden", h_cond),
+                                             ("ext_hidden", h_ph), ("ext_latent", h_pl),
+                                             ("cache_len", h_cl), ("n_extend", h_ne),
+                                             ("block_table", h_bt))]
 
     def e2e_tick():
-        for dst, src in ((dn, h_noise), (dc, h_cond), (dph, h_ph), (dpl, h_pl), (dcl, h_cl),
-                         (dne, h_ne), (dbt, h_bt)):
+        for dst, src in pairs:
             dst.copy_(src, non_blocking=True)
-        head.launch(noise=dn, act_hidden=dc, ext_hidden=dph, ext_latent=dpl, cache_len=dcl,
-                    n_extend=dne, block_table=dbt, out=out)
-        h_out.copy_(out, non_blocking=True)
+        tg.replay()
+        h_out.copy_(tg.out, non_blocking=True)
         stream.synchronize()
 
     for _ in range(2):
@@ -382,6 +422,7 @@ def run_b200(args, rank, world):
                 "e2e": {"value": round(e2e_val, 2), "unit": "audio-s/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": round(e2e_ms, 4)},
+                "eager_ms_per_step": round(eager_ms, 4),
                 "gpu_launches": launches_per_tick(cfg) * args.steps,
                 "roofline": roof, "kernels": summary, "clocks": clk.summary(),
                 "cpu_baseline": cpu}

@@ -2,6 +2,7 @@
 // TMA descriptor encoding and the per-tick launch sequence.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -65,13 +66,28 @@ bool map_pool(CUtensorMap* m, const void* base, int num_pages, int heads, int pl
 }
 
 // ---------------------------------------------------------------- launches
+// Raise a kernel's dynamic shared-memory limit once per device (the attribute
+// call is host-expensive and must not sit on the per-launch path).
+template <class K>
+cudaError_t smem_attr_once(std::atomic<uint64_t>& done, K fn, int smem) {
+  int dev = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return r;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (r == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return r;
+}
+
 template <int BN, int ST, class Epi>
 cudaError_t gemm(const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K, const Epi& e,
                  uint32_t* err, cudaStream_t s) {
   if (M <= 0) return cudaSuccess;
+  static std::atomic<uint64_t> attr_done{0};
   auto fn = gemm_bf16_tn<BN, ST, Epi>;
   constexpr int smem = GemmShape<BN, ST>::SMEM;
-  cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
   dim3 grid((M + GEMM_BM - 1) / GEMM_BM, N / BN);
   fn<<<grid, GEMM_THREADS, smem, s>>>(a, b, M, K, e, err);
@@ -94,8 +110,8 @@ EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMa
 int attn_chunks(int max_pages) { return (max_pages * 16 + kSlot + ATT_CH - 1) / ATT_CH; }
 
 cudaError_t launch_attention(const CUtensorMap& pool_map, const AttnParams& p, cudaStream_t s) {
-  cudaError_t r = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       ATT_SMEM);
+  static std::atomic<uint64_t> attr_done{0};
+  cudaError_t r = smem_attr_once(attr_done, attn_kernel, ATT_SMEM);
   if (r != cudaSuccess) return r;
   dim3 grid(p.n * p.MC, p.heads);
   attn_kernel<<<grid, ATT_THREADS, ATT_SMEM, s>>>(pool_map, p);

@@ -86,6 +86,9 @@ struct EpiStore {
 
 // h[row, col] += gate[req(row), col] * (acc + bias[col])   (fp32 residual stream)
 // with req(row) = row / rows_per_req and gate rows gate_ld floats apart.
+// Each 32-column chunk issues all of its residual, gate and bias loads before
+// any arithmetic or store, so a thread waits one memory round trip per chunk
+// instead of one per float4.
 struct EpiResid {
   float* h;
   int ldh;
@@ -96,25 +99,33 @@ struct EpiResid {
 
   template <int BN>
   DFM_DEV void run(uint32_t taddr, int row, int n0, int M) const {
+    const bool live = row < M;
+    const float* g = gate + static_cast<size_t>(live ? row / rows_per_req : 0) * gate_ld + n0;
+    float* hp = h + static_cast<size_t>(live ? row : 0) * ldh + n0;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       uint32_t r[32];
       tmem_ld32(taddr + c, r);
-      tmem_wait_ld();
-      if (row >= M) continue;
-      const float* g = gate + static_cast<size_t>(row / rows_per_req) * gate_ld + n0 + c;
-      float* hp = h + static_cast<size_t>(row) * ldh + n0 + c;
+      float4 hv[8], gv[8], bv[8];
+      if (live) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 b = *reinterpret_cast<const float4*>(bias + n0 + c + j);
-        const float4 gg = *reinterpret_cast<const float4*>(g + j);
-        float4 x = *reinterpret_cast<float4*>(hp + j);
-        x.x += gg.x * (__uint_as_float(r[j]) + b.x);
-        x.y += gg.y * (__uint_as_float(r[j + 1]) + b.y);
-        x.z += gg.z * (__uint_as_float(r[j + 2]) + b.z);
-        x.w += gg.w * (__uint_as_float(r[j + 3]) + b.w);
-        *reinterpret_cast<float4*>(hp + j) = x;
+        for (int j = 0; j < 8; ++j) {
+          hv[j] = *reinterpret_cast<const float4*>(hp + c + 4 * j);
+          gv[j] = __ldg(reinterpret_cast<const float4*>(g + c + 4 * j));
+          bv[j] = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + 4 * j));
+        }
       }
+      tmem_wait_ld();
+      if (!live) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        hv[j].x += gv[j].x * (__uint_as_float(r[4 * j]) + bv[j].x);
+        hv[j].y += gv[j].y * (__uint_as_float(r[4 * j + 1]) + bv[j].y);
+        hv[j].z += gv[j].z * (__uint_as_float(r[4 * j + 2]) + bv[j].z);
+        hv[j].w += gv[j].w * (__uint_as_float(r[4 * j + 3]) + bv[j].w);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(hp + c + 4 * j) = hv[j];
     }
   }
 };
@@ -145,21 +156,39 @@ struct EpiQKV {
 
   template <int BN>
   DFM_DEV void run(uint32_t taddr, int row, int n0, int M) const {
+    // Row metadata (position and destination page) once per row, not per head.
+    const bool in_range = row < M;
+    const int i = in_range ? row / slot : 0;
+    const int j = in_range ? row - i * slot : 0;
+    const int ne = n_ext[i], P = cache_len[i];
+    const bool ext = j < ext_slots;
+    const bool live = in_range && (!ext || j < ne);
+    const int pos = ext ? P + j : P + ne + (j - ext_slots);
+    const int pidx = pos >> 4;
+    int page = -1;
+    if (live && n0 >= H) {
+      if (pos < 0 || pidx >= max_pages || ne < 0 || ne > ext_slots) {
+        atomicOr(err, DFM_DEV_ERR_LEN);
+      } else {
+        page = block_table[static_cast<size_t>(i) * max_pages + pidx];
+        if (page < 0 || page >= num_pages) {
+          atomicOr(err, DFM_DEV_ERR_PAGE);
+          page = -1;
+        }
+      }
+    }
+    const float fpos = static_cast<float>(pos);
 #pragma unroll 1
     for (int c = 0; c < BN; c += 64) {
       uint32_t r0[32], r1[32];
       tmem_ld32(taddr + c, r0);
       tmem_ld32(taddr + c + 32, r1);
       tmem_wait_ld();
-      if (row >= M) continue;
+      if (!in_range) continue;
       const int col = n0 + c;
       const int sec = col / H;
       const int head = (col - sec * H) >> 6;
-      const int i = row / slot, j = row - (row / slot) * slot;
-      const int ne = n_ext[i], P = cache_len[i];
-      const bool ext = j < ext_slots;
-      const bool live = !ext || j < ne;
-      const int pos = ext ? P + j : P + ne + (j - ext_slots);
+      if (sec > 0 && page < 0) continue;
       float x[64];
 #pragma unroll
       for (int d = 0; d < 32; ++d) {
@@ -180,32 +209,20 @@ struct EpiQKV {
         const float rstd = rsqrtf(var * (1.0f / 64.0f) + eps);
         const float* w = qk_norm + sec * 128;
 #pragma unroll
-        for (int d = 0; d < 64; ++d) x[d] = (x[d] - mean) * rstd * w[d] + w[64 + d];
-        const float fpos = static_cast<float>(pos);
+        for (int d = 0; d < 64; ++d) x[d] = (x[d] - mean) * rstd * __ldg(w + d) + __ldg(w + 64 + d);
 #pragma unroll
         for (int d = 0; d < 32; ++d) {
-          float s, co;
-          sincosf(fpos * inv_freq[d], &s, &co);
+          float sn, co;
+          sincosf(fpos * __ldg(inv_freq + d), &sn, &co);
           const float a = x[d], b = x[d + 32];
-          x[d] = a * co - b * s;
-          x[d + 32] = b * co + a * s;
+          x[d] = a * co - b * sn;
+          x[d + 32] = b * co + a * sn;
         }
       }
       __nv_bfloat16* dst;
       if (sec == 0) {
         dst = q_out + static_cast<size_t>(row) * H + head * 64;
       } else {
-        if (!live) continue;
-        const int pidx = pos >> 4;
-        if (pos < 0 || pidx >= max_pages || ne < 0 || ne > ext_slots) {
-          atomicOr(err, DFM_DEV_ERR_LEN);
-          continue;
-        }
-        const int page = block_table[static_cast<size_t>(i) * max_pages + pidx];
-        if (page < 0 || page >= num_pages) {
-          atomicOr(err, DFM_DEV_ERR_PAGE);
-          continue;
-        }
         dst = pool + static_cast<size_t>(sec == 1 ? plane_k : plane_v) * plane_elems +
               (static_cast<size_t>(page) * heads + head) * 1024 + (pos & 15) * 64;
       }
@@ -219,7 +236,8 @@ struct EpiQKV {
 };
 
 // MeanFlow update fused into the final projection (N = latent_dim = 64):
-// z[row] += dt * (acc + bias); zb[row] = bf16(z[row]).
+// z[row] += dt * (acc + bias); zb[row] = bf16(z[row]).  Loads are batched per
+// chunk as in EpiResid.
 struct EpiSolver {
   float* z;
   __nv_bfloat16* zb;
@@ -228,30 +246,36 @@ struct EpiSolver {
 
   template <int BN>
   DFM_DEV void run(uint32_t taddr, int row, int n0, int M) const {
+    const bool live = row < M;
+    float* zp = z + static_cast<size_t>(live ? row : 0) * 64 + n0;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       uint32_t r[32];
       tmem_ld32(taddr + c, r);
-      tmem_wait_ld();
-      if (row >= M) continue;
-      float* zp = z + static_cast<size_t>(row) * 64 + n0 + c;
-      float v[32];
+      float4 zv[8], bv[8];
+      if (live) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 b = *reinterpret_cast<const float4*>(bias + n0 + c + j);
-        float4 x = *reinterpret_cast<float4*>(zp + j);
-        x.x += dt * (__uint_as_float(r[j]) + b.x);
-        x.y += dt * (__uint_as_float(r[j + 1]) + b.y);
-        x.z += dt * (__uint_as_float(r[j + 2]) + b.z);
-        x.w += dt * (__uint_as_float(r[j + 3]) + b.w);
-        *reinterpret_cast<float4*>(zp + j) = x;
-        v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
+        for (int j = 0; j < 8; ++j) {
+          zv[j] = *reinterpret_cast<const float4*>(zp + c + 4 * j);
+          bv[j] = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + 4 * j));
+        }
+      }
+      tmem_wait_ld();
+      if (!live) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        zv[j].x += dt * (__uint_as_float(r[4 * j]) + bv[j].x);
+        zv[j].y += dt * (__uint_as_float(r[4 * j + 1]) + bv[j].y);
+        zv[j].z += dt * (__uint_as_float(r[4 * j + 2]) + bv[j].z);
+        zv[j].w += dt * (__uint_as_float(r[4 * j + 3]) + bv[j].w);
+        *reinterpret_cast<float4*>(zp + c + 4 * j) = zv[j];
       }
       uint4* d4 = reinterpret_cast<uint4*>(zb + static_cast<size_t>(row) * 64 + n0 + c);
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        d4[q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                           pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+        d4[q] = make_uint4(pack_bf16(zv[2 * q].x, zv[2 * q].y), pack_bf16(zv[2 * q].z, zv[2 * q].w),
+                           pack_bf16(zv[2 * q + 1].x, zv[2 * q + 1].y),
+                           pack_bf16(zv[2 * q + 1].z, zv[2 * q + 1].w));
     }
   }
 };

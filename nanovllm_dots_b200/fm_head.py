@@ -156,7 +156,11 @@ class B200FMHead:
         self.workspace = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=self.device)
         pool_bytes = int(self.L.dfm_pool_bytes(self.acfg))
         self.pool = torch.zeros(pool_bytes // 2, dtype=torch.bfloat16, device=self.device)
-        self.pages = PageAllocator(num_pages, cfg.page_rows, max_pages_per_req)
+        if num_pages < 2:
+            raise RuntimeError("the K/V pool needs at least 2 pages")
+        # The last page is never handed to a request: graph warm-up writes there.
+        self.scratch_page = num_pages - 1
+        self.pages = PageAllocator(num_pages - 1, cfg.page_rows, max_pages_per_req)
         self.max_requests = max_requests
         self.max_pages_per_req = max_pages_per_req
         self.requests: dict[object, FMRequest] = {}
@@ -259,6 +263,13 @@ class B200FMHead:
             self.requests[rid].cache_len += int(e)
         return out
 
+    def graph(self, n: int, *, raw_inputs: bool = True, with_g: bool = False) -> "TickGraph":
+        """A CUDA graph of one ``dfm_step`` for n requests over static buffers
+        (the capture pattern of ``GraphedFlashCachedFMHead``,
+        ``flash_cached_fm.py:191-360``): copy a tick's inputs into
+        ``TickGraph.inputs``, ``replay()``, read ``TickGraph.out``."""
+        return TickGraph(self, n, raw_inputs=raw_inputs, with_g=with_g)
+
     def check_errors(self) -> None:
         """Synchronise and raise if any kernel reported a device-side error."""
         v = _lib.c_uint32(0)
@@ -279,3 +290,51 @@ class B200FMHead:
             self.close()
         except Exception:
             pass
+
+
+class TickGraph:
+    """One captured FM-head tick over static device buffers.
+
+    ``inputs`` holds noise, the active-row inputs (raw ``act_hidden`` or
+    projected ``act_row``), the graduating-row inputs, g_cond (optional) and the
+    per-request (cache_len, n_extend, block_table); ``out`` receives the next
+    latent patch.  Every kernel of the tick replays from one graph launch, so
+    the tick costs no per-kernel host work.
+    """
+
+    def __init__(self, head: B200FMHead, n: int, *, raw_inputs: bool = True, with_g: bool = False):
+        c, dev = head.cfg, head.device
+        self.head, self.n = head, n
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        t = {"noise": torch.zeros(n, c.latent_patch, c.latent_dim, **bf),
+             "cache_len": torch.zeros(n, **i32), "n_extend": torch.zeros(n, **i32),
+             "block_table": torch.zeros(n, head.max_pages_per_req, **i32)}
+        if raw_inputs:
+            t["act_hidden"] = torch.zeros(n, c.cond_dim, **bf)
+            t["ext_hidden"] = torch.zeros(n, c.cond_dim, **bf)
+            t["ext_latent"] = torch.zeros(n, c.latent_patch, c.latent_dim, **bf)
+        else:
+            t["act_row"] = torch.zeros(n, c.hidden, **bf)
+            t["ext_rows"] = torch.zeros(n, c.stride, c.hidden, **bf)
+        if with_g:
+            t["g_cond"] = torch.zeros(n, c.hidden, **bf)
+        self.inputs = t
+        self.out = torch.zeros(n, c.latent_patch, c.latent_dim, **bf)
+        # Warm-up and capture point every request at the head's scratch page, so
+        # the warm-up's K/V writes touch no request's cache.
+        t["block_table"].fill_(head.scratch_page)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            head.launch(out=self.out, stream=side, **t)     # warm-up: plans, attributes
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            head.launch(out=self.out, stream=torch.cuda.current_stream(dev), **t)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out

@@ -155,6 +155,31 @@ def test_batch_invariance_and_determinism(head):
     assert torch.equal(one.float().cpu()[0], out_all[3])
 
 
+def test_graph_replay_matches_eager(head):
+    """The captured tick (static buffers, one graph launch) equals the eager call."""
+    cfg = syn.BASE
+    b = syn.make_batch(4, [5, 0, 20, 2], seed=61, n_extend=[17, 0, 17, 17])
+    for rid in list(head.requests):
+        head.release(rid)
+    rids = [f"gr{i}" for i in range(4)]
+    for i, rid in enumerate(rids):
+        head.write_prefix(rid, syn.request_kv(b, i))
+    cl, ne, bt = head.prepare(rids, b.n_extend)
+    d = lambda t: t.to(DEV).contiguous()
+    eager = torch.empty(4, cfg.latent_patch, cfg.latent_dim, dtype=torch.bfloat16, device=DEV)
+    head.launch(noise=d(b.noise), act_hidden=d(b.cond), ext_hidden=d(b.prev_hidden),
+                ext_latent=d(b.prev_latent), cache_len=cl, n_extend=ne, block_table=bt, out=eager)
+    tg = head.graph(4)
+    for k, v in (("noise", b.noise), ("act_hidden", b.cond), ("ext_hidden", b.prev_hidden),
+                 ("ext_latent", b.prev_latent), ("cache_len", cl), ("n_extend", ne),
+                 ("block_table", bt)):
+        tg.inputs[k].copy_(v)
+    out = tg.replay().clone()
+    out2 = tg.replay().clone()
+    head.check_errors()
+    assert torch.equal(out, eager) and torch.equal(out2, eager)
+
+
 def test_device_error_on_bad_block_table(head):
     """A block table pointing outside the pool is reported, not a fault."""
     cfg = syn.BASE
