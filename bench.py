@@ -45,8 +45,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "prof"],
-                    help="prof = the first 16 requests of cfg2 (a few GB, for ncu captures)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "prof", "gemm64"],
+                    help="prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
+                         "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool)")
     ap.add_argument("--cpu-sample", type=int, default=8, help="requests in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-tick", action="store_true",
@@ -66,6 +67,8 @@ def load_peaks():
 
 def workload_batch(name: str, rank: int):
     from nanovllm_dots_b200 import synthetic as syn
+    if name == "gemm64":
+        return syn.make_batch(64, [0] * 64, seed=2)
     if name == "prof":
         full = syn.config_batch("cfg2")
         return syn.make_batch(16, [p // 17 for p in full.prefix_rows[:16]], seed=2)

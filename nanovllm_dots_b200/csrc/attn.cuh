@@ -15,8 +15,9 @@
 // rows each (rows 34..47 are padding) and run bf16 mma.sync m16n8k16 with an
 // online softmax in the exp2 domain; warp 3 is the TMA producer of a 4-stage
 // ring of 64-key K and V tiles.  A request that fits in one chunk writes its
-// normalised output directly; longer ones write (O, m, l) partials that
-// attn_combine merges.
+// normalised output directly; longer ones write (O, m, l) partials and the
+// last chunk CTA of each (request, head), found with a completion counter,
+// merges them.
 #pragma once
 
 #include "common.cuh"
@@ -29,13 +30,14 @@ constexpr int ATT_CH = 512;      // keys per work unit
 constexpr int ATT_ROWS = 34;     // query rows per request
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_TILE_BYTES = ATT_KT * 64 * 2;  // 8 KB per K (or V) tile
-constexpr int ATT_SMEM = ATT_STAGES * 2 * ATT_TILE_BYTES + 1024 + 128;
+constexpr int ATT_SMEM = ATT_STAGES * 2 * ATT_TILE_BYTES + 1024 + 256;
 
 struct AttnParams {
   const __nv_bfloat16* q;    // [n*34, H]
   __nv_bfloat16* out;        // [n*34, H]
   float* part_o;             // [n*MC*heads][34][64]
   float* part_ml;            // [n*MC*heads][34][2]
+  int* sem;                  // [n*heads] chunk-completion counters (zero between launches)
   const int* cache_len;
   const int* n_ext;
   const int* block_table;
@@ -74,6 +76,9 @@ __global__ void __launch_bounds__(ATT_THREADS)
   const int i = blockIdx.x / p.MC;
   const int c = blockIdx.x - i * p.MC;
   const int h = blockIdx.y;
+  pdl_trigger();
+  if (threadIdx.x == 0) tma_prefetch(&tm_pool);
+  pdl_wait();
   if (i >= p.n) return;
   const int P = p.cache_len[i];
   const int ne = p.n_ext[i];
@@ -83,7 +88,7 @@ __global__ void __launch_bounds__(ATT_THREADS)
     return;
   }
   const int nchunks = (total + ATT_CH - 1) / ATT_CH;
-  if (c >= nchunks) return;
+  if (c >= nchunks || nchunks > p.MC) return;
   const int k0 = c * ATT_CH;
   const int k1 = min(total, k0 + ATT_CH);
   const int ntiles = (k1 - k0 + ATT_KT - 1) / ATT_KT;
@@ -96,6 +101,7 @@ __global__ void __launch_bounds__(ATT_THREADS)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * ATT_STAGES * ATT_TILE_BYTES);
   uint64_t* empty = full + ATT_STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + ATT_STAGES);
+  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -104,12 +110,14 @@ __global__ void __launch_bounds__(ATT_THREADS)
       mbar_init(&empty[s], 3);
     }
     *abort_flag = 0;
+    *last_flag = 0;
     fence_mbar_init();
-    tma_prefetch(&tm_pool);
   }
   __syncthreads();
 
+  const size_t unit = (static_cast<size_t>(i) * p.MC + c) * p.heads + h;
   if (warp == 3) {
+    // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       const int* bt = p.block_table + static_cast<size_t>(i) * p.max_pages;
 #pragma unroll 1
@@ -137,200 +145,220 @@ __global__ void __launch_bounds__(ATT_THREADS)
         }
       }
     }
-    return;
-  }
+  } else {
+    // ------------------------------------------------------ compute warps
+    const int g = lane >> 2, tq = lane & 3;
+    const int r_lo = warp * 16 + g, r_hi = r_lo + 8;
+    const int lim_lo = r_lo < ne ? P + r_lo + 1 : total;
+    const int lim_hi = r_hi < ne ? P + r_hi + 1 : total;
+    const float cexp = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
 
-  // ---------------------------------------------------------- compute warps
-  const int g = lane >> 2, tq = lane & 3;
-  const int r_lo = warp * 16 + g, r_hi = r_lo + 8;
-  const int lim_lo = r_lo < ne ? P + r_lo + 1 : total;
-  const int lim_hi = r_hi < ne ? P + r_hi + 1 : total;
-  const float scale = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
-
-  // Q fragments (A operand, 16 rows x 64 dims = 4 k-steps).
-  uint32_t qa[4][4];
-  {
-    const __nv_bfloat16* qb = p.q + static_cast<size_t>(i) * ATT_ROWS * p.H + h * 64;
+    uint32_t qa[4][4];
+    {
+      const __nv_bfloat16* qb = p.q + static_cast<size_t>(i) * ATT_ROWS * p.H + h * 64;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const int d0 = ks * 16 + tq * 2;
-      auto ld = [&](int r, int d) -> uint32_t {
-        if (r >= ATT_ROWS) return 0u;
-        return *reinterpret_cast<const uint32_t*>(qb + static_cast<size_t>(r) * p.H + d);
-      };
-      qa[ks][0] = ld(r_lo, d0);
-      qa[ks][1] = ld(r_hi, d0);
-      qa[ks][2] = ld(r_lo, d0 + 8);
-      qa[ks][3] = ld(r_hi, d0 + 8);
+      for (int ks = 0; ks < 4; ++ks) {
+        const int d0 = ks * 16 + tq * 2;
+        auto ld = [&](int r, int d) -> uint32_t {
+          if (r >= ATT_ROWS) return 0u;
+          return *reinterpret_cast<const uint32_t*>(qb + static_cast<size_t>(r) * p.H + d);
+        };
+        qa[ks][0] = ld(r_lo, d0);
+        qa[ks][1] = ld(r_hi, d0);
+        qa[ks][2] = ld(r_lo, d0 + 8);
+        qa[ks][3] = ld(r_hi, d0 + 8);
+      }
     }
-  }
 
-  float o[8][4];
+    float o[8][4];
 #pragma unroll
-  for (int a = 0; a < 8; ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
-  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+    for (int a = 0; a < 8; ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
 
 #pragma unroll 1
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % ATT_STAGES;
-    const uint32_t ph = (t / ATT_STAGES) & 1;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag, p.err));
-    if (!ok) break;
-    const uint32_t kbase = smem_u32(sK + s * ATT_TILE_BYTES);
-    const uint32_t vbase = smem_u32(sV + s * ATT_TILE_BYTES);
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % ATT_STAGES;
+      const uint32_t ph = (t / ATT_STAGES) & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag, p.err));
+      if (!ok) break;
+      const uint32_t kbase = smem_u32(sK + s * ATT_TILE_BYTES);
+      const uint32_t vbase = smem_u32(sV + s * ATT_TILE_BYTES);
 
-    float sc[8][4];
+      float sc[8][4];
 #pragma unroll
-    for (int a = 0; a < 8; ++a) sc[a][0] = sc[a][1] = sc[a][2] = sc[a][3] = 0.f;
+      for (int a = 0; a < 8; ++a) sc[a][0] = sc[a][1] = sc[a][2] = sc[a][3] = 0.f;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
+      for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
-      for (int nb = 0; nb < 8; nb += 2) {
-        const int j = lane >> 3, rr = lane & 7;
-        const int key = (nb + (j >> 1)) * 8 + rr;
-        const int chunk = 2 * ks + (j & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + sw128(key, chunk), b0, b1, b2, b3);
-        mma_bf16_16816(sc[nb], qa[ks], b0, b1);
-        mma_bf16_16816(sc[nb + 1], qa[ks], b2, b3);
+        for (int nb = 0; nb < 8; nb += 2) {
+          const int j = lane >> 3, rr = lane & 7;
+          const int key = (nb + (j >> 1)) * 8 + rr;
+          const int chunk = 2 * ks + (j & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kbase + sw128(key, chunk), b0, b1, b2, b3);
+          mma_bf16_16816(sc[nb], qa[ks], b0, b1);
+          mma_bf16_16816(sc[nb + 1], qa[ks], b2, b3);
+        }
+      }
+
+      // mask (only tiles reaching past the cached prefix need it), running max
+      const int kb = k0 + t * ATT_KT;
+      if (kb + ATT_KT > P) {
+#pragma unroll
+        for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = kb + nb * 8 + tq * 2 + (e & 1);
+            if (key >= (e < 2 ? lim_lo : lim_hi)) sc[nb][e] = -INFINITY;
+          }
+        }
+      }
+      float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        mx_lo = fmaxf(mx_lo, fmaxf(sc[nb][0], sc[nb][1]));
+        mx_hi = fmaxf(mx_hi, fmaxf(sc[nb][2], sc[nb][3]));
+      }
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+      const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+      // rescale the running sums only when some row's max moved
+      if (!__all_sync(0xffffffffu, mn_lo == m_lo && mn_hi == m_hi)) {
+        const float al_lo = mn_lo == -INFINITY ? 1.f : exp2f((m_lo - mn_lo) * cexp);
+        const float al_hi = mn_hi == -INFINITY ? 1.f : exp2f((m_hi - mn_hi) * cexp);
+        l_lo *= al_lo;
+        l_hi *= al_hi;
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+          o[a][0] *= al_lo; o[a][1] *= al_lo;
+          o[a][2] *= al_hi; o[a][3] *= al_hi;
+        }
+        m_lo = mn_lo;
+        m_hi = mn_hi;
+      }
+      const float ms_lo = (m_lo == -INFINITY ? 0.f : m_lo) * cexp;
+      const float ms_hi = (m_hi == -INFINITY ? 0.f : m_hi) * cexp;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        sc[nb][0] = exp2f(fmaf(sc[nb][0], cexp, -ms_lo));
+        sc[nb][1] = exp2f(fmaf(sc[nb][1], cexp, -ms_lo));
+        sc[nb][2] = exp2f(fmaf(sc[nb][2], cexp, -ms_hi));
+        sc[nb][3] = exp2f(fmaf(sc[nb][3], cexp, -ms_hi));
+        l_lo += sc[nb][0] + sc[nb][1];
+        l_hi += sc[nb][2] + sc[nb][3];
+      }
+
+      // O += P V
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t pa[4];
+        pa[0] = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
+        pa[1] = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
+        pa[2] = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+        pa[3] = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+        for (int db = 0; db < 8; db += 2) {
+          const int j = lane >> 3, rr = lane & 7;
+          const int key = kk * 16 + (j & 1) * 8 + rr;
+          const int chunk = db + (j >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vbase + sw128(key, chunk), b0, b1, b2, b3);
+          mma_bf16_16816(o[db], pa, b0, b1);
+          mma_bf16_16816(o[db + 1], pa, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+
+    if (nchunks == 1) {
+      const float il_lo = l_lo > 0.f ? 1.f / l_lo : 0.f;
+      const float il_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
+      __nv_bfloat16* ob = p.out + static_cast<size_t>(i) * ATT_ROWS * p.H + h * 64;
+#pragma unroll
+      for (int db = 0; db < 8; ++db) {
+        const int d = db * 8 + tq * 2;
+        if (r_lo < ATT_ROWS)
+          *reinterpret_cast<uint32_t*>(ob + static_cast<size_t>(r_lo) * p.H + d) =
+              pack_bf16(o[db][0] * il_lo, o[db][1] * il_lo);
+        if (r_hi < ATT_ROWS)
+          *reinterpret_cast<uint32_t*>(ob + static_cast<size_t>(r_hi) * p.H + d) =
+              pack_bf16(o[db][2] * il_hi, o[db][3] * il_hi);
+      }
+    } else {
+      float* po = p.part_o + unit * ATT_ROWS * 64;
+      float* pml = p.part_ml + unit * ATT_ROWS * 2;
+#pragma unroll
+      for (int db = 0; db < 8; ++db) {
+        const int d = db * 8 + tq * 2;
+        if (r_lo < ATT_ROWS)
+          *reinterpret_cast<float2*>(po + r_lo * 64 + d) = make_float2(o[db][0], o[db][1]);
+        if (r_hi < ATT_ROWS)
+          *reinterpret_cast<float2*>(po + r_hi * 64 + d) = make_float2(o[db][2], o[db][3]);
+      }
+      if (tq == 0) {
+        // m in the exp2 domain
+        const float e_lo = m_lo == -INFINITY ? -INFINITY : m_lo * cexp;
+        const float e_hi = m_hi == -INFINITY ? -INFINITY : m_hi * cexp;
+        if (r_lo < ATT_ROWS) *reinterpret_cast<float2*>(pml + r_lo * 2) = make_float2(e_lo, l_lo);
+        if (r_hi < ATT_ROWS) *reinterpret_cast<float2*>(pml + r_hi * 2) = make_float2(e_hi, l_hi);
+      }
+      __threadfence();
+    }
+  }
+
+  if (nchunks == 1) return;   // CTA-uniform
+  // ---------------------------------------------------------- split-key merge
+  // The last chunk of (request, head) to finish merges every chunk's partial.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* cnt = p.sem + static_cast<size_t>(i) * p.heads + h;
+    const int prev = atomicAdd(cnt, 1);
+    if (prev == nchunks - 1) {
+      atomicExch(cnt, 0);
+      *last_flag = 1;
+    }
+  }
+  __syncthreads();
+  if (!*last_flag) return;
+  __threadfence();
+  const size_t base = (static_cast<size_t>(i) * p.MC) * p.heads + h;
+  for (int w = threadIdx.x; w < ATT_ROWS * 4; w += ATT_THREADS) {
+    const int r = w >> 2, seg = (w & 3) * 16;
+    float M = -INFINITY;
+    for (int cc = 0; cc < nchunks; ++cc)
+      M = fmaxf(M, p.part_ml[((base + static_cast<size_t>(cc) * p.heads) * ATT_ROWS + r) * 2]);
+    float L = 0.f, acc[16];
+#pragma unroll
+    for (int d = 0; d < 16; ++d) acc[d] = 0.f;
+    for (int cc = 0; cc < nchunks; ++cc) {
+      const size_t u2 = base + static_cast<size_t>(cc) * p.heads;
+      const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + (u2 * ATT_ROWS + r) * 2);
+      const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      L += wgt * ml.y;
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + (u2 * ATT_ROWS + r) * 64 + seg);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const float4 v = src[q4];
+        acc[4 * q4] += wgt * v.x; acc[4 * q4 + 1] += wgt * v.y;
+        acc[4 * q4 + 2] += wgt * v.z; acc[4 * q4 + 3] += wgt * v.w;
       }
     }
-
-    // scale, mask, running max
-    const int kb = k0 + t * ATT_KT;
-    float mx_lo = -INFINITY, mx_hi = -INFINITY;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kb + nb * 8 + tq * 2 + (e & 1);
-        const int lim = e < 2 ? lim_lo : lim_hi;
-        const float v = key < lim ? sc[nb][e] * scale : -INFINITY;
-        sc[nb][e] = v;
-        if (e < 2) mx_lo = fmaxf(mx_lo, v);
-        else mx_hi = fmaxf(mx_hi, v);
-      }
-    }
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-    const float mu_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
-    const float mu_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
-    const float al_lo = exp2f(m_lo - mu_lo), al_hi = exp2f(m_hi - mu_hi);
-    m_lo = mn_lo;
-    m_hi = mn_hi;
-    l_lo *= al_lo;
-    l_hi *= al_hi;
-#pragma unroll
-    for (int a = 0; a < 8; ++a) {
-      o[a][0] *= al_lo; o[a][1] *= al_lo;
-      o[a][2] *= al_hi; o[a][3] *= al_hi;
-    }
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      sc[nb][0] = exp2f(sc[nb][0] - mu_lo);
-      sc[nb][1] = exp2f(sc[nb][1] - mu_lo);
-      sc[nb][2] = exp2f(sc[nb][2] - mu_hi);
-      sc[nb][3] = exp2f(sc[nb][3] - mu_hi);
-      l_lo += sc[nb][0] + sc[nb][1];
-      l_hi += sc[nb][2] + sc[nb][3];
-    }
-
-    // O += P V
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
-      pa[1] = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
-      pa[2] = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
-      pa[3] = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
-#pragma unroll
-      for (int db = 0; db < 8; db += 2) {
-        const int j = lane >> 3, rr = lane & 7;
-        const int key = kk * 16 + (j & 1) * 8 + rr;
-        const int chunk = db + (j >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + sw128(key, chunk), b0, b1, b2, b3);
-        mma_bf16_16816(o[db], pa, b0, b1);
-        mma_bf16_16816(o[db + 1], pa, b2, b3);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    const float il = L > 0.f ? 1.f / L : 0.f;
+    uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(i) * ATT_ROWS + r) * p.H +
+                                          h * 64 + seg);
+    dst[0] = make_uint4(pack_bf16(acc[0] * il, acc[1] * il), pack_bf16(acc[2] * il, acc[3] * il),
+                        pack_bf16(acc[4] * il, acc[5] * il), pack_bf16(acc[6] * il, acc[7] * il));
+    dst[1] = make_uint4(pack_bf16(acc[8] * il, acc[9] * il), pack_bf16(acc[10] * il, acc[11] * il),
+                        pack_bf16(acc[12] * il, acc[13] * il), pack_bf16(acc[14] * il, acc[15] * il));
   }
-
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-
-  if (nchunks == 1) {
-    const float il_lo = l_lo > 0.f ? 1.f / l_lo : 0.f;
-    const float il_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
-    __nv_bfloat16* ob = p.out + static_cast<size_t>(i) * ATT_ROWS * p.H + h * 64;
-#pragma unroll
-    for (int db = 0; db < 8; ++db) {
-      const int d = db * 8 + tq * 2;
-      if (r_lo < ATT_ROWS)
-        *reinterpret_cast<uint32_t*>(ob + static_cast<size_t>(r_lo) * p.H + d) =
-            pack_bf16(o[db][0] * il_lo, o[db][1] * il_lo);
-      if (r_hi < ATT_ROWS)
-        *reinterpret_cast<uint32_t*>(ob + static_cast<size_t>(r_hi) * p.H + d) =
-            pack_bf16(o[db][2] * il_hi, o[db][3] * il_hi);
-    }
-  } else {
-    const size_t unit = (static_cast<size_t>(i) * p.MC + c) * p.heads + h;
-    float* po = p.part_o + unit * ATT_ROWS * 64;
-    float* pml = p.part_ml + unit * ATT_ROWS * 2;
-#pragma unroll
-    for (int db = 0; db < 8; ++db) {
-      const int d = db * 8 + tq * 2;
-      if (r_lo < ATT_ROWS)
-        *reinterpret_cast<float2*>(po + r_lo * 64 + d) = make_float2(o[db][0], o[db][1]);
-      if (r_hi < ATT_ROWS)
-        *reinterpret_cast<float2*>(po + r_hi * 64 + d) = make_float2(o[db][2], o[db][3]);
-    }
-    if (tq == 0) {
-      if (r_lo < ATT_ROWS) *reinterpret_cast<float2*>(pml + r_lo * 2) = make_float2(m_lo, l_lo);
-      if (r_hi < ATT_ROWS) *reinterpret_cast<float2*>(pml + r_hi * 2) = make_float2(m_hi, l_hi);
-    }
-  }
-}
-
-// Merge the per-chunk partials of requests longer than one chunk.
-// One warp per (request, row, head); lane handles two of the 64 dims.
-__global__ void attn_combine(AttnParams p) {
-  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int h = wid % p.heads;
-  const int r = (wid / p.heads) % ATT_ROWS;
-  const int i = wid / (p.heads * ATT_ROWS);
-  if (i >= p.n) return;
-  const int P = p.cache_len[i], ne = p.n_ext[i];
-  const int total = P + ne + (ATT_ROWS - p.ext_slots);
-  if (P < 0 || ne < 0 || ne > p.ext_slots || total > p.max_pages * 16) return;
-  const int nchunks = (total + ATT_CH - 1) / ATT_CH;
-  if (nchunks <= 1 || nchunks > p.MC) return;
-  float M = -INFINITY;
-  for (int c = 0; c < nchunks; ++c) {
-    const size_t unit = (static_cast<size_t>(i) * p.MC + c) * p.heads + h;
-    M = fmaxf(M, p.part_ml[(unit * ATT_ROWS + r) * 2]);
-  }
-  float L = 0.f, a0 = 0.f, a1 = 0.f;
-  for (int c = 0; c < nchunks; ++c) {
-    const size_t unit = (static_cast<size_t>(i) * p.MC + c) * p.heads + h;
-    const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + (unit * ATT_ROWS + r) * 2);
-    const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
-    L += w * ml.y;
-    const float2 ov = *reinterpret_cast<const float2*>(p.part_o + (unit * ATT_ROWS + r) * 64 + 2 * lane);
-    a0 += w * ov.x;
-    a1 += w * ov.y;
-  }
-  const float il = L > 0.f ? 1.f / L : 0.f;
-  __nv_bfloat16* ob = p.out + (static_cast<size_t>(i) * ATT_ROWS + r) * p.H + h * 64 + 2 * lane;
-  *reinterpret_cast<uint32_t*>(ob) = pack_bf16(a0 * il, a1 * il);
 }
 
 }  // namespace dfm

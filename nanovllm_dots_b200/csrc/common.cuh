@@ -179,6 +179,15 @@ DFM_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 DFM_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor drains.  Everything that
+// reads or writes activations waits in pdl_wait() for the predecessor to
+// complete (and its writes to become visible); only constant data (weights,
+// tensor maps) is touched before.  Both are no-ops without the attribute.
+DFM_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DFM_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- misc math
 DFM_DEV float silu(float x) { return x / (1.0f + expf(-x)); }
 

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <utility>
 
 #include "../../include/dfm.h"
 #include "attn.cuh"
@@ -80,6 +81,37 @@ cudaError_t smem_attr_once(std::atomic<uint64_t>& done, K fn, int smem) {
   return r;
 }
 
+int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+    v = 148;
+  cache[dev & 63].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+// Launch with programmatic stream serialization (PDL): the kernel may begin
+// while the previous kernel in the stream drains; it waits in pdl_wait()
+// before touching activations.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <int BN, int ST, class Epi>
 cudaError_t gemm(const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K, const Epi& e,
                  uint32_t* err, cudaStream_t s) {
@@ -89,9 +121,9 @@ cudaError_t gemm(const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K
   constexpr int smem = GemmShape<BN, ST>::SMEM;
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
-  dim3 grid((M + GEMM_BM - 1) / GEMM_BM, N / BN);
-  fn<<<grid, GEMM_THREADS, smem, s>>>(a, b, M, K, e, err);
-  return cudaGetLastError();
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  return launch_pdl(fn, dim3(grid), dim3(GEMM_THREADS), smem, s, a, b, M, N, K, e, err);
 }
 
 constexpr RowMap kIdentity{1 << 30, 0, 0};
@@ -113,19 +145,14 @@ cudaError_t launch_attention(const CUtensorMap& pool_map, const AttnParams& p, c
   static std::atomic<uint64_t> attr_done{0};
   cudaError_t r = smem_attr_once(attr_done, attn_kernel, ATT_SMEM);
   if (r != cudaSuccess) return r;
-  dim3 grid(p.n * p.MC, p.heads);
-  attn_kernel<<<grid, ATT_THREADS, ATT_SMEM, s>>>(pool_map, p);
-  r = cudaGetLastError();
-  if (r != cudaSuccess) return r;
-  const int warps = p.n * ATT_ROWS * p.heads;
-  attn_combine<<<(warps * 32 + 255) / 256, 256, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(attn_kernel, dim3(p.n * p.MC, p.heads), dim3(ATT_THREADS), ATT_SMEM, s,
+                    pool_map, p);
 }
 
 // ---------------------------------------------------------------- handle
 struct WsLayout {
   size_t err, csilu, mod, emb1, xrows, h, xm, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
-      part_o, part_ml, total;
+      part_o, part_ml, sem, total;
 };
 
 struct Handle {
@@ -174,6 +201,7 @@ WsLayout layout_for(const DfmConfig& c, int mc) {
   L.st_extl = take(NR * c.latent_patch * c.latent_dim * 2);
   L.part_o = take(NR * mc * c.heads * ATT_ROWS * 64 * 4);
   L.part_ml = take(NR * mc * c.heads * ATT_ROWS * 2 * 4);
+  L.sem = take(NR * c.heads * 4);
   L.total = off;
   return L;
 }
@@ -212,7 +240,9 @@ bool ensure_plan(Handle* h, void* ws, void* pool) {
     return false;
   }
   // A workspace seen for the first time starts with a clear error word.
-  if (h->plan_ws != ws && cudaMemset(b + h->ws.err, 0, sizeof(uint32_t)) != cudaSuccess) return false;
+  if (h->plan_ws != ws && (cudaMemset(b + h->ws.err, 0, sizeof(uint32_t)) != cudaSuccess ||
+                           cudaMemset(b + h->ws.sem, 0, h->ws.total - h->ws.sem) != cudaSuccess))
+    return false;
   h->plan_ws = ws;
   h->plan_pool = pool;
   return true;
@@ -367,9 +397,8 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   }
   {
     const int cnt = RL * LD;
-    init_z_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(b->noise), cnt,
-                                                    f32(hd->ws.z), bf(hd->ws.zb));
-    CK(cudaGetLastError());
+    CK(launch_pdl(init_z_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s,
+                  static_cast<const __nv_bfloat16*>(b->noise), cnt, f32(hd->ws.z), bf(hd->ws.zb)));
   }
 
   // ---- condition and adaLN modulation for every step (one GEMM)
@@ -380,13 +409,11 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
     grid.t[k] = __bfloat162float(__float2bfloat16(t0));
     grid.dt[k] = __bfloat162float(__float2bfloat16(t1)) - grid.t[k];
   }
-  embed1_kernel<<<(2 * H * 32 + 255) / 256, 256, 0, s>>>(W(w.temb_w1), w.temb_b1, W(w.demb_w1),
-                                                         w.demb_b1, grid, NFE, H, f32(hd->ws.emb1));
-  CK(cudaGetLastError());
-  embed2_kernel<<<(H * 32 + 255) / 256, 256, 0, s>>>(
-      W(w.temb_w2), w.temb_b2, W(w.demb_w2), w.demb_b2, f32(hd->ws.emb1),
-      static_cast<const __nv_bfloat16*>(b->g_cond), n, NFE, H, bf(hd->ws.csilu));
-  CK(cudaGetLastError());
+  CK(launch_pdl(embed1_kernel, dim3((2 * H * 32 + 255) / 256), dim3(256), 0, s, W(w.temb_w1),
+                w.temb_b1, W(w.demb_w1), w.demb_b1, grid, NFE, H, f32(hd->ws.emb1)));
+  CK(launch_pdl(embed2_kernel, dim3((H * 32 + 255) / 256), dim3(256), 0, s, W(w.temb_w2), w.temb_b2,
+                W(w.demb_w2), w.demb_b2, static_cast<const float*>(f32(hd->ws.emb1)),
+                static_cast<const __nv_bfloat16*>(b->g_cond), n, NFE, H, bf(hd->ws.csilu)));
   CK(gemm<256, 4>(hd->a_csilu, hd->m_ada, NFE * n, static_cast<int>(modw), H,
                   store(f32(hd->ws.mod), static_cast<int>(modw), true, w.ada_b, false), err, s));
 
@@ -417,6 +444,7 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   ap.out = bf(hd->ws.ob);
   ap.part_o = f32(hd->ws.part_o);
   ap.part_ml = f32(hd->ws.part_ml);
+  ap.sem = reinterpret_cast<int*>(ws + hd->ws.sem);
   ap.cache_len = b->cache_len;
   ap.n_ext = b->n_extend;
   ap.block_table = b->block_table;
@@ -439,9 +467,9 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
     CK(gemm<128, 6>(hd->a_xrows, hd->m_in, R, H, H, store(hbuf, H, true, w.input_b, false), err, s));
     for (int l = 0; l < L; ++l) {
       const float* mb = mod_k + static_cast<size_t>(l) * 6 * H;
-      ln_mod_kernel<<<(R * 32 + 255) / 256, 256, 0, s>>>(hbuf, R, kIdentity, mb, mb + H,
-                                                         static_cast<int>(modw), kSlot, xm, c.ln_eps);
-      CK(cudaGetLastError());
+      CK(launch_pdl(ln_mod_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, s,
+                    static_cast<const float*>(hbuf), R, kIdentity, mb, mb + H, static_cast<int>(modw),
+                    kSlot, xm, c.ln_eps));
       EpiQKV eq;
       eq.q_out = bf(hd->ws.qb);
       eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
@@ -467,9 +495,9 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       CK(launch_attention(hd->pool, ap, s));
       EpiResid ea{hbuf, H, w.o_b + static_cast<size_t>(l) * H, mb + 2 * H, static_cast<int>(modw), kSlot};
       CK(gemm<128, 6>(hd->a_ob, hd->m_o[l], R, H, H, ea, err, s));
-      ln_mod_kernel<<<(R * 32 + 255) / 256, 256, 0, s>>>(hbuf, R, kIdentity, mb + 3 * H, mb + 4 * H,
-                                                         static_cast<int>(modw), kSlot, xm, c.ln_eps);
-      CK(cudaGetLastError());
+      CK(launch_pdl(ln_mod_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, s,
+                    static_cast<const float*>(hbuf), R, kIdentity, mb + 3 * H, mb + 4 * H,
+                    static_cast<int>(modw), kSlot, xm, c.ln_eps));
       CK(gemm<256, 4>(hd->a_xm, hd->m_fc1[l], R, c.ffn, H,
                       store(bf(hd->ws.u), c.ffn, false, w.fc1_b + static_cast<size_t>(l) * c.ffn, true),
                       err, s));
@@ -478,10 +506,9 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
     }
     // final layer on the 16 latent rows of each request, then z += dt * v
     const float* mf = mod_k + static_cast<size_t>(L) * 6 * H;
-    ln_mod_kernel<<<(RL * 32 + 255) / 256, 256, 0, s>>>(hbuf, RL, RowMap{LPAT, kSlot, kStride + 1}, mf,
-                                                        mf + H, static_cast<int>(modw), LPAT,
-                                                        bf(hd->ws.xmf), c.ln_eps);
-    CK(cudaGetLastError());
+    CK(launch_pdl(ln_mod_kernel, dim3((RL * 32 + 255) / 256), dim3(256), 0, s,
+                  static_cast<const float*>(hbuf), RL, RowMap{LPAT, kSlot, kStride + 1}, mf, mf + H,
+                  static_cast<int>(modw), LPAT, bf(hd->ws.xmf), c.ln_eps));
     EpiSolver es;
     es.z = f32(hd->ws.z);
     es.zb = k == NFE - 1 ? static_cast<__nv_bfloat16*>(b->out) : bf(hd->ws.zb);
@@ -511,11 +538,24 @@ int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* Wt,
   return r == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
 
+// Standalone attention workspace: [error word | partial O | partial (m, l) | counters].
+struct AttnWs {
+  size_t part_o, part_ml, sem, total;
+};
+AttnWs attn_ws(int32_t n, int32_t max_pages, int32_t heads) {
+  const size_t mc = attn_chunks(max_pages);
+  auto up = [](size_t x) { return (x + 1023) & ~static_cast<size_t>(1023); };
+  AttnWs a;
+  a.part_o = 1024;
+  a.part_ml = a.part_o + up(static_cast<size_t>(n) * mc * heads * ATT_ROWS * 64 * 4);
+  a.sem = a.part_ml + up(static_cast<size_t>(n) * mc * heads * ATT_ROWS * 2 * 4);
+  a.total = a.sem + up(static_cast<size_t>(n) * heads * 4);
+  return a;
+}
+
 size_t dfm_attention_workspace_size(int32_t n, int32_t max_pages, int32_t heads) {
   if (n < 1 || max_pages < 1 || heads < 1) return 0;
-  const size_t mc = attn_chunks(max_pages);
-  const size_t a = (static_cast<size_t>(n) * mc * heads * ATT_ROWS * 64 * 4 + 1023) & ~static_cast<size_t>(1023);
-  return 1024 + a + static_cast<size_t>(n) * mc * heads * ATT_ROWS * 2 * 4;
+  return attn_ws(n, max_pages, heads).total;
 }
 
 int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t num_pages,
@@ -538,9 +578,10 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.out = static_cast<__nv_bfloat16*>(out);
   p.err = reinterpret_cast<uint32_t*>(ws);
-  p.part_o = reinterpret_cast<float*>(ws + 1024);
-  p.part_ml = reinterpret_cast<float*>(
-      ws + 1024 + ((static_cast<size_t>(n) * mc * heads * ATT_ROWS * 64 * 4 + 1023) & ~static_cast<size_t>(1023)));
+  const AttnWs aw = attn_ws(n, max_pages, heads);
+  p.part_o = reinterpret_cast<float*>(ws + aw.part_o);
+  p.part_ml = reinterpret_cast<float*>(ws + aw.part_ml);
+  p.sem = reinterpret_cast<int*>(ws + aw.sem);
   p.cache_len = cache_len;
   p.n_ext = n_extend;
   p.block_table = block_table;

@@ -16,6 +16,8 @@ __global__ void __launch_bounds__(256)
   constexpr int H = 1024;
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (r >= M) return;
   const float* hr = h + static_cast<size_t>(in_map(r)) * H;
   float4 x[8];
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(256)
                   TimeGrid grid, int nfe, int H, float* __restrict__ out1) {
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (wid >= 2 * H) return;
   const int e = wid / H, j = wid - e * H;
   const __nv_bfloat16* w = (e == 0 ? w_t : w_d) + static_cast<size_t>(j) * 256 + lane * 8;
@@ -105,6 +109,8 @@ __global__ void __launch_bounds__(256)
                   int nfe, int H, __nv_bfloat16* __restrict__ csilu) {
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (j >= H) return;
   float ck[EMB_MAX_STEPS];
 #pragma unroll
@@ -150,6 +156,8 @@ __global__ void __launch_bounds__(256)
 __global__ void init_z_kernel(const __nv_bfloat16* __restrict__ noise, int count,
                               float* __restrict__ z, __nv_bfloat16* __restrict__ zb) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_trigger();
+  pdl_wait();
   if (idx >= count) return;
   const __nv_bfloat16 v = noise[idx];
   z[idx] = __bfloat162float(v);

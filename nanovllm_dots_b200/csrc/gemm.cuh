@@ -2,7 +2,7 @@
 // epilogue fused (bias, GELU, adaLN gate + residual, per-head LayerNorm +
 // rotary + paged K/V write, MeanFlow solver update).
 //
-// One CTA computes one 128 x BN output tile.  Warp roles (192 threads):
+// Output tiles are 128 x BN.  Warp roles (192 threads):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a
 //               STAGES-deep shared-memory ring, one mbarrier per stage
 //   warp 1      TMEM allocator + the single thread that issues tcgen05.mma
@@ -30,7 +30,9 @@ struct GemmShape {
   static constexpr int B_BYTES = BN * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  // two accumulator buffers of BN fp32 columns, rounded up to a power of two
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128
+                                        : 2 * BN <= 256 ? 256 : 512;
 };
 
 // ---------------------------------------------------------------- epilogues
@@ -281,10 +283,14 @@ struct EpiSolver {
 };
 
 // ---------------------------------------------------------------- kernel
+// Persistent: grid = min(tiles, SMs); CTA b computes tiles b, b + grid, ...
+// in (m fastest) order, so CTAs working at the same time share weight tiles in
+// L2.  The TMEM accumulator is double-buffered: the epilogue of tile u drains
+// buffer u%2 while the MMA thread fills the other buffer for tile u+1.
 template <int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 int M, int K, Epi epi, uint32_t* err) {
+                 int M, int N, int K, Epi epi, uint32_t* err) {
   using S = GemmShape<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -293,12 +299,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* sB = smem + STAGES * S::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* tmem_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  uint64_t* tm_full = empty + STAGES;   // [2]
+  uint64_t* tm_empty = tm_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * GEMM_BM, n0 = blockIdx.y * BN;
+  const int tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+  const int total = tiles_m * (N / BN);
   const int nk = K / GEMM_BK;
 
   if (threadIdx.x == 0) {
@@ -307,7 +315,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tmem_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tm_full[b], 1);
+      mbar_init(&tm_empty[b], 4);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch(&tmA);
@@ -321,50 +332,89 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
+      // Weights do not depend on the previous kernel: fetch the first stages of
+      // the first tile's W before waiting for it, then its activations.
+      const int pre = (blockIdx.x < total) ? (nk < STAGES ? nk : STAGES) : 0;
+      const int n00 = (blockIdx.x / tiles_m) * BN;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], S::STAGE_BYTES);
+        tma_load_2d(sB + kb * S::B_BYTES, &tmB, &full[kb], kb * GEMM_BK, n00);
+      }
+      pdl_wait();
+      int g = 0;
+      bool ok = true;
 #pragma unroll 1
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (kb >= STAGES && !mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) break;
-        mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
-        tma_load_2d(sA + s * S::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m0);
-        tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], kb * GEMM_BK, n0);
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        const int m0 = (t % tiles_m) * GEMM_BM, n0 = (t / tiles_m) * BN;
+#pragma unroll 1
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (g >= pre) {
+            if (g >= STAGES && !mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+            tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], kb * GEMM_BK, n0);
+          }
+          tma_load_2d(sA + s * S::A_BYTES, &tmA, &full[s], kb * GEMM_BK, m0);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(GEMM_BM, BN);
+      int g = 0, u = 0;
       bool ok = true;
 #pragma unroll 1
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag, err)) {
-          ok = false;
-          break;
-        }
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++u) {
+        const int b = u & 1;
+        if (u >= 2 && !mbar_wait(&tm_empty[b], ((u >> 1) & 1) ^ 1, abort_flag, err)) break;
         tc_fence_after();
-        const uint32_t a = smem_u32(sA + s * S::A_BYTES);
-        const uint32_t b = smem_u32(sB + s * S::B_BYTES);
+        const uint32_t acc = tmem + b * BN;
+#pragma unroll 1
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + s * S::A_BYTES);
+          const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < GEMM_BK / 16; ++kk)
-          umma_bf16(tmem, umma_desc_sw128(a + kk * 32), umma_desc_sw128(b + kk * 32), idesc,
-                    (kb | kk) != 0);
-        umma_commit(&empty[s]);
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk)
+            umma_bf16(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+                      (kb | kk) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tm_full[b]);
       }
-      if (ok) umma_commit(tmem_full);
     }
   } else {
+    pdl_wait();
     const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
-    // The TMEM loads are warp-collective: decide for the whole warp.
-    const bool ready = __all_sync(0xffffffffu, mbar_wait(tmem_full, 0, abort_flag, err));
-    if (ready) {
+    int u = 0;
+#pragma unroll 1
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++u) {
+      const int b = u & 1;
+      // The TMEM loads are warp-collective: decide for the whole warp.
+      const bool ready =
+          __all_sync(0xffffffffu, mbar_wait(&tm_full[b], (u >> 1) & 1, abort_flag, err));
+      if (!ready) break;
       tc_fence_after();
-      epi.template run<BN>(tmem + (static_cast<uint32_t>(q * 32) << 16), row, n0, M);
+      const int m0 = (t % tiles_m) * GEMM_BM, n0 = (t / tiles_m) * BN;
+      epi.template run<BN>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), m0 + q * 32 + lane,
+                           n0, M);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[b]);
     }
   }
   tc_fence_before();
