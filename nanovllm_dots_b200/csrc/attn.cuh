@@ -25,8 +25,9 @@
 namespace dfm {
 
 constexpr int ATT_KT = 64;       // keys per tile
-constexpr int ATT_STAGES = 4;
-constexpr int ATT_CH = 512;      // keys per work unit
+constexpr int ATT_STAGES = 3;
+constexpr int ATT_CH = 1024;     // target keys per work unit (a request's keys are split
+                                 // into ceil(total / ATT_CH) equal chunks of whole tiles)
 constexpr int ATT_ROWS = 34;     // query rows per request
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_TILE_BYTES = ATT_KT * 64 * 2;  // 8 KB per K (or V) tile
@@ -71,7 +72,7 @@ DFM_DEV uint32_t sw128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(ATT_THREADS)
+__global__ void __launch_bounds__(ATT_THREADS, 4)
     attn_kernel(const __grid_constant__ CUtensorMap tm_pool, AttnParams p) {
   const int i = blockIdx.x / p.MC;
   const int c = blockIdx.x - i * p.MC;
@@ -89,9 +90,11 @@ __global__ void __launch_bounds__(ATT_THREADS)
   }
   const int nchunks = (total + ATT_CH - 1) / ATT_CH;
   if (c >= nchunks || nchunks > p.MC) return;
-  const int k0 = c * ATT_CH;
-  const int k1 = min(total, k0 + ATT_CH);
-  const int ntiles = (k1 - k0 + ATT_KT - 1) / ATT_KT;
+  const int tiles_all = (total + ATT_KT - 1) / ATT_KT;
+  const int tiles_per = (tiles_all + nchunks - 1) / nchunks;
+  const int k0 = c * tiles_per * ATT_KT;
+  const int k1 = min(total, k0 + tiles_per * ATT_KT);
+  const int ntiles = k1 > k0 ? (k1 - k0 + ATT_KT - 1) / ATT_KT : 0;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -175,16 +178,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
     for (int a = 0; a < 8; ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
     float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
 
-#pragma unroll 1
-    for (int t = 0; t < ntiles; ++t) {
-      const int s = t % ATT_STAGES;
-      const uint32_t ph = (t / ATT_STAGES) & 1;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag, p.err));
-      if (!ok) break;
-      const uint32_t kbase = smem_u32(sK + s * ATT_TILE_BYTES);
-      const uint32_t vbase = smem_u32(sV + s * ATT_TILE_BYTES);
-
-      float sc[8][4];
+    // S = Q K^T of one 64-key tile (raw scores, fp32)
+    auto qk = [&](uint32_t kbase, float (&sc)[8][4]) {
 #pragma unroll
       for (int a = 0; a < 8; ++a) sc[a][0] = sc[a][1] = sc[a][2] = sc[a][3] = 0.f;
 #pragma unroll
@@ -200,9 +195,22 @@ __global__ void __launch_bounds__(ATT_THREADS)
           mma_bf16_16816(sc[nb + 1], qa[ks], b2, b3);
         }
       }
+    };
+    auto wait_tile = [&](int t) {
+      return __all_sync(0xffffffffu, mbar_wait(&full[t % ATT_STAGES], (t / ATT_STAGES) & 1,
+                                               abort_flag, p.err));
+    };
 
-      // mask (only tiles reaching past the cached prefix need it), running max
+    // Software pipeline: the QK^T of tile t+1 is issued before the PV of tile
+    // t, so a warp always has independent tensor work while its softmax runs.
+    float sc[8][4];
+    bool ok = ntiles > 0 && wait_tile(0);
+    if (ok) qk(smem_u32(sK), sc);
+#pragma unroll 1
+    for (int t = 0; ok && t < ntiles; ++t) {
+      const int s = t % ATT_STAGES;
       const int kb = k0 + t * ATT_KT;
+      // mask (only tiles reaching past the cached prefix need it), running max
       if (kb + ATT_KT > P) {
 #pragma unroll
         for (int nb = 0; nb < 8; ++nb) {
@@ -240,24 +248,34 @@ __global__ void __launch_bounds__(ATT_THREADS)
       }
       const float ms_lo = (m_lo == -INFINITY ? 0.f : m_lo) * cexp;
       const float ms_hi = (m_hi == -INFINITY ? 0.f : m_hi) * cexp;
-#pragma unroll
-      for (int nb = 0; nb < 8; ++nb) {
-        sc[nb][0] = exp2f(fmaf(sc[nb][0], cexp, -ms_lo));
-        sc[nb][1] = exp2f(fmaf(sc[nb][1], cexp, -ms_lo));
-        sc[nb][2] = exp2f(fmaf(sc[nb][2], cexp, -ms_hi));
-        sc[nb][3] = exp2f(fmaf(sc[nb][3], cexp, -ms_hi));
-        l_lo += sc[nb][0] + sc[nb][1];
-        l_hi += sc[nb][2] + sc[nb][3];
-      }
-
-      // O += P V
+      uint32_t pa[4][4];
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        uint32_t pa[4];
-        pa[0] = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
-        pa[1] = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
-        pa[2] = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
-        pa[3] = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+        float e[2][4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int nb = 2 * kk + hh;
+          e[hh][0] = exp2f(fmaf(sc[nb][0], cexp, -ms_lo));
+          e[hh][1] = exp2f(fmaf(sc[nb][1], cexp, -ms_lo));
+          e[hh][2] = exp2f(fmaf(sc[nb][2], cexp, -ms_hi));
+          e[hh][3] = exp2f(fmaf(sc[nb][3], cexp, -ms_hi));
+          l_lo += e[hh][0] + e[hh][1];
+          l_hi += e[hh][2] + e[hh][3];
+        }
+        pa[kk][0] = pack_bf16(e[0][0], e[0][1]);
+        pa[kk][1] = pack_bf16(e[0][2], e[0][3]);
+        pa[kk][2] = pack_bf16(e[1][0], e[1][1]);
+        pa[kk][3] = pack_bf16(e[1][2], e[1][3]);
+      }
+      // next tile's scores
+      if (t + 1 < ntiles) {
+        ok = wait_tile(t + 1);
+        if (ok) qk(smem_u32(sK + ((t + 1) % ATT_STAGES) * ATT_TILE_BYTES), sc);
+      }
+      // O += P V
+      const uint32_t vbase = smem_u32(sV + s * ATT_TILE_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
         for (int db = 0; db < 8; db += 2) {
           const int j = lane >> 3, rr = lane & 7;
@@ -265,8 +283,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
           const int chunk = db + (j >> 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(vbase + sw128(key, chunk), b0, b1, b2, b3);
-          mma_bf16_16816(o[db], pa, b0, b1);
-          mma_bf16_16816(o[db + 1], pa, b2, b3);
+          mma_bf16_16816(o[db], pa[kk], b0, b1);
+          mma_bf16_16816(o[db + 1], pa[kk], b2, b3);
         }
       }
       __syncwarp();
