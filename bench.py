@@ -42,13 +42,14 @@ METRIC = "FM-head latent xRT (audio-s/s) at conc 64 per GPU"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "prof", "gemm64"],
                     help="prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool)")
-    ap.add_argument("--cpu-sample", type=int, default=8, help="requests in the CPU baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=64,
+                    help="requests in the CPU baseline sample (64 = one whole tick)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-tick", action="store_true",
                     help="run one eager tick inside cudaProfilerStart/Stop (for ncu "
@@ -102,7 +103,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.index)],
+                 "-lms", "100", "-i", str(self.index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
