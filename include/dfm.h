@@ -36,6 +36,7 @@ extern "C" {
 #define DFM_ERR_CUDA 3          /* a CUDA runtime/driver call failed */
 #define DFM_ERR_WORKSPACE 4     /* workspace too small */
 #define DFM_ERR_DEVICE 5        /* a kernel reported an error (dfm_read_error bits) */
+#define DFM_ERR_SCRATCH_LIMIT 6 /* a call needs more than the fixed scratch of a no-allocation entry point */
 
 /* Bits of the device error word returned by dfm_read_error. */
 #define DFM_DEVERR_TIMEOUT 1u   /* a bounded in-kernel wait gave up */
@@ -166,6 +167,33 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
                         const int32_t* cache_len, const int32_t* n_extend,
                         const int32_t* block_table, int32_t max_pages, int32_t n,
                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Paged prefix attention with no workspace argument and no allocation.
+ * This entry point has no counterpart in the reference.  It is for callers
+ * that cannot allocate device memory at the point of the call, for example a
+ * host framework whose allocator is not reachable from the thread that
+ * launches work, or code running inside a tight memory budget that may not
+ * grow.  It computes exactly what dfm_paged_attention computes; its split-key
+ * partials and completion counters live in one fixed array inside the library
+ * (DFM_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held until
+ * the process exits) instead of a caller workspace.
+ *   - Calls needing more than that scratch (dfm_attention_workspace_size(n,
+ *     max_pages, heads) > DFM_NOALLOC_SCRATCH_BYTES) return
+ *     DFM_ERR_SCRATCH_LIMIT and launch nothing.
+ *   - The first call on a device looks up the scratch's device address (a
+ *     synchronous runtime call); make that first call before any stream
+ *     capture.
+ *   - All calls share the one array, which keeps the last call's contents:
+ *     calls that overlap on the GPU (different streams, no ordering between
+ *     them) race and corrupt each other's results.
+ *   - err_word (device, may be NULL) receives the DFM_DEVERR_* bits; it is not
+ *     cleared by the call. */
+#define DFM_NOALLOC_SCRATCH_BYTES (8u << 20)
+int dfm_paged_attention_noalloc(const void* q, void* out, const void* kv_pool, int32_t num_pages,
+                                int32_t num_planes, int32_t heads, int32_t plane_k, int32_t plane_v,
+                                const int32_t* cache_len, const int32_t* n_extend,
+                                const int32_t* block_table, int32_t max_pages, int32_t n,
+                                uint32_t* err_word, void* stream);
 
 #ifdef __cplusplus
 }

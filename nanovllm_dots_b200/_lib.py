@@ -18,7 +18,7 @@ DEVERR_BITS = {1: "timeout", 2: "page", 4: "len"}
 
 EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "dfm_read_error",
            "dfm_destroy", "dfm_error_string", "dfm_linear", "dfm_attention_workspace_size",
-           "dfm_paged_attention")
+           "dfm_paged_attention", "dfm_paged_attention_noalloc")
 
 
 class DfmConfig(ctypes.Structure):
@@ -83,6 +83,10 @@ def lib() -> ctypes.CDLL:
                                       c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32,
                                       c_int32, c_void_p, c_size_t, c_void_p]
     L.dfm_paged_attention.restype = c_int32
+    L.dfm_paged_attention_noalloc.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                              c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                              c_void_p, c_int32, c_int32, c_void_p, c_void_p]
+    L.dfm_paged_attention_noalloc.restype = c_int32
     _lib = L
     return L
 

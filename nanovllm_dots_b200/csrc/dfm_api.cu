@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <utility>
 
@@ -266,6 +267,8 @@ const char* dfm_error_string(int code) {
     case DFM_ERR_CUDA: return "CUDA error";
     case DFM_ERR_WORKSPACE: return "workspace too small";
     case DFM_ERR_DEVICE: return "device-side error";
+    case DFM_ERR_SCRATCH_LIMIT:
+      return "call exceeds the fixed scratch of the no-allocation entry point";
     default: return "unknown error";
   }
 }
@@ -598,3 +601,79 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation attention
+// Scratch of dfm_paged_attention_noalloc: [error word | partial O | partial
+// (m, l) | counters], laid out as for dfm_paged_attention's workspace.  In host
+// code `g_noalloc_scratch` names a host-side stand-in, not device memory: the
+// kernel gets the address cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[DFM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch on the current device, looked up once per
+// device (a synchronous runtime call: the first call must precede capture).
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return r;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    r = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (r != cudaSuccess) return r;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void* kv_pool,
+                                           int32_t num_pages, int32_t num_planes, int32_t heads,
+                                           int32_t plane_k, int32_t plane_v,
+                                           const int32_t* cache_len, const int32_t* n_extend,
+                                           const int32_t* block_table, int32_t max_pages,
+                                           int32_t n, uint32_t* err_word, void* stream) {
+  if (!q || !out || !kv_pool || !cache_len || !n_extend || !block_table) return DFM_ERR_INVALID_ARG;
+  if (n < 1 || heads < 1 || num_pages < 1 || max_pages < 1 || plane_k < 0 || plane_v < 0 ||
+      plane_k >= num_planes || plane_v >= num_planes)
+    return DFM_ERR_INVALID_ARG;
+  const AttnWs aw = attn_ws(n, max_pages, heads);
+  if (aw.total > DFM_NOALLOC_SCRATCH_BYTES) return DFM_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (noalloc_scratch(&scratch) != cudaSuccess) return DFM_ERR_CUDA;
+  CUtensorMap pm;
+  if (!map_pool(&pm, kv_pool, num_pages, heads, num_planes)) return DFM_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  // the array keeps the previous call's contents: clear the counters (and the
+  // internal error word) this call relies on starting at zero
+  if (cudaMemsetAsync(ws + aw.sem, 0, aw.total - aw.sem, s) != cudaSuccess) return DFM_ERR_CUDA;
+  if (!err_word && cudaMemsetAsync(ws, 0, sizeof(uint32_t), s) != cudaSuccess) return DFM_ERR_CUDA;
+  AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.err = err_word ? err_word : reinterpret_cast<uint32_t*>(ws);
+  p.part_o = reinterpret_cast<float*>(ws + aw.part_o);
+  p.part_ml = reinterpret_cast<float*>(ws + aw.part_ml);
+  p.sem = reinterpret_cast<int*>(ws + aw.sem);
+  p.cache_len = cache_len;
+  p.n_ext = n_extend;
+  p.block_table = block_table;
+  p.n = n;
+  p.max_pages = max_pages;
+  p.num_pages = num_pages;
+  p.heads = heads;
+  p.H = heads * 64;
+  p.MC = attn_chunks(max_pages);
+  p.plane_k = plane_k;
+  p.plane_v = plane_v;
+  p.ext_slots = kStride;
+  return launch_attention(pm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
+}
