@@ -16,7 +16,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdfm.so")
 SOURCES = ["dfm_api.cu"]
-DEPS = ["dfm_api.cu", "common.cuh", "gemm.cuh", "attn.cuh", "ew.cuh"]
+DEPS = ["dfm_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh"]
 HEADER = os.path.join(os.path.dirname(PKG), "include", "dfm.h")
 
 

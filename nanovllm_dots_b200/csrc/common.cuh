@@ -68,6 +68,26 @@ DFM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase with the given parity.
+DFM_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// 2^x with the hardware approximation (ex2.approx.ftz.f32; -inf -> +0).
+DFM_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false when the
 // CTA is aborting (flag already set, or this wait timed out and set it).
 DFM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -152,6 +172,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
          | (static_cast<uint32_t>(M >> 4) << 24); // M / 16
 }
 
+// Instruction descriptor as above with B MN-major (B stored [K][N], N contiguous).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) {
+  return umma_idesc_bf16(M, N) | (1u << 16);
+}
+
 // Shared-memory matrix descriptor of a K-major tile stored with the 128-byte
 // swizzle (rows of 64 bf16, 8-row atoms of 1024 bytes, atoms packed densely).
 DFM_DEV uint64_t umma_desc_sw128(uint32_t smem_addr) {
@@ -163,6 +188,10 @@ DFM_DEV uint64_t umma_desc_sw128(uint32_t smem_addr) {
   d |= static_cast<uint64_t>(2) << 61;                      // layout: 128-byte swizzle
   return d;
 }
+
+// The same descriptor fields describe an MN-major operand whose N extent is one
+// 64-element swizzle atom (rows = K index, 128 bytes of N each, 8-row groups
+// 1024 bytes apart): the stride byte offset is then the K-group stride.
 
 // 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
 DFM_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -178,6 +207,37 @@ DFM_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 DFM_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns -> 16 registers per thread.
+DFM_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// 32 registers per thread -> 32 lanes x 32 consecutive 32-bit TMEM columns.
+DFM_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31]));
+}
+DFM_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tcgen05.mma operand reads).
+DFM_DEV void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 // ---------------------------------------------------------------- PDL
 // Programmatic dependent launch: a kernel launched with programmatic stream

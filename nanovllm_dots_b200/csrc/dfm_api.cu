@@ -11,7 +11,7 @@
 #include <utility>
 
 #include "../../include/dfm.h"
-#include "attn.cuh"
+#include "attn_tc.cuh"
 #include "ew.cuh"
 #include "gemm.cuh"
 
@@ -140,14 +140,20 @@ EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMa
   return e;
 }
 
-int attn_chunks(int max_pages) { return (max_pages * 16 + kSlot + ATT_CH - 1) / ATT_CH; }
+int attn_chunks(int max_pages) { return (max_pages * 16 + kSlot + TA_CH - 1) / TA_CH; }
 
-cudaError_t launch_attention(const CUtensorMap& pool_map, const AttnParams& p, cudaStream_t s) {
+cudaError_t launch_attention(const CUtensorMap& pool_map, const CUtensorMap& q_map,
+                             const AttnParams& p, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
-  cudaError_t r = smem_attr_once(attr_done, attn_kernel, ATT_SMEM);
+  cudaError_t r = smem_attr_once(attr_done, attn_tc_kernel, TA_SMEM);
   if (r != cudaSuccess) return r;
-  return launch_pdl(attn_kernel, dim3(p.n * p.MC, p.heads), dim3(ATT_THREADS), ATT_SMEM, s,
-                    pool_map, p);
+  return launch_pdl(attn_tc_kernel, dim3(p.n * p.MC * p.heads), dim3(TA_THREADS), TA_SMEM, s,
+                    pool_map, q_map, p);
+}
+
+// Query rows of the 34-row request layout as TMA boxes of 48 rows x 64 dims.
+bool map_q(CUtensorMap* m, const void* q, uint64_t rows, int heads) {
+  return map_2d(m, q, rows, static_cast<uint64_t>(heads) * 64, static_cast<uint64_t>(heads) * 64, TA_QN);
 }
 
 // ---------------------------------------------------------------- handle
@@ -171,7 +177,7 @@ struct Handle {
   // per-workspace/pool descriptors
   const void* plan_ws = nullptr;
   const void* plan_pool = nullptr;
-  CUtensorMap a_csilu, a_xrows, a_xm, a_ob, a_u, a_zb, a_xmf, a_act, a_exth, a_extl, pool;
+  CUtensorMap a_csilu, a_xrows, a_xm, a_ob, a_u, a_zb, a_xmf, a_act, a_exth, a_extl, pool, q_att;
 };
 
 WsLayout layout_for(const DfmConfig& c, int mc) {
@@ -200,8 +206,8 @@ WsLayout layout_for(const DfmConfig& c, int mc) {
   L.st_act = take(NR * c.cond_dim * 2);
   L.st_exth = take(NR * c.cond_dim * 2);
   L.st_extl = take(NR * c.latent_patch * c.latent_dim * 2);
-  L.part_o = take(NR * mc * c.heads * ATT_ROWS * 64 * 4);
-  L.part_ml = take(NR * mc * c.heads * ATT_ROWS * 2 * 4);
+  L.part_o = take(NR * mc * c.heads * TA_ROWS * 64 * 4);
+  L.part_ml = take(NR * mc * c.heads * TA_ROWS * 2 * 4);
   L.sem = take(NR * c.heads * 4);
   L.total = off;
   return L;
@@ -235,6 +241,7 @@ bool ensure_plan(Handle* h, void* ws, void* pool) {
             map_2d(&h->a_act, b + h->ws.st_act, NR, c.cond_dim, c.cond_dim, 128) &&
             map_2d(&h->a_exth, b + h->ws.st_exth, NR, c.cond_dim, c.cond_dim, 128) &&
             map_2d(&h->a_extl, b + h->ws.st_extl, LP, c.latent_dim, c.latent_dim, 128) &&
+            map_q(&h->q_att, b + h->ws.qb, R, c.heads) &&
             map_pool(&h->pool, pool, c.num_pages, c.heads, c.layers * c.nfe * 2);
   if (!ok) {
     h->plan_ws = h->plan_pool = nullptr;
@@ -495,7 +502,7 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       CK(gemm<256, 4>(hd->a_xm, hd->m_qkv[l], R, 3 * H, H, eq, err, s));
       ap.plane_k = eq.plane_k;
       ap.plane_v = eq.plane_v;
-      CK(launch_attention(hd->pool, ap, s));
+      CK(launch_attention(hd->pool, hd->q_att, ap, s));
       EpiResid ea{hbuf, H, w.o_b + static_cast<size_t>(l) * H, mb + 2 * H, static_cast<int>(modw), kSlot};
       CK(gemm<128, 6>(hd->a_ob, hd->m_o[l], R, H, H, ea, err, s));
       CK(launch_pdl(ln_mod_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, s,
@@ -550,8 +557,8 @@ AttnWs attn_ws(int32_t n, int32_t max_pages, int32_t heads) {
   auto up = [](size_t x) { return (x + 1023) & ~static_cast<size_t>(1023); };
   AttnWs a;
   a.part_o = 1024;
-  a.part_ml = a.part_o + up(static_cast<size_t>(n) * mc * heads * ATT_ROWS * 64 * 4);
-  a.sem = a.part_ml + up(static_cast<size_t>(n) * mc * heads * ATT_ROWS * 2 * 4);
+  a.part_ml = a.part_o + up(static_cast<size_t>(n) * mc * heads * TA_ROWS * 64 * 4);
+  a.sem = a.part_ml + up(static_cast<size_t>(n) * mc * heads * TA_ROWS * 2 * 4);
   a.total = a.sem + up(static_cast<size_t>(n) * heads * 4);
   return a;
 }
@@ -572,8 +579,9 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
       plane_k >= num_planes || plane_v >= num_planes)
     return DFM_ERR_INVALID_ARG;
   if (workspace_bytes < dfm_attention_workspace_size(n, max_pages, heads)) return DFM_ERR_WORKSPACE;
-  CUtensorMap pm;
+  CUtensorMap pm, qm;
   if (!map_pool(&pm, kv_pool, num_pages, heads, num_planes)) return DFM_ERR_CUDA;
+  if (!map_q(&qm, q, static_cast<uint64_t>(n) * TA_ROWS, heads)) return DFM_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int mc = attn_chunks(max_pages);
@@ -597,7 +605,7 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
   p.plane_k = plane_k;
   p.plane_v = plane_v;
   p.ext_slots = kStride;
-  return launch_attention(pm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
+  return launch_attention(pm, qm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
 
 }  // extern "C"
@@ -648,8 +656,9 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
   if (aw.total > DFM_NOALLOC_SCRATCH_BYTES) return DFM_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   if (noalloc_scratch(&scratch) != cudaSuccess) return DFM_ERR_CUDA;
-  CUtensorMap pm;
+  CUtensorMap pm, qm;
   if (!map_pool(&pm, kv_pool, num_pages, heads, num_planes)) return DFM_ERR_CUDA;
+  if (!map_q(&qm, q, static_cast<uint64_t>(n) * TA_ROWS, heads)) return DFM_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(scratch);
   // the array keeps the previous call's contents: clear the counters (and the
@@ -675,5 +684,5 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
   p.plane_k = plane_k;
   p.plane_v = plane_v;
   p.ext_slots = kStride;
-  return launch_attention(pm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
+  return launch_attention(pm, qm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }

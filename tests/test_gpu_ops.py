@@ -94,10 +94,13 @@ def _attn_reference(q, pool, heads, plane_k, plane_v, cache_len, n_ext, tables):
     return out
 
 
-@pytest.mark.parametrize("lens", [[(0, 0), (0, 17), (5, 17), (40, 3)],
-                                  [(496, 17), (511, 17), (1000, 0), (2040, 17), (17, 17)]])
-def test_paged_attention_matches_reference(lens):
-    heads, num_pages, max_pages, planes = 16, 400, 130, 4
+@pytest.mark.parametrize("lens,max_pages", [
+    ([(0, 0), (0, 17), (5, 17), (40, 3)], 130),
+    ([(496, 17), (511, 17), (1000, 0), (2040, 17), (17, 17)], 130),
+    # requests longer than one 4096-key work unit: split keys + merge
+    ([(5000, 17), (4110, 0), (100, 17), (4062, 17)], 330)])
+def test_paged_attention_matches_reference(lens, max_pages):
+    heads, num_pages, planes = 16, 1200, 4
     g = torch.Generator(device=DEV).manual_seed(len(lens))
     pool = torch.randn(planes, num_pages, heads, 16, 64, device=DEV, generator=g).to(torch.bfloat16)
     n = len(lens)

@@ -35,8 +35,9 @@ def test_noalloc_refuses_calls_beyond_its_scratch():
 
 @pytest.mark.gpu
 def test_noalloc_matches_workspace_entry_point():
-    heads, num_pages, max_pages, planes = 16, 400, 130, 2
-    lens = [(496, 17), (1000, 0), (2040, 17), (17, 17), (0, 0)]   # one, two and three key chunks
+    heads, num_pages, max_pages, planes = 16, 1000, 330, 2
+    # the long requests are split over work units and merged through the scratch
+    lens = [(496, 17), (5000, 17), (2040, 17), (4110, 0), (0, 0)]
     g = torch.Generator(device=DEV).manual_seed(11)
     pool = torch.randn(planes, num_pages, heads, 16, 64, device=DEV, generator=g).to(torch.bfloat16)
     n = len(lens)
