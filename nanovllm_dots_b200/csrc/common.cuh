@@ -251,11 +251,19 @@ DFM_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::
 // ---------------------------------------------------------------- misc math
 DFM_DEV float silu(float x) { return x / (1.0f + expf(-x)); }
 
+// tanh with the hardware approximation (tanh.approx.f32, relative error ~2^-11;
+// its result is rounded to bf16 downstream).
+DFM_DEV float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 DFM_DEV float gelu_tanh(float x) {
   // GELU with the tanh approximation (torch GELU(approximate="tanh")).
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  return 0.5f * x * (1.0f + tanh_approx(k0 * (x + k1 * x * x * x)));
 }
 
 DFM_DEV float warp_sum(float v) {

@@ -159,7 +159,7 @@ bool map_q(CUtensorMap* m, const void* q, uint64_t rows, int heads) {
 // ---------------------------------------------------------------- handle
 struct WsLayout {
   size_t err, csilu, mod, emb1, xrows, h, xm, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
-      part_o, part_ml, sem, total;
+      part_o, part_ml, sem, rope, total;
 };
 
 struct Handle {
@@ -209,6 +209,7 @@ WsLayout layout_for(const DfmConfig& c, int mc) {
   L.part_o = take(NR * mc * c.heads * TA_ROWS * 64 * 4);
   L.part_ml = take(NR * mc * c.heads * TA_ROWS * 2 * 4);
   L.sem = take(NR * c.heads * 4);
+  L.rope = take(static_cast<size_t>(c.max_pages_per_req) * 16 * 32 * 8);
   L.total = off;
   return L;
 }
@@ -225,7 +226,7 @@ int validate_config(const DfmConfig& c) {
   return DFM_OK;
 }
 
-bool ensure_plan(Handle* h, void* ws, void* pool) {
+bool ensure_plan(Handle* h, void* ws, void* pool, cudaStream_t s) {
   if (h->plan_ws == ws && h->plan_pool == pool) return true;
   const DfmConfig& c = h->c;
   uint8_t* b = static_cast<uint8_t*>(ws);
@@ -249,8 +250,14 @@ bool ensure_plan(Handle* h, void* ws, void* pool) {
   }
   // A workspace seen for the first time starts with a clear error word.
   if (h->plan_ws != ws && (cudaMemset(b + h->ws.err, 0, sizeof(uint32_t)) != cudaSuccess ||
-                           cudaMemset(b + h->ws.sem, 0, h->ws.total - h->ws.sem) != cudaSuccess))
+                           cudaMemset(b + h->ws.sem, 0, h->ws.rope - h->ws.sem) != cudaSuccess))
     return false;
+  if (h->plan_ws != ws) {
+    const int cnt = h->c.max_pages_per_req * 16 * 32;
+    rope_table_kernel<<<(cnt + 255) / 256, 256, 0, s>>>(h->w.rope_inv_freq, h->c.max_pages_per_req * 16,
+                                                        reinterpret_cast<float2*>(b + h->ws.rope));
+    if (cudaGetLastError() != cudaSuccess) return false;
+  }
   h->plan_ws = ws;
   h->plan_pool = pool;
   return true;
@@ -383,7 +390,7 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   int dev = -1;
   CK(cudaGetDevice(&dev));
   if (dev != hd->device) return DFM_ERR_INVALID_ARG;
-  if (!ensure_plan(hd, workspace, b->kv_pool)) return DFM_ERR_CUDA;
+  if (!ensure_plan(hd, workspace, b->kv_pool, static_cast<cudaStream_t>(stream))) return DFM_ERR_CUDA;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -496,7 +503,8 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       eq.slot = kSlot;
       eq.ext_slots = kStride;
       eq.qk_norm = w.qk_norm + static_cast<size_t>(l) * 4 * c.head_dim;
-      eq.inv_freq = w.rope_inv_freq;
+      eq.rope = reinterpret_cast<const float2*>(ws + hd->ws.rope);
+      eq.max_pos = c.max_pages_per_req * 16;
       eq.eps = c.ln_eps;
       eq.err = err;
       CK(gemm<256, 4>(hd->a_xm, hd->m_qkv[l], R, 3 * H, H, eq, err, s));

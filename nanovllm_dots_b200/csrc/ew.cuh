@@ -152,6 +152,17 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Rotary table: tab[pos * 32 + d] = (cos, sin)(pos * inv_freq[d]), the angles
+// of ``layers.py:95-134`` for every cache position, computed once per workspace.
+__global__ void rope_table_kernel(const float* __restrict__ inv_freq, int max_pos,
+                                  float2* __restrict__ tab) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= max_pos * 32) return;
+  float sn, co;
+  sincosf(static_cast<float>(idx >> 5) * inv_freq[idx & 31], &sn, &co);
+  tab[idx] = make_float2(co, sn);
+}
+
 // z = float(noise), zb = noise (the solver state and its bf16 GEMM copy).
 __global__ void init_z_kernel(const __nv_bfloat16* __restrict__ noise, int count,
                               float* __restrict__ z, __nv_bfloat16* __restrict__ zb) {

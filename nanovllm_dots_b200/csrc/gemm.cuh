@@ -87,10 +87,9 @@ struct EpiStore {
 };
 
 // h[row, col] += gate[req(row), col] * (acc + bias[col])   (fp32 residual stream)
-// with req(row) = row / rows_per_req and gate rows gate_ld floats apart.
-// Each 32-column chunk issues all of its residual, gate and bias loads before
-// any arithmetic or store, so a thread waits one memory round trip per chunk
-// instead of one per float4.
+// with req(row) = row / rows_per_req and gate rows gate_ld floats apart.  The
+// loads of the next 32-column chunk are issued before the current chunk's
+// math, so the memory latency overlaps the TMEM load and the stores.
 struct EpiResid {
   float* h;
   int ldh;
@@ -104,30 +103,42 @@ struct EpiResid {
     const bool live = row < M;
     const float* g = gate + static_cast<size_t>(live ? row / rows_per_req : 0) * gate_ld + n0;
     float* hp = h + static_cast<size_t>(live ? row : 0) * ldh + n0;
-#pragma unroll 1
+    const float* bp = bias + n0;
+    float4 hv[8], gv[8], bv[8];
+    auto load = [&](int c, float4 (&hh)[8], float4 (&gg)[8], float4 (&bb)[8]) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        hh[j] = *reinterpret_cast<const float4*>(hp + c + 4 * j);
+        gg[j] = __ldg(reinterpret_cast<const float4*>(g + c + 4 * j));
+        bb[j] = __ldg(reinterpret_cast<const float4*>(bp + c + 4 * j));
+      }
+    };
+    if (live) load(0, hv, gv, bv);
+#pragma unroll
     for (int c = 0; c < BN; c += 32) {
       uint32_t r[32];
       tmem_ld32(taddr + c, r);
-      float4 hv[8], gv[8], bv[8];
+      float4 hn[8], gn[8], bn[8];
+      if (live && c + 32 < BN) load(c + 32, hn, gn, bn);
+      tmem_wait_ld();
       if (live) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          hv[j] = *reinterpret_cast<const float4*>(hp + c + 4 * j);
-          gv[j] = __ldg(reinterpret_cast<const float4*>(g + c + 4 * j));
-          bv[j] = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + 4 * j));
+          hv[j].x += gv[j].x * (__uint_as_float(r[4 * j]) + bv[j].x);
+          hv[j].y += gv[j].y * (__uint_as_float(r[4 * j + 1]) + bv[j].y);
+          hv[j].z += gv[j].z * (__uint_as_float(r[4 * j + 2]) + bv[j].z);
+          hv[j].w += gv[j].w * (__uint_as_float(r[4 * j + 3]) + bv[j].w);
+          *reinterpret_cast<float4*>(hp + c + 4 * j) = hv[j];
         }
       }
-      tmem_wait_ld();
-      if (!live) continue;
+      if (c + 32 < BN) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        hv[j].x += gv[j].x * (__uint_as_float(r[4 * j]) + bv[j].x);
-        hv[j].y += gv[j].y * (__uint_as_float(r[4 * j + 1]) + bv[j].y);
-        hv[j].z += gv[j].z * (__uint_as_float(r[4 * j + 2]) + bv[j].z);
-        hv[j].w += gv[j].w * (__uint_as_float(r[4 * j + 3]) + bv[j].w);
+        for (int j = 0; j < 8; ++j) {
+          hv[j] = hn[j];
+          gv[j] = gn[j];
+          bv[j] = bn[j];
+        }
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(hp + c + 4 * j) = hv[j];
     }
   }
 };
@@ -152,7 +163,8 @@ struct EpiQKV {
   int max_pages, num_pages, heads, H;
   int slot, ext_slots;
   const float* qk_norm;   // this layer's [4][64]: q_w, q_b, k_w, k_b
-  const float* inv_freq;  // [32]
+  const float2* rope;     // [max_pages*16][32] (cos, sin) of pos * inv_freq[d]
+  int max_pos;
   float eps;
   uint32_t* err;
 
@@ -179,7 +191,6 @@ struct EpiQKV {
         }
       }
     }
-    const float fpos = static_cast<float>(pos);
 #pragma unroll 1
     for (int c = 0; c < BN; c += 64) {
       uint32_t r0[32], r1[32];
@@ -212,13 +223,13 @@ struct EpiQKV {
         const float* w = qk_norm + sec * 128;
 #pragma unroll
         for (int d = 0; d < 64; ++d) x[d] = (x[d] - mean) * rstd * __ldg(w + d) + __ldg(w + 64 + d);
+        const float2* cs = rope + static_cast<size_t>(pos < 0 ? 0 : (pos < max_pos ? pos : max_pos - 1)) * 32;
 #pragma unroll
         for (int d = 0; d < 32; ++d) {
-          float sn, co;
-          sincosf(fpos * __ldg(inv_freq + d), &sn, &co);
+          const float2 t = __ldg(cs + d);
           const float a = x[d], b = x[d + 32];
-          x[d] = a * co - b * sn;
-          x[d + 32] = b * co + a * sn;
+          x[d] = a * t.x - b * t.y;
+          x[d + 32] = b * t.x + a * t.y;
         }
       }
       __nv_bfloat16* dst;
