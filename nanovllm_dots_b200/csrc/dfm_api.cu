@@ -158,7 +158,7 @@ bool map_q(CUtensorMap* m, const void* q, uint64_t rows, int heads) {
 
 // ---------------------------------------------------------------- handle
 struct WsLayout {
-  size_t err, csilu, mod, emb1, xrows, h, xm, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
+  size_t err, csilu, mod, emb1, xrows, h, sub, xm, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
       part_o, part_ml, sem, rope, total;
 };
 
@@ -196,6 +196,7 @@ WsLayout layout_for(const DfmConfig& c, int mc) {
   L.emb1 = take(2ull * c.nfe * H * 4);
   L.xrows = take(R * H * 2);
   L.h = take(R * H * 4);
+  L.sub = take(R * H * 4);
   L.xm = take(R * H * 2);
   L.qb = take(R * H * 2);
   L.ob = take(R * H * 2);
@@ -475,18 +476,23 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   ap.err = err;
 
   float* hbuf = f32(hd->ws.h);
+  float* sub = f32(hd->ws.sub);   // the last sublayer's output, added to h by the next LN
   __nv_bfloat16* xm = bf(hd->ws.xm);
+  auto ln = [&](int M, RowMap map, const float* subp, const float* gate, const float* shift,
+                const float* scale, int rows_per_req, __nv_bfloat16* out) {
+    return launch_pdl(ln_mod_kernel, dim3((M * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp, gate,
+                      M, map, shift, scale, static_cast<int>(modw), rows_per_req, out, c.ln_eps);
+  };
   for (int k = 0; k < NFE; ++k) {
     const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;
     // active latent rows = coordinate_proj(z) (batched_fm.py:117-119)
     CK(gemm<128, 6>(hd->a_zb, hd->m_coord, RL, H, LD,
                     store(xrows, H, false, w.coord_b, false, RowMap{LPAT, kSlot, kStride + 1}), err, s));
     CK(gemm<128, 6>(hd->a_xrows, hd->m_in, R, H, H, store(hbuf, H, true, w.input_b, false), err, s));
+    const float* pending_gate = nullptr;   // gate of the sublayer whose output sits in `sub`
     for (int l = 0; l < L; ++l) {
       const float* mb = mod_k + static_cast<size_t>(l) * 6 * H;
-      CK(launch_pdl(ln_mod_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, s,
-                    static_cast<const float*>(hbuf), R, kIdentity, mb, mb + H, static_cast<int>(modw),
-                    kSlot, xm, c.ln_eps));
+      CK(ln(R, kIdentity, pending_gate ? sub : nullptr, pending_gate, mb, mb + H, kSlot, xm));
       EpiQKV eq;
       eq.q_out = bf(hd->ws.qb);
       eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
@@ -511,22 +517,22 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       ap.plane_k = eq.plane_k;
       ap.plane_v = eq.plane_v;
       CK(launch_attention(hd->pool, hd->q_att, ap, s));
-      EpiResid ea{hbuf, H, w.o_b + static_cast<size_t>(l) * H, mb + 2 * H, static_cast<int>(modw), kSlot};
-      CK(gemm<128, 6>(hd->a_ob, hd->m_o[l], R, H, H, ea, err, s));
-      CK(launch_pdl(ln_mod_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, s,
-                    static_cast<const float*>(hbuf), R, kIdentity, mb + 3 * H, mb + 4 * H,
-                    static_cast<int>(modw), kSlot, xm, c.ln_eps));
+      // attention out projection -> sub; h += gate_a * sub inside the next LN
+      CK(gemm<128, 6>(hd->a_ob, hd->m_o[l], R, H, H,
+                      store(sub, H, true, w.o_b + static_cast<size_t>(l) * H, false), err, s));
+      CK(ln(R, kIdentity, sub, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, xm));
       CK(gemm<256, 4>(hd->a_xm, hd->m_fc1[l], R, c.ffn, H,
                       store(bf(hd->ws.u), c.ffn, false, w.fc1_b + static_cast<size_t>(l) * c.ffn, true),
                       err, s));
-      EpiResid ef{hbuf, H, w.fc2_b + static_cast<size_t>(l) * H, mb + 5 * H, static_cast<int>(modw), kSlot};
-      CK(gemm<128, 6>(hd->a_u, hd->m_fc2[l], R, H, c.ffn, ef, err, s));
+      CK(gemm<128, 6>(hd->a_u, hd->m_fc2[l], R, H, c.ffn,
+                      store(sub, H, true, w.fc2_b + static_cast<size_t>(l) * H, false), err, s));
+      pending_gate = mb + 5 * H;
     }
-    // final layer on the 16 latent rows of each request, then z += dt * v
+    // final layer on the 16 latent rows of each request (after the last MLP
+    // residual), then z += dt * v
     const float* mf = mod_k + static_cast<size_t>(L) * 6 * H;
-    CK(launch_pdl(ln_mod_kernel, dim3((RL * 32 + 255) / 256), dim3(256), 0, s,
-                  static_cast<const float*>(hbuf), RL, RowMap{LPAT, kSlot, kStride + 1}, mf, mf + H,
-                  static_cast<int>(modw), LPAT, bf(hd->ws.xmf), c.ln_eps));
+    CK(ln(RL, RowMap{LPAT, kSlot, kStride + 1}, pending_gate ? sub : nullptr, pending_gate, mf, mf + H,
+          LPAT, bf(hd->ws.xmf)));
     EpiSolver es;
     es.z = f32(hd->ws.z);
     es.zb = k == NFE - 1 ? static_cast<__nv_bfloat16*>(b->out) : bf(hd->ws.zb);

@@ -6,27 +6,48 @@
 
 namespace dfm {
 
-// out[r] = LN(h[in_map(r)]) * (1 + scale[req]) + shift[req], req = r / rows_per_req,
-// LayerNorm without affine over H = 1024 (``native/dit.py:70-71,19-20``).
-// One warp per row; h is the fp32 residual stream, out the bf16 GEMM operand.
+// Residual update + adaLN LayerNorm + modulate, one warp per row:
+//   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h)
+//   out[r] = LN(x) * (1 + scale[req]) + shift[req],   req = r / rows_per_req
+// LayerNorm without affine over H = 1024 (``native/dit.py:70-71,19-20``).  The
+// residual add of the previous sublayer (``dit.py:102-107``: x + gate * f(x))
+// is applied here, on coalesced rows, instead of in that sublayer's GEMM
+// epilogue.  h is the fp32 residual stream, out the bf16 GEMM operand.
 __global__ void __launch_bounds__(256)
-    ln_mod_kernel(const float* __restrict__ h, int M, RowMap in_map, const float* __restrict__ shift,
-                  const float* __restrict__ scale, int mod_ld, int rows_per_req,
-                  __nv_bfloat16* __restrict__ out, float eps) {
+    ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub,
+                  const float* __restrict__ gate, int M, RowMap in_map,
+                  const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
+                  int rows_per_req, __nv_bfloat16* __restrict__ out, float eps) {
   constexpr int H = 1024;
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_trigger();
   pdl_wait();
   if (r >= M) return;
-  const float* hr = h + static_cast<size_t>(in_map(r)) * H;
+  const size_t hrow = static_cast<size_t>(in_map(r)) * H;
+  const size_t req = static_cast<size_t>(r / rows_per_req);
+  float* hr = h + hrow;
   float4 x[8];
   float s = 0.f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    x[j] = *reinterpret_cast<const float4*>(hr + j * 128 + lane * 4);
-    s += x[j].x + x[j].y + x[j].z + x[j].w;
+  for (int j = 0; j < 8; ++j) x[j] = *reinterpret_cast<const float4*>(hr + j * 128 + lane * 4);
+  if (sub) {
+    const float* sr = sub + hrow;
+    const float* gr = gate + req * mod_ld;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int col = j * 128 + lane * 4;
+      const float4 a = *reinterpret_cast<const float4*>(sr + col);
+      const float4 g = *reinterpret_cast<const float4*>(gr + col);
+      x[j].x += g.x * a.x;
+      x[j].y += g.y * a.y;
+      x[j].z += g.z * a.z;
+      x[j].w += g.w * a.w;
+      *reinterpret_cast<float4*>(hr + col) = x[j];
+    }
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += x[j].x + x[j].y + x[j].z + x[j].w;
   const float mean = warp_sum(s) * (1.0f / H);
   float v = 0.f;
 #pragma unroll
@@ -35,7 +56,6 @@ __global__ void __launch_bounds__(256)
     v += a * a + b * b + c * c + d * d;
   }
   const float rstd = rsqrtf(warp_sum(v) * (1.0f / H) + eps);
-  const size_t req = static_cast<size_t>(r / rows_per_req);
   const float* sh = shift + req * mod_ld;
   const float* sc = scale + req * mod_ld;
   __nv_bfloat16* o = out + static_cast<size_t>(r) * H;

@@ -1,6 +1,6 @@
 // tcgen05 GEMM for the FM head: C[M, N] = A[M, K] . W[N, K]^T with the
-// epilogue fused (bias, GELU, adaLN gate + residual, per-head LayerNorm +
-// rotary + paged K/V write, MeanFlow solver update).
+// epilogue fused (bias, GELU, per-head LayerNorm + rotary + paged K/V write,
+// MeanFlow solver update).
 //
 // Output tiles are 128 x BN.  Warp roles (192 threads):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a
@@ -81,63 +81,6 @@ struct EpiStore {
         for (int j = 0; j < 4; ++j)
           dst[j] = make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
                               pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
-      }
-    }
-  }
-};
-
-// h[row, col] += gate[req(row), col] * (acc + bias[col])   (fp32 residual stream)
-// with req(row) = row / rows_per_req and gate rows gate_ld floats apart.  The
-// loads of the next 32-column chunk are issued before the current chunk's
-// math, so the memory latency overlaps the TMEM load and the stores.
-struct EpiResid {
-  float* h;
-  int ldh;
-  const float* bias;
-  const float* gate;
-  int gate_ld;
-  int rows_per_req;
-
-  template <int BN>
-  DFM_DEV void run(uint32_t taddr, int row, int n0, int M) const {
-    const bool live = row < M;
-    const float* g = gate + static_cast<size_t>(live ? row / rows_per_req : 0) * gate_ld + n0;
-    float* hp = h + static_cast<size_t>(live ? row : 0) * ldh + n0;
-    const float* bp = bias + n0;
-    float4 hv[8], gv[8], bv[8];
-    auto load = [&](int c, float4 (&hh)[8], float4 (&gg)[8], float4 (&bb)[8]) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        hh[j] = *reinterpret_cast<const float4*>(hp + c + 4 * j);
-        gg[j] = __ldg(reinterpret_cast<const float4*>(g + c + 4 * j));
-        bb[j] = __ldg(reinterpret_cast<const float4*>(bp + c + 4 * j));
-      }
-    };
-    if (live) load(0, hv, gv, bv);
-#pragma unroll
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(taddr + c, r);
-      float4 hn[8], gn[8], bn[8];
-      if (live && c + 32 < BN) load(c + 32, hn, gn, bn);
-      tmem_wait_ld();
-      if (live) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          hv[j].x += gv[j].x * (__uint_as_float(r[4 * j]) + bv[j].x);
-          hv[j].y += gv[j].y * (__uint_as_float(r[4 * j + 1]) + bv[j].y);
-          hv[j].z += gv[j].z * (__uint_as_float(r[4 * j + 2]) + bv[j].z);
-          hv[j].w += gv[j].w * (__uint_as_float(r[4 * j + 3]) + bv[j].w);
-          *reinterpret_cast<float4*>(hp + c + 4 * j) = hv[j];
-        }
-      }
-      if (c + 32 < BN) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          hv[j] = hn[j];
-          gv[j] = gn[j];
-          bv[j] = bn[j];
-        }
       }
     }
   }
@@ -250,7 +193,7 @@ struct EpiQKV {
 
 // MeanFlow update fused into the final projection (N = latent_dim = 64):
 // z[row] += dt * (acc + bias); zb[row] = bf16(z[row]).  Loads are batched per
-// chunk as in EpiResid.
+// chunk.
 struct EpiSolver {
   float* z;
   __nv_bfloat16* zb;
