@@ -19,7 +19,9 @@
 //              against a running max per query, re-reduced across the 128 rows
 //              only on the first tile or when a score exceeds it by 2^16;
 //              probabilities written to shared memory as the bf16 A operand of
-//              the PV product; per-query sums reduced once at the end.
+//              the PV product (MN-major: each thread stores its key row's 34
+//              query values as five 16-byte chunks); per-query sums reduced
+//              once at the end.
 // S^T and P are double-buffered, so QK^T of tile t+1 and PV of tile t-1 overlap
 // the softmax of tile t.  Units are launched longest request first.  A request
 // split over several chunks writes (O, m, l) partials; the last chunk CTA of a
@@ -37,14 +39,14 @@ constexpr int TA_ROWS = 34;             // query rows per request
 constexpr int TA_CH = 4096;             // most keys one work unit takes (longer requests split)
 constexpr int TA_THREADS = 192;
 constexpr int TA_KV_BYTES = TA_KT * 128;           // 16 KB: 128 keys x 64 dims
-constexpr int TA_Q_BYTES = 8192;                   // 48 rows x 128 B, padded
-// P (the bf16 A operand of O = P V) holds 48 query rows x 128 keys per buffer,
-// as two k-blocks of 6 row groups (8 rows x 128 B).  The M=128 product also
-// reads row groups 6..15 of each k-block, which fall on whatever shared memory
-// follows; they only feed output rows 48..127, which are never read.
-constexpr int TA_P_BLOCK = 6 * 1024;
-constexpr int TA_P_BUF = 2 * TA_P_BLOCK;
-constexpr int TA_OFF_P = 0;                        // first: its over-read lands on K
+constexpr int TA_Q_BYTES = TA_QN * 128;           // 48 rows x 128 B
+// P (the bf16 A operand of O = P V) is stored MN-major: key k of the tile is
+// the 128-byte row k of one 64-query swizzle atom (queries 0..33 used, 34..39
+// zero).  The M=128 product reads a second 64-query atom TA_P_BUF bytes further
+// on (the other P buffer, or the K ring after buffer 1): finite data that only
+// feeds output rows 64..127, which are never read.
+constexpr int TA_P_BUF = TA_KT * 128;              // 16 KB
+constexpr int TA_OFF_P = 0;
 constexpr int TA_OFF_K = TA_OFF_P + 2 * TA_P_BUF;
 constexpr int TA_OFF_V = TA_OFF_K + 2 * TA_KV_BYTES;
 constexpr int TA_OFF_Q = TA_OFF_V + 2 * TA_KV_BYTES;
@@ -54,6 +56,7 @@ constexpr int TA_SMEM = TA_OFF_MISC + TA_MISC_BYTES + 1024;
 constexpr uint32_t TA_TMEM_COLS = 256;             // S^T buffers at 0 and 64, O at 128
 constexpr uint32_t TA_O_COL = 128;
 constexpr float TA_TAU = 16.0f;                    // lazy-rescale threshold, log2 units
+constexpr float TA_M0 = 0.0f;                      // running-max start value (log2 units)
 constexpr int TA_MAX_PAGES = (TA_CH / TA_KT + 1) * (TA_KT / 16);  // pages of one unit
 constexpr int TA_MAX_ORDER = 256;                  // requests ordered longest-first
 
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, TA_QN);
-      constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(128, 64);
+      constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(128, 64) | (1u << 15);  // A MN-major too
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t p_addr = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err);
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
           const uint32_t pb = p_addr + (t2 & 1) * TA_P_BUF;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem + TA_O_COL, umma_desc_sw128(pb + (kk >> 2) * TA_P_BLOCK + (kk & 3) * 32),
+            umma_bf16(tmem + TA_O_COL, umma_desc_sw128_mn(pb + kk * 2048, TA_P_BUF),
                       umma_desc_sw128(v_addr + kk * 2048), idesc_o, (t2 > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&v_empty[t2 & 1]);
           umma_commit(&p_empty[t2 & 1]);
@@ -341,8 +344,13 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
     const int row = q4 * 32 + lane;     // key row of the tile
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     const float cexp = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+    // Running max per query in log2 units (score * cexp).  It starts at 0 so
+    // that the first tile's x = score * cexp - max is exact; the first tile
+    // always takes the update path, which replaces it with the tile's max.  A
+    // query whose keys are all masked keeps max = -inf (its unmasked keys form
+    // a prefix, so every later key is masked too) and x = -inf.
     if (sw == 0)
-      for (int j = lane; j < TA_ROWS; j += 32) m_s[j] = -INFINITY;
+      for (int j = lane; j < TA_ROWS; j += 32) m_s[j] = TA_M0;
     int ver = 0;   // m_s[ver & 1] holds the running max (one writer per update)
     float l[TA_ROWS];
 #pragma unroll
@@ -357,23 +365,27 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
     };
     // the first tile's reduction reads m_s: make the initialisation visible
     bool ok = team_sync();
-    const uint32_t pcol = smem_u32(sP) + (row >> 6) * TA_P_BLOCK + (row & 7) * 2;
-    const int pch = (row & 63) >> 3;
+    const uint32_t prow = smem_u32(sP) + row * 128;   // this key's row of the P atom
+    const int psw = row & 7;
 #pragma unroll 1
     for (int t = 0; ok && t < ntiles; ++t) {
       const int sb = t & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (t >> 1) & 1, abort_flag, p.err));
       if (!ok) break;
       tc_fence_after();
-      uint32_t r32[32], r16[16];
-      tmem_ld32(tmem + sb * 64 + lane_off, r32);
-      tmem_ld16(tmem + sb * 64 + 32 + lane_off, r16);
-      tmem_wait_ld();
-      float s[TA_ROWS];
+      // x[j] = score * cexp - max_j   (log2 units, relative to the running max)
+      float x[TA_ROWS];
+      {
+        uint32_t r32[32], r16[16];
+        tmem_ld32(tmem + sb * 64 + lane_off, r32);
+        tmem_ld16(tmem + sb * 64 + 32 + lane_off, r16);
+        const float* mc = m_s + (ver & 1) * TA_ROWS;
+        tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r32[j]);
-      s[32] = __uint_as_float(r16[0]);
-      s[33] = __uint_as_float(r16[1]);
+        for (int j = 0; j < 32; ++j) x[j] = fmaf(__uint_as_float(r32[j]), cexp, -mc[j]);
+        x[32] = fmaf(__uint_as_float(r16[0]), cexp, -mc[32]);
+        x[33] = fmaf(__uint_as_float(r16[1]), cexp, -mc[33]);
+      }
       if (k0 + t * TA_KT + TA_KT > P) {   // only tiles reaching past the cached prefix
         // key k is hidden from graduating rows j with P + j < k, and from all
         // rows beyond the request's keys
@@ -382,15 +394,11 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
         const int jmask = key >= total ? TA_ROWS : (d <= 0 ? 0 : (d < ne ? d : ne));
 #pragma unroll
         for (int j = 0; j < TA_ROWS; ++j)
-          if (j < jmask) s[j] = -INFINITY;
+          if (j < jmask) x[j] = -INFINITY;
       }
-      const float* mc = m_s + (ver & 1) * TA_ROWS;
-      float mreg[TA_ROWS];
-#pragma unroll
-      for (int j = 0; j < TA_ROWS; ++j) mreg[j] = mc[j];
       bool over = (t == 0);
 #pragma unroll
-      for (int j = 0; j < TA_ROWS; ++j) over |= (s[j] - mreg[j]) * cexp > TA_TAU;
+      for (int j = 0; j < TA_ROWS; ++j) over |= x[j] > TA_TAU;
       const bool any = __any_sync(0xffffffffu, over);
       if (lane == 0) flags[(t & 1) * 4 + sw] = any ? 1 : 0;
       // Releasing the S buffer doubles as the per-tile agreement of the four
@@ -410,8 +418,13 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
         tc_fence_after();
       }
       if (need) {
+        // new running max: the old one raised by this tile's scores (x + max_old)
+        const float* mc = m_s + (ver & 1) * TA_ROWS;
+        float y[TA_ROWS];
+#pragma unroll
+        for (int j = 0; j < TA_ROWS; ++j) y[j] = x[j] + mc[j];
         float* rb = red + (t & 1) * 4 * TA_ROWS;
-        warp_reduce34<true>(s, rb, sw, lane);
+        warp_reduce34<true>(y, rb, sw, lane);
         ok = team_sync();
         if (!ok) break;
         if (sw == 0) {
@@ -420,18 +433,18 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
             const float mt = fmaxf(fmaxf(rb[j], rb[TA_ROWS + j]),
                                    fmaxf(rb[2 * TA_ROWS + j], rb[3 * TA_ROWS + j]));
             const float mo = mc[j];
-            const float mn = fmaxf(mo, mt);
+            const float mn = t == 0 ? mt : fmaxf(mo, mt);
             mn_s[j] = mn;
-            vals[j] = mn == -INFINITY ? 1.f : (mo == -INFINITY ? 0.f : fast_exp2((mo - mn) * cexp));
+            vals[j] = (t == 0 || mn == -INFINITY) ? 1.f : fast_exp2(mo - mn);
           }
         }
         ok = team_sync();
         if (!ok) break;
         ++ver;
-        mc = m_s + (ver & 1) * TA_ROWS;
+        const float* mn = m_s + (ver & 1) * TA_ROWS;
 #pragma unroll
         for (int j = 0; j < TA_ROWS; ++j) {
-          mreg[j] = mc[j];
+          x[j] = mn[j] == -INFINITY ? -INFINITY : x[j] + (mc[j] - mn[j]);
           l[j] *= vals[j];
         }
         if (t >= 1) {
@@ -457,20 +470,22 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
           }
         }
       }
-      // probabilities into column `row` of P buffer t&1, row sums
-      float e[TA_ROWS];
+      // probabilities: this key's row of P buffer t&1 (queries 0..39), row sums
+      float e[40];
 #pragma unroll
       for (int j = 0; j < TA_ROWS; ++j) {
-        e[j] = mreg[j] == -INFINITY ? 0.f : fast_exp2(fmaf(s[j], cexp, -mreg[j] * cexp));
+        e[j] = fast_exp2(x[j]);
         l[j] += e[j];
       }
-      const uint32_t pbase = pcol + (t & 1) * TA_P_BUF;
 #pragma unroll
-      for (int j = 0; j < TA_ROWS; ++j) {
-        const __nv_bfloat16 v = __float2bfloat16(e[j]);
-        asm volatile("st.shared.b16 [%0], %1;" ::"r"(pbase + j * 128 + ((pch ^ (j & 7)) << 4)),
-                     "h"(*reinterpret_cast<const unsigned short*>(&v)));
-      }
+      for (int j = TA_ROWS; j < 40; ++j) e[j] = 0.f;
+      const uint32_t pbase = prow + (t & 1) * TA_P_BUF;
+#pragma unroll
+      for (int c = 0; c < 5; ++c)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(pbase + ((c ^ psw) << 4)),
+                     "r"(pack_bf16(e[8 * c], e[8 * c + 1])), "r"(pack_bf16(e[8 * c + 2], e[8 * c + 3])),
+                     "r"(pack_bf16(e[8 * c + 4], e[8 * c + 5])), "r"(pack_bf16(e[8 * c + 6], e[8 * c + 7]))
+                     : "memory");
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -489,7 +504,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
       const float* mcur = m_s + (ver & 1) * TA_ROWS;
       for (int j = lane; j < TA_ROWS; j += 32) {
         vals[j] = rs[j] + rs[TA_ROWS + j] + rs[2 * TA_ROWS + j] + rs[3 * TA_ROWS + j];
-        mfin[j] = mcur[j] == -INFINITY ? -INFINITY : mcur[j] * cexp;
+        mfin[j] = mcur[j];
       }
     }
     if (ok) ok = team_sync();

@@ -189,6 +189,112 @@ DFM_DEV uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Descriptor of an MN-major operand stored with the 128-byte swizzle: rows are
+// K indices of 128 bytes (64 bf16 along M or N), 8-row groups 1024 bytes
+// apart along K, and consecutive 64-element atoms along M/N `atom_bytes` apart.
+DFM_DEV uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t atom_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>((atom_bytes >> 4) & 0x3FFFu) << 16;  // leading byte offset: next atom
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;              // stride byte offset: 8 K rows
+  d |= static_cast<uint64_t>(1) << 46;                      // descriptor version (sm100)
+  d |= static_cast<uint64_t>(2) << 61;                      // layout: 128-byte swizzle
+  return d;
+}
+
+// ---------------------------------------------------------------- CTA pairs
+// A cluster of two CTAs on neighbouring SMs issues one tcgen05.mma with
+// cta_group::2: M = 256 rows, A rows [0,128) from CTA 0's shared memory and
+// [128,256) from CTA 1's at the same offset, B split along N the same way, and
+// each CTA's TMEM holding its own 128 rows of D.  Every tcgen05 instruction of
+// such a kernel uses cta_group::2.
+DFM_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the variable at `smem_addr` in CTA `rank` of the cluster.
+DFM_DEV uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+// All threads of all CTAs of the cluster.
+DFM_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+DFM_DEV void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr)
+               : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion (bytes) is counted
+// on an mbarrier of either CTA of the pair (shared::cluster address).
+DFM_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int x,
+                              int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
+// TMA store of a shared-memory box to a 3-D tensor (bulk-group completion).
+DFM_DEV void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+DFM_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+DFM_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until every committed bulk group of this thread has completed.
+DFM_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+DFM_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {  // whole warp, both CTAs
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols));
+}
+DFM_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+DFM_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+// One pair MMA (issued by one thread of CTA 0): D(tmem, both CTAs) (+)= A . B^T.
+DFM_DEV void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                            uint32_t accumulate) {
+  const uint32_t z = 0;  // no disabled output lanes
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z),
+      "r"(z), "r"(z), "r"(z));
+}
+
+// Arrive on the mbarrier at `bar_cluster_addr` (either CTA of the pair) once
+// every pair MMA this thread issued so far is done.
+DFM_DEV void umma_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          bar_cluster_addr)
+      : "memory");
+}
+
 // The same descriptor fields describe an MN-major operand whose N extent is one
 // 64-element swizzle atom (rows = K index, 128 bytes of N each, 8-row groups
 // 1024 bytes apart): the stride byte offset is then the K-group stride.

@@ -22,6 +22,11 @@ namespace {
 constexpr int kH = 1024;
 constexpr int kStride = 17;      // hidden_patch + latent_patch
 constexpr int kSlot = 2 * kStride;  // graduating + active rows per request
+// Tile widths of the per-layer CTA-pair GEMMs (output tiles 256 x BN).
+constexpr int kQkvBN = 256, kQkvST = 6;
+constexpr int kFc1BN = 256, kFc1ST = 6;
+constexpr int kOutBN = 256, kOutST = 6;  // O-projection and fc2 (N = hidden) ...
+constexpr int kOutSplit = 2;             // ... as two split-K partial sums (72 units at n = 64)
 
 // ---------------------------------------------------------------- TMA encoding
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -127,6 +132,65 @@ cudaError_t gemm(const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K
   return launch_pdl(fn, dim3(grid), dim3(GEMM_THREADS), smem, s, a, b, M, N, K, e, err);
 }
 
+// CTA-pair GEMM (256 x BN output tiles on two SMs).  The grid is the number
+// of work units or the number of pairs that fit on the device at once,
+// whichever is smaller, so the kernel stays persistent.  W's tensor map must
+// have box rows BN / 2; `c` is the output map of staged epilogues (ignored by
+// the others); ksplit > 1 splits K into that many partial sums.
+template <int BN, int ST, class Epi>
+cudaError_t gemm2(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, int M, int N,
+                  int K, int ksplit, const Epi& e, uint32_t* err, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  if (ksplit < 1 || (K / GEMM_BK) % ksplit) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr_done{0};
+  static std::atomic<int> pairs_cache[64];
+  auto fn = gemm2_bf16_tn<BN, ST, Epi>;
+  constexpr int smem = Gemm2Shape<BN, ST, Epi::kStageBytes>::SMEM;
+  cudaError_t r = smem_attr_once(attr_done, fn, smem);
+  if (r != cudaSuccess) return r;
+  int dev = 0;
+  if ((r = cudaGetDevice(&dev)) != cudaSuccess) return r;
+  int pairs = pairs_cache[dev & 63].load(std::memory_order_relaxed);
+  if (pairs <= 0) {
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(2 * (sm_count() / 2));
+    q.blockDim = dim3(GEMM_THREADS);
+    q.dynamicSmemBytes = smem;
+    int nc = 0;
+    r = cudaOccupancyMaxActiveClusters(&nc, fn, &q);
+    if (r != cudaSuccess) return r;
+    pairs = nc > 0 ? nc : 1;
+    pairs_cache[dev & 63].store(pairs, std::memory_order_relaxed);
+  }
+  const int units = ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * (N / BN) * ksplit;
+  const int grid = 2 * (units < pairs ? units : pairs);
+  return launch_pdl(fn, dim3(grid), dim3(GEMM_THREADS), smem, s, a, b, c, M, N, K, ksplit, e, err);
+}
+
+// Output map of the staged (TMA-store) epilogue: {cols, rows, planes} of fp32
+// or bf16 with plane stride `plane_bytes`, box {128 bytes of columns, 32, 1}.
+bool map_out(CUtensorMap* m, void* base, bool f32, uint64_t rows, uint64_t cols, uint64_t planes,
+             uint64_t plane_bytes) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  const uint64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[3] = {cols, rows, planes};
+  cuuint64_t strides[2] = {cols * es, plane_bytes};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), 32, 1};
+  cuuint32_t el[3] = {1, 1, 1};
+  return fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base,
+            dims, strides, box, el, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool F32>
+EpiStoreT<F32> store_t(const float* bias, bool gelu) {
+  EpiStoreT<F32> e;
+  e.bias = bias;
+  e.gelu = gelu ? 1 : 0;
+  return e;
+}
+
 constexpr RowMap kIdentity{1 << 30, 0, 0};
 
 EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMap m = kIdentity) {
@@ -178,6 +242,7 @@ struct Handle {
   const void* plan_ws = nullptr;
   const void* plan_pool = nullptr;
   CUtensorMap a_csilu, a_xrows, a_xm, a_ob, a_u, a_zb, a_xmf, a_act, a_exth, a_extl, pool, q_att;
+  CUtensorMap o_sub, o_u;  // staged-epilogue outputs: fp32 sub planes, bf16 MLP hidden
 };
 
 WsLayout layout_for(const DfmConfig& c, int mc) {
@@ -196,7 +261,7 @@ WsLayout layout_for(const DfmConfig& c, int mc) {
   L.emb1 = take(2ull * c.nfe * H * 4);
   L.xrows = take(R * H * 2);
   L.h = take(R * H * 4);
-  L.sub = take(R * H * 4);
+  L.sub = take(2 * R * H * 4);   // two split-K partial planes
   L.xm = take(R * H * 2);
   L.qb = take(R * H * 2);
   L.ob = take(R * H * 2);
@@ -244,6 +309,8 @@ bool ensure_plan(Handle* h, void* ws, void* pool, cudaStream_t s) {
             map_2d(&h->a_exth, b + h->ws.st_exth, NR, c.cond_dim, c.cond_dim, 128) &&
             map_2d(&h->a_extl, b + h->ws.st_extl, LP, c.latent_dim, c.latent_dim, 128) &&
             map_q(&h->q_att, b + h->ws.qb, R, c.heads) &&
+            map_out(&h->o_sub, b + h->ws.sub, true, R, H, 2, R * H * 4) &&
+            map_out(&h->o_u, b + h->ws.u, false, R, c.ffn, 1, R * c.ffn * 2) &&
             map_pool(&h->pool, pool, c.num_pages, c.heads, c.layers * c.nfe * 2);
   if (!ok) {
     h->plan_ws = h->plan_pool = nullptr;
@@ -332,10 +399,14 @@ int dfm_create(const DfmConfig* cfg, const DfmWeights* w, void** out) {
             map_2d(&h->m_hid, w->hidden_w, H, c.cond_dim, c.cond_dim, 128) &&
             map_2d(&h->m_lat, w->latent_w, H, c.latent_dim, c.latent_dim, 128);
   for (int l = 0; ok && l < L; ++l) {
-    ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * 3 * H * H, 3 * H, H, H, 256) &&
-         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * H * H, H, H, H, 128) &&
-         map_2d(&h->m_fc1[l], bw(w->fc1_w) + static_cast<size_t>(l) * c.ffn * H, c.ffn, H, H, 256) &&
-         map_2d(&h->m_fc2[l], bw(w->fc2_w) + static_cast<size_t>(l) * H * c.ffn, H, c.ffn, c.ffn, 128);
+    // per-layer weights feed the CTA-pair GEMM: box rows = half the tile's N
+    ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * 3 * H * H, 3 * H, H, H,
+                kQkvBN / 2) &&
+         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * H * H, H, H, H, kOutBN / 2) &&
+         map_2d(&h->m_fc1[l], bw(w->fc1_w) + static_cast<size_t>(l) * c.ffn * H, c.ffn, H, H,
+                kFc1BN / 2) &&
+         map_2d(&h->m_fc2[l], bw(w->fc2_w) + static_cast<size_t>(l) * H * c.ffn, H, c.ffn, c.ffn,
+                kOutBN / 2);
   }
   if (!ok) {
     dfm_destroy(h);
@@ -478,10 +549,13 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   float* hbuf = f32(hd->ws.h);
   float* sub = f32(hd->ws.sub);   // the last sublayer's output, added to h by the next LN
   __nv_bfloat16* xm = bf(hd->ws.xm);
+  // the second split-K partial of `sub` (O-projection and fc2 outputs)
+  const size_t sub_plane = kOutSplit > 1 ? static_cast<size_t>(kSlot) * c.max_requests * H : 0;
   auto ln = [&](int M, RowMap map, const float* subp, const float* gate, const float* shift,
                 const float* scale, int rows_per_req, __nv_bfloat16* out) {
-    return launch_pdl(ln_mod_kernel, dim3((M * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp, gate,
-                      M, map, shift, scale, static_cast<int>(modw), rows_per_req, out, c.ln_eps);
+    return launch_pdl(ln_mod_kernel, dim3((M * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp,
+                      subp ? sub_plane : size_t{0}, gate, M, map, shift, scale,
+                      static_cast<int>(modw), rows_per_req, out, c.ln_eps);
   };
   for (int k = 0; k < NFE; ++k) {
     const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;
@@ -513,19 +587,19 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       eq.max_pos = c.max_pages_per_req * 16;
       eq.eps = c.ln_eps;
       eq.err = err;
-      CK(gemm<256, 4>(hd->a_xm, hd->m_qkv[l], R, 3 * H, H, eq, err, s));
+      CK(gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s));
       ap.plane_k = eq.plane_k;
       ap.plane_v = eq.plane_v;
       CK(launch_attention(hd->pool, hd->q_att, ap, s));
       // attention out projection -> sub; h += gate_a * sub inside the next LN
-      CK(gemm<128, 6>(hd->a_ob, hd->m_o[l], R, H, H,
-                      store(sub, H, true, w.o_b + static_cast<size_t>(l) * H, false), err, s));
+      CK(gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, kOutSplit,
+                               store_t<true>(w.o_b + static_cast<size_t>(l) * H, false), err, s));
       CK(ln(R, kIdentity, sub, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, xm));
-      CK(gemm<256, 4>(hd->a_xm, hd->m_fc1[l], R, c.ffn, H,
-                      store(bf(hd->ws.u), c.ffn, false, w.fc1_b + static_cast<size_t>(l) * c.ffn, true),
-                      err, s));
-      CK(gemm<128, 6>(hd->a_u, hd->m_fc2[l], R, H, c.ffn,
-                      store(sub, H, true, w.fc2_b + static_cast<size_t>(l) * H, false), err, s));
+      CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1,
+                               store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, true), err,
+                               s));
+      CK(gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, H, c.ffn, kOutSplit,
+                               store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, false), err, s));
       pending_gate = mb + 5 * H;
     }
     // final layer on the 16 latent rows of each request (after the last MLP
@@ -550,15 +624,33 @@ int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* Wt,
   if (lda < K || ldw < K || (lda * 2) % 16 || (ldw * 2) % 16) return DFM_ERR_INVALID_ARG;
   if (out_f32 && N % 4) return DFM_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap ma, mw;
-  const int bn = N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 64);
-  if (!map_2d(&ma, A, M, K, lda, 128) || !map_2d(&mw, Wt, N, K, ldw, bn)) return DFM_ERR_CUDA;
+  CUtensorMap ma, mw, mo;
+  int bn = N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 64);
+  // CTA pairs (256-row tiles) once there is more than one 128-row tile of A;
+  // 128-wide tiles when 256-wide ones would leave most SM pairs idle
+  const bool pair = M > GEMM_BM && bn >= 128;
+  const int tiles_m2 = (M + 2 * GEMM_BM - 1) / (2 * GEMM_BM);
+  if (pair && bn == 256 && tiles_m2 * (N / 256) < 64) bn = 128;
+  if (!map_2d(&ma, A, M, K, lda, 128) || !map_2d(&mw, Wt, N, K, ldw, pair ? bn / 2 : bn))
+    return DFM_ERR_CUDA;
+  if (pair && !map_out(&mo, out, out_f32 != 0, M, N, 1, static_cast<uint64_t>(M) * N * 4))
+    return DFM_ERR_CUDA;
   EpiStore e = store(out, N, out_f32 != 0, bias, gelu != 0);
-  if (bias == nullptr) e.bias = nullptr;
   cudaError_t r;
-  if (bn == 256) r = gemm<256, 4>(ma, mw, M, N, K, e, nullptr, s);
-  else if (bn == 128) r = gemm<128, 6>(ma, mw, M, N, K, e, nullptr, s);
-  else r = gemm<64, 8>(ma, mw, M, N, K, e, nullptr, s);
+  if (pair && bn == 256 && out_f32)
+    r = gemm2<256, 6>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
+  else if (pair && bn == 256)
+    r = gemm2<256, 6>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
+  else if (pair && out_f32)
+    r = gemm2<128, 8>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
+  else if (pair)
+    r = gemm2<128, 8>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
+  else if (bn == 256)
+    r = gemm<256, 4>(ma, mw, M, N, K, e, nullptr, s);
+  else if (bn == 128)
+    r = gemm<128, 6>(ma, mw, M, N, K, e, nullptr, s);
+  else
+    r = gemm<64, 8>(ma, mw, M, N, K, e, nullptr, s);
   return r == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
 

@@ -7,14 +7,15 @@
 namespace dfm {
 
 // Residual update + adaLN LayerNorm + modulate, one warp per row:
-//   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h)
+//   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h; with
+//   sub_plane != 0, sub is the sum of two split-K partials sub[.] + sub[. + sub_plane])
 //   out[r] = LN(x) * (1 + scale[req]) + shift[req],   req = r / rows_per_req
 // LayerNorm without affine over H = 1024 (``native/dit.py:70-71,19-20``).  The
 // residual add of the previous sublayer (``dit.py:102-107``: x + gate * f(x))
 // is applied here, on coalesced rows, instead of in that sublayer's GEMM
 // epilogue.  h is the fp32 residual stream, out the bf16 GEMM operand.
 __global__ void __launch_bounds__(256)
-    ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub,
+    ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub, size_t sub_plane,
                   const float* __restrict__ gate, int M, RowMap in_map,
                   const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
                   int rows_per_req, __nv_bfloat16* __restrict__ out, float eps) {
@@ -37,7 +38,11 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int col = j * 128 + lane * 4;
-      const float4 a = *reinterpret_cast<const float4*>(sr + col);
+      float4 a = *reinterpret_cast<const float4*>(sr + col);
+      if (sub_plane) {  // split-K: the second partial sum
+        const float4 a2 = *reinterpret_cast<const float4*>(sr + sub_plane + col);
+        a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
+      }
       const float4 g = *reinterpret_cast<const float4*>(gr + col);
       x[j].x += g.x * a.x;
       x[j].y += g.y * a.y;
@@ -176,10 +181,14 @@ __global__ void __launch_bounds__(256)
 // of ``layers.py:95-134`` for every cache position, computed once per workspace.
 __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int max_pos,
                                   float2* __restrict__ tab) {
+  // tab[d][pos]: consecutive positions are adjacent, so the 32 rows of an
+  // epilogue warp (consecutive positions of one or two requests) read one
+  // frequency's (cos, sin) in one or two 256-byte segments.
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= max_pos * 32) return;
+  const int d = idx / max_pos, pos = idx - d * max_pos;
   float sn, co;
-  sincosf(static_cast<float>(idx >> 5) * inv_freq[idx & 31], &sn, &co);
+  sincosf(static_cast<float>(pos) * inv_freq[d], &sn, &co);
   tab[idx] = make_float2(co, sn);
 }
 
