@@ -206,18 +206,24 @@ EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMa
 
 int attn_chunks(int max_pages) { return (max_pages * 16 + kSlot + TA_CH - 1) / TA_CH; }
 
+// The attention kernel is persistent: two CTAs per SM (its register bound
+// and shared-memory budget are sized for that), or one per work unit if there
+// are fewer units.
 cudaError_t launch_attention(const CUtensorMap& pool_map, const CUtensorMap& q_map,
                              const AttnParams& p, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
   cudaError_t r = smem_attr_once(attr_done, attn_tc_kernel, TA_SMEM);
   if (r != cudaSuccess) return r;
-  return launch_pdl(attn_tc_kernel, dim3(p.n * p.MC * p.heads), dim3(TA_THREADS), TA_SMEM, s,
+  const int ctas = TA_CTAS_PER_SM * sm_count();
+  const int units = p.n * p.MC * p.heads;
+  return launch_pdl(attn_tc_kernel, dim3(units < ctas ? units : ctas), dim3(TA_THREADS), TA_SMEM, s,
                     pool_map, q_map, p);
 }
 
-// Query rows of the 34-row request layout as TMA boxes of 48 rows x 64 dims.
+// Query rows of the 34-row request layout as TMA boxes of 40 rows x 64 dims.
 bool map_q(CUtensorMap* m, const void* q, uint64_t rows, int heads) {
-  return map_2d(m, q, rows, static_cast<uint64_t>(heads) * 64, static_cast<uint64_t>(heads) * 64, TA_QN);
+  return map_2d(m, q, rows, static_cast<uint64_t>(heads) * 64, static_cast<uint64_t>(heads) * 64,
+                TA_QROWS);
 }
 
 // ---------------------------------------------------------------- handle
