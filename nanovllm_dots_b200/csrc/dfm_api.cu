@@ -24,8 +24,8 @@ constexpr int kStride = 17;      // hidden_patch + latent_patch
 constexpr int kSlot = 2 * kStride;  // graduating + active rows per request
 // Tile widths of the per-layer CTA-pair GEMMs (output tiles 256 x BN).
 constexpr int kQkvBN = 256, kQkvST = 6;
-constexpr int kFc1BN = 256, kFc1ST = 6;
-constexpr int kOutBN = 256, kOutST = 6;  // O-projection and fc2 (N = hidden) ...
+constexpr int kFc1BN = 256, kFc1ST = 5;
+constexpr int kOutBN = 256, kOutST = 5;  // O-projection and fc2 (N = hidden) ...
 constexpr int kOutSplit = 2;             // ... as two split-K partial sums (72 units at n = 64)
 
 // ---------------------------------------------------------------- TMA encoding
@@ -145,7 +145,7 @@ cudaError_t gemm2(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   static std::atomic<uint64_t> attr_done{0};
   static std::atomic<int> pairs_cache[64];
   auto fn = gemm2_bf16_tn<BN, ST, Epi>;
-  constexpr int smem = Gemm2Shape<BN, ST, Epi::kStageBytes>::SMEM;
+  constexpr int smem = Gemm2Shape<BN, ST, Epi::kStageBytes, Epi::kEpiWarps>::SMEM;
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
   int dev = 0;
@@ -154,7 +154,7 @@ cudaError_t gemm2(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   if (pairs <= 0) {
     cudaLaunchConfig_t q = {};
     q.gridDim = dim3(2 * (sm_count() / 2));
-    q.blockDim = dim3(GEMM_THREADS);
+    q.blockDim = dim3(gemm2_threads<Epi>());
     q.dynamicSmemBytes = smem;
     int nc = 0;
     r = cudaOccupancyMaxActiveClusters(&nc, fn, &q);
@@ -164,7 +164,8 @@ cudaError_t gemm2(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   }
   const int units = ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * (N / BN) * ksplit;
   const int grid = 2 * (units < pairs ? units : pairs);
-  return launch_pdl(fn, dim3(grid), dim3(GEMM_THREADS), smem, s, a, b, c, M, N, K, ksplit, e, err);
+  return launch_pdl(fn, dim3(grid), dim3(gemm2_threads<Epi>()), smem, s, a, b, c, M, N, K, ksplit,
+                    e, err);
 }
 
 // Output map of the staged (TMA-store) epilogue: {cols, rows, planes} of fp32
@@ -644,13 +645,13 @@ int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* Wt,
   EpiStore e = store(out, N, out_f32 != 0, bias, gelu != 0);
   cudaError_t r;
   if (pair && bn == 256 && out_f32)
-    r = gemm2<256, 6>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
+    r = gemm2<256, 5>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
   else if (pair && bn == 256)
-    r = gemm2<256, 6>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
+    r = gemm2<256, 5>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
   else if (pair && out_f32)
-    r = gemm2<128, 8>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
+    r = gemm2<128, 6>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
   else if (pair)
-    r = gemm2<128, 8>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
+    r = gemm2<128, 6>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
   else if (bn == 256)
     r = gemm<256, 4>(ma, mw, M, N, K, e, nullptr, s);
   else if (bn == 128)

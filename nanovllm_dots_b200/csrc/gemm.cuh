@@ -23,6 +23,11 @@ namespace dfm {
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;  // one 128-byte swizzle row of bf16
 constexpr int GEMM_THREADS = 192;
+// CTA-pair kernel: TMA warp, MMA warp, and Epi::kEpiWarps epilogue warps (4:
+// one per TMEM lane quadrant; 8: two per quadrant, each taking half of the
+// tile's columns).
+template <class Epi>
+constexpr int gemm2_threads() { return 64 + 32 * Epi::kEpiWarps; }
 
 template <int BN, int STAGES>
 struct GemmShape {
@@ -42,6 +47,7 @@ struct GemmShape {
 // out[omap(row), col] = act(acc + bias[col]) in bf16 or fp32.
 struct EpiStore {
   static constexpr int kStageBytes = 0;
+  static constexpr int kEpiWarps = 4;
   void* out;
   int ldo;
   int out_f32;
@@ -96,6 +102,7 @@ struct EpiStore {
 template <bool F32>
 struct EpiStoreT {
   static constexpr int kStageBytes = 8192;  // per epilogue warp: two 4 KB boxes
+  static constexpr int kEpiWarps = 8;
   static constexpr int CW = F32 ? 32 : 64;  // columns per 128-byte line
   const float* bias;
   int gelu;
@@ -187,6 +194,7 @@ struct EpiStoreT {
 // 16-byte pieces.
 struct EpiQKV {
   static constexpr int kStageBytes = 4096;  // per epilogue warp: 32 rows x 128 bytes
+  static constexpr int kEpiWarps = 4;       // the row state needs the registers
   __nv_bfloat16* q_out;
   __nv_bfloat16* pool;
   size_t plane_elems;  // elements of one (layer, step, K|V) plane: pages*heads*16*dh
@@ -329,6 +337,7 @@ struct EpiQKV {
 // chunk.
 struct EpiSolver {
   static constexpr int kStageBytes = 0;
+  static constexpr int kEpiWarps = 4;
   float* z;
   __nv_bfloat16* zb;
   const float* bias;
@@ -524,14 +533,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 //   - TMA bytes of both CTAs count on CTA 0's full[s] (CTA 0 expects both);
 //   - CTA 0's MMA commits to empty[s] and tm_full[b] of both CTAs;
 //   - the epilogue warps of both CTAs arrive on CTA 0's tm_empty[b].
-template <int BN, int STAGES, int EPI_STAGE = 0>
+template <int BN, int STAGES, int EPI_STAGE = 0, int EPI_WARPS = 4>
 struct Gemm2Shape {
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair MMA N");
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;     // this CTA's 128 rows of A
   static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;    // this CTA's half of the W tile
   static_assert(B_BYTES % 1024 == 0, "swizzle atoms");
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int EPI_BYTES = 4 * EPI_STAGE;           // staging boxes of the 4 epilogue warps
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_STAGE;  // staging boxes of the epilogue warps
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   static_assert(SMEM <= 232448, "shared memory per CTA");
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
@@ -541,11 +550,12 @@ struct Gemm2Shape {
 // k-blocks [s * nk / ksplit, (s + 1) * nk / ksplit) with s = t / tiles; the
 // epilogue gets s (split-K partial sums go to separate output planes).
 template <int BN, int STAGES, class Epi>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads<Epi>(), 1)
     gemm2_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int ksplit, Epi epi,
                   uint32_t* err) {
-  using S = Gemm2Shape<BN, STAGES, Epi::kStageBytes>;
+  using S = Gemm2Shape<BN, STAGES, Epi::kStageBytes, Epi::kEpiWarps>;
+  static_assert(Epi::kEpiWarps == 4 || Epi::kEpiWarps == 8, "epilogue warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -575,7 +585,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tm_full[b], 1);
-      mbar_init(&tm_empty[b], 8);
+      mbar_init(&tm_empty[b], 2 * Epi::kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -670,30 +680,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     pdl_wait();
-    const int q = warp & 3;
+    const int q = warp & 3;               // TMEM lane quadrant (rows 32q .. 32q + 31)
+    const int half = (warp - 2) >> 2;     // which part of the tile's columns
+    constexpr int HB = BN * 4 / Epi::kEpiWarps;
     int u = 0;
 #pragma unroll 1
     for (int t = pair; t < total; t += npairs, ++u) {
       const int b = u & 1;
       const int tile = t % tiles;
       const int row0 = (tile % tiles_m) * 2 * GEMM_BM + static_cast<int>(rank) * GEMM_BM + q * 32;
-      const int n0 = (tile / tiles_m) * BN;
-      const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16);
+      const int n0 = (tile / tiles_m) * BN + half * HB;
+      const uint32_t taddr = tmem + b * BN + half * HB + (static_cast<uint32_t>(q * 32) << 16);
       if constexpr (Epi::kStageBytes > 0) {
         // row-only state first: its loads overlap the wait for the accumulator
-        const auto st = epi.template row_state<BN>(row0, lane, n0, M);
+        const auto st = epi.template row_state<HB>(row0, lane, n0, M);
         const bool ready =
             __all_sync(0xffffffffu, mbar_wait(&tm_full[b], (u >> 1) & 1, abort_flag, err));
         if (!ready) break;
         tc_fence_after();
-        epi.template run_staged<BN>(st, taddr, row0, lane, n0, M, t / tiles,
-                                    sE + q * Epi::kStageBytes, &tmC);
+        epi.template run_staged<HB>(st, taddr, row0, lane, n0, M, t / tiles,
+                                    sE + (warp - 2) * Epi::kStageBytes, &tmC);
       } else {
         const bool ready =
             __all_sync(0xffffffffu, mbar_wait(&tm_full[b], (u >> 1) & 1, abort_flag, err));
         if (!ready) break;
         tc_fence_after();
-        epi.template run<BN>(taddr, row0 + lane, n0, M);
+        epi.template run<HB>(taddr, row0 + lane, n0, M);
       }
       tc_fence_before();
       __syncwarp();
