@@ -54,14 +54,16 @@ constexpr int TA_Q_BYTES = TA_QROWS * 128;         // 5 KB per query buffer
 // a query buffer (the other buffer or the barrier area); they only feed S^T
 // columns 40..47, which are never read.
 constexpr int TA_P_BYTES = TA_KT * 128;            // 16 KB
+constexpr int TA_PSLOTS = 1;             // P buffers (2: the softmax of tile t+1 overlaps PV of tile t)
 constexpr int TA_OFF_P = 0;
-constexpr int TA_OFF_K = TA_OFF_P + TA_P_BYTES;
+constexpr int TA_OFF_K = TA_OFF_P + TA_PSLOTS * TA_P_BYTES;
 constexpr int TA_KSLOTS = 2;            // K ring: a slot is released as soon as QK^T has read it
 constexpr int TA_VSLOTS = 3;            // V ring: a slot is held until PV, after the softmax
 constexpr int TA_OFF_V = TA_OFF_K + TA_KSLOTS * TA_KV_BYTES;
 constexpr int TA_OFF_Q = TA_OFF_V + TA_VSLOTS * TA_KV_BYTES;
 constexpr int TA_OFF_MISC = TA_OFF_Q + 2 * TA_Q_BYTES;
 constexpr int TA_MISC_BYTES = 6144;
+constexpr int TA_MISC_RED = 512;         // barriers and flags first, then the float scratch
 constexpr int TA_SMEM = TA_OFF_MISC + TA_MISC_BYTES + 1024;
 constexpr int TA_CTAS_PER_SM = 2;
 // dynamic shared memory + the 1 KB the runtime reserves per CTA
@@ -220,29 +222,31 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
   uint8_t* sV = smem + TA_OFF_V;
   uint8_t* sQ = smem + TA_OFF_Q;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TA_OFF_MISC);
-  uint64_t* k_full = bars;         // [2]
-  uint64_t* k_empty = bars + 2;    // [2]
-  uint64_t* v_full = bars + 4;     // [3]
-  uint64_t* v_empty = bars + 7;    // [3]
-  uint64_t* s_full = bars + 10;    // [2]
-  uint64_t* s_empty = bars + 12;   // [2]  arrivals of the 4 softmax warps
-  uint64_t* q_full = bars + 14;    // [2]  per unit parity
-  uint64_t* q_empty = bars + 16;   // [2]
-  uint64_t* p_full = bars + 18;    //      arrivals of the 4 softmax warps
-  uint64_t* p_empty = bars + 19;
-  uint64_t* o_empty = bars + 20;   // [2]  per unit parity, arrivals of the 4 softmax warps
-  uint64_t* team = bars + 22;      // the 4 softmax warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
+  uint64_t* k_full = bars;                          // [TA_KSLOTS]
+  uint64_t* k_empty = k_full + TA_KSLOTS;           // [TA_KSLOTS]
+  uint64_t* v_full = k_empty + TA_KSLOTS;           // [TA_VSLOTS]
+  uint64_t* v_empty = v_full + TA_VSLOTS;           // [TA_VSLOTS]
+  uint64_t* s_full = v_empty + TA_VSLOTS;           // [2]
+  uint64_t* s_empty = s_full + 2;   // [2]  arrivals of the 4 softmax warps
+  uint64_t* q_full = s_empty + 2;   // [2]  per unit parity
+  uint64_t* q_empty = q_full + 2;   // [2]
+  uint64_t* p_full = q_empty + 2;   // [TA_PSLOTS]  arrivals of the 4 softmax warps
+  uint64_t* p_empty = p_full + TA_PSLOTS;  // [TA_PSLOTS]
+  uint64_t* o_empty = p_empty + TA_PSLOTS;  // [2]  per unit parity, arrivals of the 4 softmax warps
+  uint64_t* team = o_empty + 2;     // the 4 softmax warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(team + 1);
+  static_assert((2 * (TA_KSLOTS + TA_VSLOTS + TA_PSLOTS) + 11) * 8 + 44 <= TA_MISC_RED,
+                "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;
   volatile int* flags = abort_flag + 2;                              // [2][4]
-  float* red = reinterpret_cast<float*>(smem + TA_OFF_MISC + 320);   // [3][4][34]
+  float* red = reinterpret_cast<float*>(smem + TA_OFF_MISC + TA_MISC_RED);   // [3][4][34]
   float* vals = red + 3 * 4 * TA_ROWS;                               // [34]
   float* mfin = vals + TA_ROWS;                                      // [34]
   float* m_s = mfin + TA_ROWS;                                       // [2][34]
   int* page_s = reinterpret_cast<int*>(m_s + 2 * TA_ROWS);           // [2][TA_MAX_PAGES]
   int* order_s = page_s + 2 * TA_MAX_PAGES;                          // [TA_MAX_ORDER]
-  static_assert(320 + (3 * 4 + 5) * TA_ROWS * 4 + (2 * TA_MAX_PAGES + TA_MAX_ORDER) * 4 <=
+  static_assert(TA_MISC_RED + (3 * 4 + 5) * TA_ROWS * 4 + (2 * TA_MAX_PAGES + TA_MAX_ORDER) * 4 <=
                     TA_MISC_BYTES, "misc area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -263,17 +267,21 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
       mbar_init(&v_full[b], 1);
       mbar_init(&v_empty[b], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < TA_KSLOTS; ++b) {
       mbar_init(&k_full[b], 1);
       mbar_init(&k_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_empty[b], 4);
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
       mbar_init(&o_empty[b], 4);
     }
-    mbar_init(p_full, 4);
-    mbar_init(p_empty, 1);
+    for (int b = 0; b < TA_PSLOTS; ++b) {
+      mbar_init(&p_full[b], 4);
+      mbar_init(&p_empty[b], 1);
+    }
     mbar_init(team, 4);
     *abort_flag = 0;
     *last_flag = 0;
@@ -314,7 +322,8 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
     while (!ck.done || !cv.done) {
       int doK = 0, doV = 0, stop = 0;
       if (lane == 0) {
-        doK = !ck.done && (gk < 2 || mbar_test(&k_empty[gk & 1], ((gk >> 1) & 1) ^ 1));
+        doK = !ck.done && (gk < TA_KSLOTS ||
+                           mbar_test(&k_empty[gk % TA_KSLOTS], ((gk / TA_KSLOTS) & 1) ^ 1));
         if (doK && ck.t == 0)   // a new unit: its page ids and query buffer must be free
           doK = ck.seq <= cv.seq + 1 &&
                 (ck.seq < 2 || mbar_test(&q_empty[ck.seq & 1], ((ck.seq >> 1) & 1) ^ 1));
@@ -362,7 +371,7 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
                         ck.f.i * TA_ROWS);
           }
         }
-        load_tile(sK + (gk & 1) * TA_KV_BYTES, &k_full[gk & 1], ck, p.plane_k);
+        load_tile(sK + (gk % TA_KSLOTS) * TA_KV_BYTES, &k_full[gk % TA_KSLOTS], ck, p.plane_k);
         ++gk;
         attn_step(ck, p, order_s, U);
       }
@@ -386,24 +395,24 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
       uint64_t t_idle = 0;
       while (!c2.done && !*abort_flag) {
         bool prog = false;
-        if (!c1.done && mbar_test(&k_full[g1 & 1], (g1 >> 1) & 1) &&
+        if (!c1.done && mbar_test(&k_full[g1 % TA_KSLOTS], (g1 / TA_KSLOTS) & 1) &&
             (g1 < 2 || mbar_test(&s_empty[g1 & 1], ((g1 >> 1) & 1) ^ 1)) &&
             (c1.t > 0 || mbar_test(&q_full[c1.seq & 1], (c1.seq >> 1) & 1))) {
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + (g1 & 1) * TA_KV_BYTES);
+          const uint32_t k_addr = smem_u32(sK + (g1 % TA_KSLOTS) * TA_KV_BYTES);
           const uint32_t q_addr = smem_u32(sQ + (c1.seq & 1) * TA_Q_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_bf16(tmem + (g1 & 1) * 64, umma_desc_sw128(k_addr + kk * 32),
                       umma_desc_sw128(q_addr + kk * 32), idesc_s, kk > 0);
           umma_commit(&s_full[g1 & 1]);
-          umma_commit(&k_empty[g1 & 1]);
+          umma_commit(&k_empty[g1 % TA_KSLOTS]);
           if (c1.t == c1.f.ntiles - 1) umma_commit(&q_empty[c1.seq & 1]);
           ++g1;
           attn_step(c1, p, order_s, U);
           prog = true;
         }
-        if (g2 < g1 && mbar_test(p_full, g2 & 1) &&
+        if (g2 < g1 && mbar_test(&p_full[g2 % TA_PSLOTS], (g2 / TA_PSLOTS) & 1) &&
             mbar_test(&v_full[g2 % TA_VSLOTS], (g2 / TA_VSLOTS) & 1) &&
             (c2.t > 0 || c2.seq < 2 || mbar_test(&o_empty[c2.seq & 1], ((c2.seq >> 1) & 1) ^ 1))) {
           tc_fence_after();
@@ -411,10 +420,12 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
           const uint32_t o_col = tmem + TA_O_COL + (c2.seq & 1) * 64;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(o_col, umma_desc_sw128_mn(p_addr + kk * 2048, TA_P_BYTES),
+            umma_bf16(o_col,
+                      umma_desc_sw128_mn(p_addr + (g2 % TA_PSLOTS) * TA_P_BYTES + kk * 2048,
+                                         TA_P_BYTES),
                       umma_desc_sw128(v_addr + kk * 2048), idesc_o, (c2.t > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&v_empty[g2 % TA_VSLOTS]);
-          umma_commit(p_empty);
+          umma_commit(&p_empty[g2 % TA_PSLOTS]);
           ++g2;
           attn_step(c2, p, order_s, U);
           prog = true;
@@ -511,9 +522,17 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
         ok = __all_sync(0xffffffffu, mbar_wait(&s_empty[sb], (g >> 1) & 1, abort_flag, p.err));
         if (!ok) break;
         const bool need = flags[sb * 4] | flags[sb * 4 + 1] | flags[sb * 4 + 2] | flags[sb * 4 + 3];
-        // the previous PV product must be done before P is rewritten (and O rescaled)
-        if (g >= 1) {
-          ok = __all_sync(0xffffffffu, mbar_wait(p_empty, (g - 1) & 1, abort_flag, p.err));
+        // the PV product that last read this P buffer must be done before it is rewritten
+        if (g >= TA_PSLOTS) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[g % TA_PSLOTS],
+                                                 ((g / TA_PSLOTS) & 1) ^ 1, abort_flag, p.err));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        if (need && TA_PSLOTS > 1 && t >= 1) {
+          // every earlier PV product of the unit must be done before O is rescaled
+          ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[(g - 1) % TA_PSLOTS],
+                                                 ((g - 1) / TA_PSLOTS) & 1, abort_flag, p.err));
           if (!ok) break;
           tc_fence_after();
         }
@@ -575,18 +594,20 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
         for (int j = TA_ROWS; j < 40; ++j) e[j] = 0.f;
 #pragma unroll
         for (int c = 0; c < 5; ++c)
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + ((c ^ psw) << 4)),
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                           prow + (g % TA_PSLOTS) * TA_P_BYTES + ((c ^ psw) << 4)),
                        "r"(pack_bf16(e[8 * c], e[8 * c + 1])), "r"(pack_bf16(e[8 * c + 2], e[8 * c + 3])),
                        "r"(pack_bf16(e[8 * c + 4], e[8 * c + 5])), "r"(pack_bf16(e[8 * c + 6], e[8 * c + 7]))
                        : "memory");
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
+        if (lane == 0) mbar_arrive(&p_full[g % TA_PSLOTS]);
       }
       if (!ok) break;
       // the unit's last PV product
-      ok = __all_sync(0xffffffffu, mbar_wait(p_empty, (g - 1) & 1, abort_flag, p.err));
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[(g - 1) % TA_PSLOTS],
+                                             ((g - 1) / TA_PSLOTS) & 1, abort_flag, p.err));
       if (!ok) break;
       tc_fence_after();
       // per-query sums over the 128 key rows
