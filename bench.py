@@ -45,8 +45,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "prof", "gemm64"],
-                    help="prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
+    ap.add_argument("--workload", default="cfg2",
+                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64"],
+                    help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
+                         "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool)")
     ap.add_argument("--cpu-sample", type=int, default=64,
                     help="requests in the CPU baseline sample (64 = one whole tick)")
@@ -70,6 +72,8 @@ def workload_batch(name: str, rank: int):
     from nanovllm_dots_b200 import synthetic as syn
     if name == "gemm64":
         return syn.make_batch(64, [0] * 64, seed=2)
+    if name == "cfg3":
+        name = "cfg2"
     if name == "prof":
         full = syn.config_batch("cfg2")
         return syn.make_batch(16, [p // 17 for p in full.prefix_rows[:16]], seed=2)
@@ -218,8 +222,9 @@ def run_b200(args, rank, world):
     max_pages = max(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows)
     num_pages = sum(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows) + 8
     weights = syn.make_weights(cfg)
+    precision = "fp8" if args.workload == "cfg3" else "bf16"
     head = B200FMHead(weights, cfg, num_pages=num_pages, max_pages_per_req=max_pages,
-                      max_requests=n, device=dev)
+                      max_requests=n, device=dev, precision=precision)
     # cached prefixes: N(0, 0.5^2) K/V drawn on the device straight into the pool
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     chunk = 1 << 28
@@ -416,13 +421,15 @@ def run_b200(args, rank, world):
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16" if args.workload != "cfg3" else "fp8-e4m3 (QKV, fc1) + bf16",
                 "data": "synthetic (seeded random-init DiT, N(0,1) inputs, N(0,0.5^2) cached K/V)",
                 "config": {"workload": args.workload, "requests_per_gpu": n,
                            "mean_prefix_rows": round(sum(b.prefix_rows) / n, 1),
                            "nfe": cfg.nfe, "layers": cfg.layers, "page_rows": cfg.page_rows,
                            "l2": "inputs larger than L2 (K/V pool and weights), no flush",
-                           "parallelism": f"request-sharded x{world}"},
+                           "parallelism": f"request-sharded x{world}",
+                           "precision": "fp8" if args.workload == "cfg3" else "bf16"},
                 "e2e": {"value": round(e2e_val, 2), "unit": "audio-s/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": round(e2e_ms, 4)},

@@ -38,6 +38,14 @@ extern "C" {
 #define DFM_ERR_DEVICE 5        /* a kernel reported an error (dfm_read_error bits) */
 #define DFM_ERR_SCRATCH_LIMIT 6 /* a call needs more than the fixed scratch of a no-allocation entry point */
 
+/* DfmConfig.precision.  FP8: the QKV and fc1 projections run on e4m3 operands
+ * (the cfg 3 path of the FP8 replacement of the reference's Int8DynamicLinear,
+ * int8_dit.py:34-65): per-output-row weight scales from the caller and per-row
+ * activation scales computed where the LayerNorm writes its rows; every other
+ * GEMM stays bf16. */
+#define DFM_PRECISION_BF16 0
+#define DFM_PRECISION_FP8 1
+
 /* Bits of the device error word returned by dfm_read_error. */
 #define DFM_DEVERR_TIMEOUT 1u   /* a bounded in-kernel wait gave up */
 #define DFM_DEVERR_PAGE 2u      /* a block-table entry was outside [0, num_pages) */
@@ -62,7 +70,7 @@ typedef struct DfmConfig {
   int32_t max_pages_per_req; /* block-table width */
   int32_t max_requests;      /* largest n a dfm_step may carry */
   float ln_eps;              /* LayerNorm eps (1e-5) */
-  int32_t precision;         /* 0 = bf16 (only value supported) */
+  int32_t precision;         /* DFM_PRECISION_BF16 (0) or DFM_PRECISION_FP8 (1) */
 } DfmConfig;
 
 /* Weights.  Replaces the module tree read by the reference accelerators:
@@ -87,6 +95,11 @@ typedef struct DfmWeights {
   const void* hidden_w;  const float* hidden_b;   /* hidden_proj [H, cond_dim] */
   const void* latent_w;  const float* latent_b;   /* latent_proj [H, ld] */
   const float* rope_inv_freq;                     /* [head_dim/2], theta^(-2i/head_dim) */
+  /* precision DFM_PRECISION_FP8 only (qkv_w and fc1_w may then be NULL):
+   * e4m3 bytes of the same matrices with one fp32 scale per output row
+   * (W ~= w8 * scale[row]; scale = row absmax / 448) */
+  const void* qkv_w8;    const float* qkv_ws;     /* [layers, 3H, H] e4m3, [layers, 3H] */
+  const void* fc1_w8;    const float* fc1_ws;     /* [layers, F, H] e4m3, [layers, F] */
 } DfmWeights;
 
 /* One engine tick for n requests.  Replaces the payload list handed to

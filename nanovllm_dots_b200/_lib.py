@@ -33,7 +33,8 @@ class DfmConfig(ctypes.Structure):
 WEIGHT_FIELDS = ("input_w", "input_b", "temb_w1", "temb_b1", "temb_w2", "temb_b2", "demb_w1",
                  "demb_b1", "demb_w2", "demb_b2", "ada_w", "ada_b", "qkv_w", "qk_norm", "o_w",
                  "o_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "final_w", "final_b", "coord_w",
-                 "coord_b", "hidden_w", "hidden_b", "latent_w", "latent_b", "rope_inv_freq")
+                 "coord_b", "hidden_w", "hidden_b", "latent_w", "latent_b", "rope_inv_freq",
+                 "qkv_w8", "qkv_ws", "fc1_w8", "fc1_ws")
 
 
 class DfmWeights(ctypes.Structure):

@@ -57,6 +57,21 @@ bool map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D 8-bit K-major operand [rows, cols] (e4m3 bytes) with row stride ld bytes,
+// box {128, box_rows}, 128-byte swizzle, zero fill out of bounds.
+bool map_2d_u8(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+               uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The K/V pool as a 5-D tensor [planes][pages][heads][16][64]; one box is one
 // (page, head) block of 16 rows x 64 dims.
 bool map_pool(CUtensorMap* m, const void* base, int num_pages, int heads, int planes) {
@@ -137,14 +152,14 @@ cudaError_t gemm(const CUtensorMap& a, const CUtensorMap& b, int M, int N, int K
 // whichever is smaller, so the kernel stays persistent.  W's tensor map must
 // have box rows BN / 2; `c` is the output map of staged epilogues (ignored by
 // the others); ksplit > 1 splits K into that many partial sums.
-template <int BN, int ST, class Epi>
+template <int BN, int ST, class Epi, bool FP8 = false>
 cudaError_t gemm2(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, int M, int N,
                   int K, int ksplit, const Epi& e, uint32_t* err, cudaStream_t s) {
   if (M <= 0) return cudaSuccess;
-  if (ksplit < 1 || (K / GEMM_BK) % ksplit) return cudaErrorInvalidValue;
+  if (ksplit < 1 || (K / (FP8 ? 2 * GEMM_BK : GEMM_BK)) % ksplit) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr_done{0};
   static std::atomic<int> pairs_cache[64];
-  auto fn = gemm2_bf16_tn<BN, ST, Epi>;
+  auto fn = gemm2_bf16_tn<BN, ST, Epi, FP8>;
   constexpr int smem = Gemm2Shape<BN, ST, Epi::kStageBytes, Epi::kEpiWarps>::SMEM;
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
@@ -229,7 +244,7 @@ bool map_q(CUtensorMap* m, const void* q, uint64_t rows, int heads) {
 
 // ---------------------------------------------------------------- handle
 struct WsLayout {
-  size_t err, csilu, mod, emb1, xrows, h, sub, xm, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
+  size_t err, csilu, mod, emb1, xrows, h, sub, xm, xm8, xs, qb, ob, u, z, zb, xmf, st_act, st_exth, st_extl,
       part_o, part_ml, sem, rope, total;
 };
 
@@ -245,6 +260,9 @@ struct Handle {
   CUtensorMap* m_o;
   CUtensorMap* m_fc1;
   CUtensorMap* m_fc2;
+  CUtensorMap* m_qkv8;   // precision 1: e4m3 QKV and fc1 weights
+  CUtensorMap* m_fc18;
+  CUtensorMap a_xm8;     // precision 1: e4m3 LayerNorm output rows
   // per-workspace/pool descriptors
   const void* plan_ws = nullptr;
   const void* plan_pool = nullptr;
@@ -270,6 +288,8 @@ WsLayout layout_for(const DfmConfig& c, int mc) {
   L.h = take(R * H * 4);
   L.sub = take(2 * R * H * 4);   // two split-K partial planes
   L.xm = take(R * H * 2);
+  L.xm8 = take(R * H);        // e4m3 rows (precision 1)
+  L.xs = take(R * 4);         // their per-row scales
   L.qb = take(R * H * 2);
   L.ob = take(R * H * 2);
   L.u = take(R * c.ffn * 2);
@@ -291,7 +311,8 @@ int validate_config(const DfmConfig& c) {
   if (c.hidden != kH || c.heads * c.head_dim != c.hidden || c.head_dim != 64) return DFM_ERR_UNSUPPORTED;
   if (c.latent_patch != 16 || c.hidden_patch != 1 || c.latent_dim != 64) return DFM_ERR_UNSUPPORTED;
   if (c.ffn % 256 != 0 || c.cond_dim % 64 != 0 || c.cond_dim <= 0) return DFM_ERR_UNSUPPORTED;
-  if (c.page_rows != 16 || c.precision != 0) return DFM_ERR_UNSUPPORTED;
+  if (c.page_rows != 16 || (c.precision != DFM_PRECISION_BF16 && c.precision != DFM_PRECISION_FP8))
+    return DFM_ERR_UNSUPPORTED;
   if (c.nfe < 1 || c.nfe > EMB_MAX_STEPS) return DFM_ERR_UNSUPPORTED;
   if (c.layers < 1 || c.num_pages < 1 || c.max_pages_per_req < 1 || c.max_requests < 1)
     return DFM_ERR_INVALID_ARG;
@@ -317,6 +338,7 @@ bool ensure_plan(Handle* h, void* ws, void* pool, cudaStream_t s) {
             map_2d(&h->a_extl, b + h->ws.st_extl, LP, c.latent_dim, c.latent_dim, 128) &&
             map_q(&h->q_att, b + h->ws.qb, R, c.heads) &&
             map_out(&h->o_sub, b + h->ws.sub, true, R, H, 2, R * H * 4) &&
+            map_2d_u8(&h->a_xm8, b + h->ws.xm8, R, H, H, 128) &&
             map_out(&h->o_u, b + h->ws.u, false, R, c.ffn, 1, R * c.ffn * 2) &&
             map_pool(&h->pool, pool, c.num_pages, c.heads, c.layers * c.nfe * 2);
   if (!ok) {
@@ -373,11 +395,14 @@ int dfm_create(const DfmConfig* cfg, const DfmWeights* w, void** out) {
   *out = nullptr;
   int rc = validate_config(*cfg);
   if (rc != DFM_OK) return rc;
+  const bool fp8 = cfg->precision == DFM_PRECISION_FP8;
   const void* req[] = {w->input_w, w->input_b, w->temb_w1, w->temb_b1, w->temb_w2, w->temb_b2,
                        w->demb_w1, w->demb_b1, w->demb_w2, w->demb_b2, w->ada_w, w->ada_b,
-                       w->qkv_w, w->qk_norm, w->o_w, w->o_b, w->fc1_w, w->fc1_b, w->fc2_w,
-                       w->fc2_b, w->final_w, w->final_b, w->coord_w, w->coord_b, w->hidden_w,
-                       w->hidden_b, w->latent_w, w->latent_b, w->rope_inv_freq};
+                       fp8 ? w->qkv_w8 : w->qkv_w, w->qk_norm, w->o_w, w->o_b,
+                       fp8 ? w->fc1_w8 : w->fc1_w, w->fc1_b, w->fc2_w, w->fc2_b, w->final_w,
+                       w->final_b, w->coord_w, w->coord_b, w->hidden_w, w->hidden_b, w->latent_w,
+                       w->latent_b, w->rope_inv_freq, fp8 ? w->qkv_ws : w->rope_inv_freq,
+                       fp8 ? w->fc1_ws : w->rope_inv_freq};
   for (const void* p : req)
     if (!p) return DFM_ERR_INVALID_ARG;
   if (!encode_fn()) return DFM_ERR_CUDA;
@@ -398,7 +423,10 @@ int dfm_create(const DfmConfig* cfg, const DfmWeights* w, void** out) {
   h->m_o = new CUtensorMap[L];
   h->m_fc1 = new CUtensorMap[L];
   h->m_fc2 = new CUtensorMap[L];
+  h->m_qkv8 = new CUtensorMap[L];
+  h->m_fc18 = new CUtensorMap[L];
   auto bw = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  auto b8 = [](const void* p) { return static_cast<const uint8_t*>(p); };
   bool ok = map_2d(&h->m_ada, w->ada_w, h->mod_w, H, H, 256) &&
             map_2d(&h->m_in, w->input_w, H, H, H, 128) &&
             map_2d(&h->m_final, w->final_w, c.latent_dim, H, H, 64) &&
@@ -407,13 +435,19 @@ int dfm_create(const DfmConfig* cfg, const DfmWeights* w, void** out) {
             map_2d(&h->m_lat, w->latent_w, H, c.latent_dim, c.latent_dim, 128);
   for (int l = 0; ok && l < L; ++l) {
     // per-layer weights feed the CTA-pair GEMM: box rows = half the tile's N
-    ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * 3 * H * H, 3 * H, H, H,
-                kQkvBN / 2) &&
-         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * H * H, H, H, H, kOutBN / 2) &&
-         map_2d(&h->m_fc1[l], bw(w->fc1_w) + static_cast<size_t>(l) * c.ffn * H, c.ffn, H, H,
-                kFc1BN / 2) &&
+    ok = map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * H * H, H, H, H, kOutBN / 2) &&
          map_2d(&h->m_fc2[l], bw(w->fc2_w) + static_cast<size_t>(l) * H * c.ffn, H, c.ffn, c.ffn,
                 kOutBN / 2);
+    if (ok && fp8)
+      ok = map_2d_u8(&h->m_qkv8[l], b8(w->qkv_w8) + static_cast<size_t>(l) * 3 * H * H, 3 * H, H, H,
+                     kQkvBN / 2) &&
+           map_2d_u8(&h->m_fc18[l], b8(w->fc1_w8) + static_cast<size_t>(l) * c.ffn * H, c.ffn, H, H,
+                     kFc1BN / 2);
+    else if (ok)
+      ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * 3 * H * H, 3 * H, H, H,
+                  kQkvBN / 2) &&
+           map_2d(&h->m_fc1[l], bw(w->fc1_w) + static_cast<size_t>(l) * c.ffn * H, c.ffn, H, H,
+                  kFc1BN / 2);
   }
   if (!ok) {
     dfm_destroy(h);
@@ -434,6 +468,8 @@ int dfm_destroy(void* handle) {
   delete[] h->m_o;
   delete[] h->m_fc1;
   delete[] h->m_fc2;
+  delete[] h->m_qkv8;
+  delete[] h->m_fc18;
   delete h;
   return DFM_OK;
 }
@@ -558,11 +594,16 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   __nv_bfloat16* xm = bf(hd->ws.xm);
   // the second split-K partial of `sub` (O-projection and fc2 outputs)
   const size_t sub_plane = kOutSplit > 1 ? static_cast<size_t>(kSlot) * c.max_requests * H : 0;
+  // precision 1: the LayerNorm outputs that feed QKV and fc1 are e4m3 rows
+  const bool fp8 = c.precision == DFM_PRECISION_FP8;
+  uint8_t* xm8 = ws + hd->ws.xm8;
+  float* xs = f32(hd->ws.xs);
   auto ln = [&](int M, RowMap map, const float* subp, const float* gate, const float* shift,
-                const float* scale, int rows_per_req, __nv_bfloat16* out) {
+                const float* scale, int rows_per_req, __nv_bfloat16* out, uint8_t* out8 = nullptr,
+                float* out_scale = nullptr) {
     return launch_pdl(ln_mod_kernel, dim3((M * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp,
                       subp ? sub_plane : size_t{0}, gate, M, map, shift, scale,
-                      static_cast<int>(modw), rows_per_req, out, c.ln_eps);
+                      static_cast<int>(modw), rows_per_req, out, c.ln_eps, out8, out_scale);
   };
   for (int k = 0; k < NFE; ++k) {
     const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;
@@ -573,7 +614,8 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
     const float* pending_gate = nullptr;   // gate of the sublayer whose output sits in `sub`
     for (int l = 0; l < L; ++l) {
       const float* mb = mod_k + static_cast<size_t>(l) * 6 * H;
-      CK(ln(R, kIdentity, pending_gate ? sub : nullptr, pending_gate, mb, mb + H, kSlot, xm));
+      CK(ln(R, kIdentity, pending_gate ? sub : nullptr, pending_gate, mb, mb + H, kSlot, xm,
+            fp8 ? xm8 : nullptr, xs));
       EpiQKV eq;
       eq.q_out = bf(hd->ws.qb);
       eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
@@ -594,17 +636,31 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       eq.max_pos = c.max_pages_per_req * 16;
       eq.eps = c.ln_eps;
       eq.err = err;
-      CK(gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s));
+      if (fp8) {
+        eq.a_scale = xs;
+        eq.w_scale = w.qkv_ws + static_cast<size_t>(l) * 3 * H;
+        CK((gemm2<kQkvBN, kQkvST, EpiQKV, true>(hd->a_xm8, hd->m_qkv8[l], hd->a_xm8, R, 3 * H, H, 1,
+                                                eq, err, s)));
+      } else {
+        CK(gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s));
+      }
       ap.plane_k = eq.plane_k;
       ap.plane_v = eq.plane_v;
       CK(launch_attention(hd->pool, hd->q_att, ap, s));
       // attention out projection -> sub; h += gate_a * sub inside the next LN
       CK(gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, kOutSplit,
                                store_t<true>(w.o_b + static_cast<size_t>(l) * H, false), err, s));
-      CK(ln(R, kIdentity, sub, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, xm));
-      CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1,
-                               store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, true), err,
-                               s));
+      CK(ln(R, kIdentity, sub, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, xm, fp8 ? xm8 : nullptr,
+            xs));
+      auto e1 = store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, true);
+      if (fp8) {
+        e1.a_scale = xs;
+        e1.w_scale = w.fc1_ws + static_cast<size_t>(l) * c.ffn;
+        CK((gemm2<kFc1BN, kFc1ST, EpiStoreT<false>, true>(hd->a_xm8, hd->m_fc18[l], hd->o_u, R,
+                                                          c.ffn, H, 1, e1, err, s)));
+      } else {
+        CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1, e1, err, s));
+      }
       CK(gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, H, c.ffn, kOutSplit,
                                store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, false), err, s));
       pending_gate = mb + 5 * H;

@@ -10,6 +10,7 @@ namespace dfm {
 //   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h; with
 //   sub_plane != 0, sub is the sum of two split-K partials sub[.] + sub[. + sub_plane])
 //   out[r] = LN(x) * (1 + scale[req]) + shift[req],   req = r / rows_per_req
+//   (bf16; or, with out8, e4m3 values out8[r] with out[r] = out8[r] * out_scale[r])
 // LayerNorm without affine over H = 1024 (``native/dit.py:70-71,19-20``).  The
 // residual add of the previous sublayer (``dit.py:102-107``: x + gate * f(x))
 // is applied here, on coalesced rows, instead of in that sublayer's GEMM
@@ -18,7 +19,8 @@ __global__ void __launch_bounds__(256)
     ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub, size_t sub_plane,
                   const float* __restrict__ gate, int M, RowMap in_map,
                   const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
-                  int rows_per_req, __nv_bfloat16* __restrict__ out, float eps) {
+                  int rows_per_req, __nv_bfloat16* __restrict__ out, float eps,
+                  uint8_t* __restrict__ out8, float* __restrict__ out_scale) {
   constexpr int H = 1024;
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -63,18 +65,38 @@ __global__ void __launch_bounds__(256)
   const float rstd = rsqrtf(warp_sum(v) * (1.0f / H) + eps);
   const float* sh = shift + req * mod_ld;
   const float* sc = scale + req * mod_ld;
-  __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int col = j * 128 + lane * 4;
     const float4 a = *reinterpret_cast<const float4*>(sh + col);
     const float4 b = *reinterpret_cast<const float4*>(sc + col);
-    const float y0 = (x[j].x - mean) * rstd * (1.f + b.x) + a.x;
-    const float y1 = (x[j].y - mean) * rstd * (1.f + b.y) + a.y;
-    const float y2 = (x[j].z - mean) * rstd * (1.f + b.z) + a.z;
-    const float y3 = (x[j].w - mean) * rstd * (1.f + b.w) + a.w;
-    *reinterpret_cast<uint2*>(o + col) = make_uint2(pack_bf16(y0, y1), pack_bf16(y2, y3));
+    x[j].x = (x[j].x - mean) * rstd * (1.f + b.x) + a.x;
+    x[j].y = (x[j].y - mean) * rstd * (1.f + b.y) + a.y;
+    x[j].z = (x[j].z - mean) * rstd * (1.f + b.z) + a.z;
+    x[j].w = (x[j].w - mean) * rstd * (1.f + b.w) + a.w;
   }
+  if (out8) {
+    // e4m3 row with one fp32 scale per row (row absmax / 448)
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(x[j].x), fabsf(x[j].y)), fmaxf(fabsf(x[j].z), fabsf(x[j].w))));
+    m = warp_max(m);
+    const float s = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
+    const float inv = 1.0f / s;
+    uint8_t* o8 = out8 + static_cast<size_t>(r) * H;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint32_t*>(o8 + j * 128 + lane * 4) =
+          pack_e4m3x4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
+    if (lane == 0) out_scale[r] = s;
+    return;
+  }
+  __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint2*>(o + j * 128 + lane * 4) =
+        make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
 }
 
 constexpr int EMB_MAX_STEPS = 8;

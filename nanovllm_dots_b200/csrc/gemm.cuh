@@ -106,17 +106,39 @@ struct EpiStoreT {
   static constexpr int CW = F32 ? 32 : 64;  // columns per 128-byte line
   const float* bias;
   int gelu;
+  const float* a_scale = nullptr;  // FP8 operands: per-row scale of A ...
+  const float* w_scale = nullptr;  // ... and per-output-column scale of W
 
-  struct Row {};
+  // Loaded before the accumulator is ready: lane l holds the bias and weight
+  // scale of columns n0 + 4l .. 4l + 3 (the warp's BN <= 128 columns), handed
+  // to the other lanes by shuffles, and the scale of its own row.
+  struct Row {
+    float4 b4, w4;
+    float sa;
+  };
   template <int BN>
-  DFM_DEV Row row_state(int, int, int, int) const { return {}; }
+  DFM_DEV Row row_state(int row0, int lane, int n0, int M) const {
+    static_assert(BN <= 128, "four columns per lane");
+    Row st;
+    st.b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    st.w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    st.sa = 1.f;
+    if (4 * lane < BN) {
+      if (bias) st.b4 = __ldg(reinterpret_cast<const float4*>(bias + n0) + lane);
+      if (a_scale) st.w4 = __ldg(reinterpret_cast<const float4*>(w_scale + n0) + lane);
+    }
+    if (a_scale) st.sa = row0 + lane < M ? a_scale[row0 + lane] : 0.f;
+    return st;
+  }
 
   template <int BN>
-  DFM_DEV void run_staged(const Row&, uint32_t taddr, int row0, int lane, int n0, int M, int split,
+  DFM_DEV void run_staged(const Row& st, uint32_t taddr, int row0, int lane, int n0, int M, int split,
                           uint8_t* stage, const CUtensorMap* map) const {
     static_assert(BN % CW == 0, "tile width");
     if (row0 >= M) return;  // all 32 rows of this warp are padding
     const bool add_bias = bias != nullptr && split == 0;
+    const float bsel[4] = {st.b4.x, st.b4.y, st.b4.z, st.b4.w};
+    const float wsel[4] = {st.w4.x, st.w4.y, st.w4.z, st.w4.w};
     uint8_t* rowp = stage + lane * 128;
     const int sw = lane & 7;
     int it = 0;
@@ -141,12 +163,14 @@ struct EpiStoreT {
           }
         }
       }
+      if (a_scale) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j)
+          v[j] *= st.sa * __shfl_sync(0xffffffffu, wsel[j & 3], (c + j) >> 2);
+      }
       if (add_bias) {
 #pragma unroll
-        for (int j = 0; j < CW; j += 4) {
-          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + j));
-          v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
-        }
+        for (int j = 0; j < CW; ++j) v[j] += __shfl_sync(0xffffffffu, bsel[j & 3], (c + j) >> 2);
       }
       if (gelu) {
 #pragma unroll
@@ -209,6 +233,8 @@ struct EpiQKV {
   int max_pos;
   float eps;
   uint32_t* err;
+  const float* a_scale = nullptr;  // FP8 operands: per-row scale of A ...
+  const float* w_scale = nullptr;  // ... and per-output-column scale of W
 
   // Per-row state gathered before the accumulator is ready (the loads overlap
   // the mainloop): position, destination page (k/v tiles) and the rotary
@@ -217,6 +243,8 @@ struct EpiQKV {
     int pos, page;
     bool in_range;
     float2 cs[32];
+    float sa;        // FP8: this row's activation scale
+    float4 wlo, whi; // FP8: weight scales of columns n0 + 8l .. 8l + 7 (lane l)
   };
 
   template <int BN>
@@ -242,6 +270,16 @@ struct EpiQKV {
           atomicOr(err, DFM_DEV_ERR_PAGE);
           st.page = -1;
         }
+      }
+    }
+    st.sa = 1.f;
+    st.wlo = st.whi = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (a_scale) {
+      static_assert(BN <= 256, "eight columns per lane");
+      st.sa = st.in_range ? a_scale[row] : 0.f;
+      if (8 * lane < BN) {
+        st.wlo = __ldg(reinterpret_cast<const float4*>(w_scale + n0) + 2 * lane);
+        st.whi = __ldg(reinterpret_cast<const float4*>(w_scale + n0) + 2 * lane + 1);
       }
     }
     if (n0 < 2 * H) {  // q or k columns: rotary at this row's position
@@ -273,6 +311,13 @@ struct EpiQKV {
         }
       }
       const int col = n0 + c;
+      if (a_scale) {
+        const float wsel[8] = {st.wlo.x, st.wlo.y, st.wlo.z, st.wlo.w,
+                               st.whi.x, st.whi.y, st.whi.z, st.whi.w};
+#pragma unroll
+        for (int d = 0; d < 64; ++d)
+          x[d] *= st.sa * __shfl_sync(0xffffffffu, wsel[d & 7], (c + d) >> 3);
+      }
       const int sec = col / H;
       const int head = (col - sec * H) >> 6;
       __nv_bfloat16* dst = nullptr;
@@ -549,7 +594,9 @@ struct Gemm2Shape {
 // Work units are (output tile, K split): unit t covers tile t % tiles and
 // k-blocks [s * nk / ksplit, (s + 1) * nk / ksplit) with s = t / tiles; the
 // epilogue gets s (split-K partial sums go to separate output planes).
-template <int BN, int STAGES, class Epi>
+// FP8: both operands e4m3 (one 128-byte swizzle row = 128 elements of K per
+// k-block, kind::f8f6f4 MMAs); the epilogue applies the row and column scales.
+template <int BN, int STAGES, class Epi, bool FP8 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads<Epi>(), 1)
     gemm2_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int ksplit, Epi epi,
@@ -575,7 +622,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads<Epi>()
   const int tiles_m = (M + 2 * GEMM_BM - 1) / (2 * GEMM_BM);
   const int tiles = tiles_m * (N / BN);
   const int total = tiles * ksplit;
-  const int nkb = K / GEMM_BK / ksplit;  // k-blocks per unit
+  constexpr int BKE = FP8 ? 2 * GEMM_BK : GEMM_BK;  // K elements per 128-byte k-block
+  const int nkb = K / BKE / ksplit;  // k-blocks per unit
 
   if (threadIdx.x == 0) {
 #pragma unroll 1
@@ -615,7 +663,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads<Epi>()
       for (int kb = 0; kb < pre; ++kb) {
         if (rank == 0) mbar_arrive_expect_tx(&full[kb], 2 * S::STAGE_BYTES);
         tma_load_2d_pair(sB + kb * S::B_BYTES, &tmB, cluster_map(smem_u32(&full[kb]), 0),
-                         (k00 + kb) * GEMM_BK, n00);
+                         (k00 + kb) * BKE, n00);
       }
       pdl_wait();
       int g = 0;
@@ -635,15 +683,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads<Epi>()
               break;
             }
             if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * S::STAGE_BYTES);
-            tma_load_2d_pair(sB + s * S::B_BYTES, &tmB, bar, (k0 + kb) * GEMM_BK, n0);
+            tma_load_2d_pair(sB + s * S::B_BYTES, &tmB, bar, (k0 + kb) * BKE, n0);
           }
-          tma_load_2d_pair(sA + s * S::A_BYTES, &tmA, bar, (k0 + kb) * GEMM_BK, m0);
+          tma_load_2d_pair(sA + s * S::A_BYTES, &tmA, bar, (k0 + kb) * BKE, m0);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(2 * GEMM_BM, BN);
+      constexpr uint32_t idesc = FP8 ? umma_idesc_e4m3(2 * GEMM_BM, BN) : umma_idesc_bf16(2 * GEMM_BM, BN);
       int g = 0, u = 0;
       bool ok = true;
 #pragma unroll 1
@@ -664,9 +712,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads<Epi>()
           const uint32_t a = smem_u32(sA + s * S::A_BYTES);
           const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk)
-            umma_bf16_pair(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
-                           (kb | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk) {  // 32 bytes of K per MMA
+            if constexpr (FP8)
+              umma_fp8_pair(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+                            (kb | kk) != 0);
+            else
+              umma_bf16_pair(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+                             (kb | kk) != 0);
+          }
           const uint32_t e = smem_u32(&empty[s]);
           umma_commit_pair(cluster_map(e, 0));
           umma_commit_pair(cluster_map(e, 1));

@@ -26,11 +26,28 @@ from .synthetic import BASE, FMConfig
 # --------------------------------------------------------------------------- #
 # Weights                                                                      #
 # --------------------------------------------------------------------------- #
-def pack_weights(sd: dict[str, torch.Tensor], cfg: FMConfig, device) -> dict[str, torch.Tensor]:
+PRECISIONS = {"bf16": 0, "fp8": 1}   # DFM_PRECISION_BF16 / DFM_PRECISION_FP8
+
+
+def quantize_rows_e4m3(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rowwise e4m3 quantisation of the last dimension: returns (bytes uint8,
+    fp32 scale per row) with w ~= e4m3(bytes) * scale, scale = row absmax / 448
+    (1 for an all-zero row).  The FP8 counterpart of the reference's
+    Int8DynamicLinear weight quantisation (``int8_dit.py:34-65``)."""
+    wf = w.float()
+    amax = wf.abs().amax(dim=-1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (wf / scale.unsqueeze(-1)).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8), scale
+
+
+def pack_weights(sd: dict[str, torch.Tensor], cfg: FMConfig, device,
+                 precision: str = "bf16") -> dict[str, torch.Tensor]:
     """Pack reference-named weights into the C-ABI layout (bf16 matrices, fp32
     vectors) on ``device``.  Keys follow the reference state dict
     (``native/dit.py`` module names plus ``coordinate_proj``, ``hidden_proj``,
-    ``latent_proj``)."""
+    ``latent_proj``).  ``precision="fp8"`` adds the e4m3 QKV and fc1 matrices
+    with their per-row scales (quantised from the bf16 weights)."""
     L = cfg.layers
     bf = lambda t: t.detach().to(device=device, dtype=torch.bfloat16).contiguous()
     f32 = lambda t: t.detach().to(device=device, dtype=torch.float32).contiguous()
@@ -66,13 +83,22 @@ def pack_weights(sd: dict[str, torch.Tensor], cfg: FMConfig, device) -> dict[str
     # RotaryEmbedding.inv_freq exactly as the reference builds it (layers.py:105-110)
     dh = cfg.head_dim
     out["rope_inv_freq"] = f32(1.0 / (cfg.rotary_theta ** (torch.arange(0, dh, 2).float() / dh)))
+    if precision not in PRECISIONS:
+        raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {precision!r}")
+    if precision == "fp8":
+        for name in ("qkv", "fc1"):
+            q, s = quantize_rows_e4m3(out[f"{name}_w"])
+            out[f"{name}_w8"] = q.contiguous()
+            out[f"{name}_ws"] = s.contiguous()
     return out
 
 
-def abi_config(cfg: FMConfig, num_pages: int, max_pages_per_req: int, max_requests: int):
+def abi_config(cfg: FMConfig, num_pages: int, max_pages_per_req: int, max_requests: int,
+               precision: str = "bf16"):
     return _lib.DfmConfig(cfg.layers, cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn, cfg.latent_dim,
                           cfg.latent_patch, cfg.hidden_patch, cfg.cond_dim, cfg.nfe, cfg.page_rows,
-                          num_pages, max_pages_per_req, max_requests, cfg.ln_eps, 0)
+                          num_pages, max_pages_per_req, max_requests, cfg.ln_eps,
+                          PRECISIONS[precision])
 
 
 # --------------------------------------------------------------------------- #
@@ -137,17 +163,18 @@ class B200FMHead:
 
     def __init__(self, weights: dict[str, torch.Tensor], cfg: FMConfig = BASE, *,
                  num_pages: int, max_pages_per_req: int, max_requests: int,
-                 device: torch.device | str = "cuda"):
+                 device: torch.device | str = "cuda", precision: str = "bf16"):
         self.cfg = cfg
+        self.precision = precision
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("B200FMHead runs on a CUDA device only (no CPU path)")
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.L = _lib.lib()
-        self.w = pack_weights(weights, cfg, self.device)
-        self.acfg = abi_config(cfg, num_pages, max_pages_per_req, max_requests)
-        wstruct = _lib.DfmWeights(*[_lib.ptr(self.w[f]) for f in _lib.WEIGHT_FIELDS])
+        self.w = pack_weights(weights, cfg, self.device, precision)
+        self.acfg = abi_config(cfg, num_pages, max_pages_per_req, max_requests, precision)
+        wstruct = _lib.DfmWeights(*[_lib.ptr(self.w.get(f)) for f in _lib.WEIGHT_FIELDS])
         h = _lib.c_void_p()
         with torch.cuda.device(self.device):
             _lib.check(self.L.dfm_create(self.acfg, wstruct, h), "dfm_create")

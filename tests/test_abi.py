@@ -84,5 +84,24 @@ def test_pack_weights_layout(weights):
     assert p["qk_norm"].shape == (L, 4, 64)
     assert p["fc2_w"].shape == (L, H, F)
     assert p["rope_inv_freq"].shape == (32,)
+    fp8_only = {"qkv_w8", "qkv_ws", "fc1_w8", "fc1_ws"}
     for f in _lib.WEIGHT_FIELDS:
-        assert f in p
+        assert (f in p) == (f not in fp8_only)
+
+
+def test_pack_weights_fp8_rowwise(weights):
+    """The e4m3 copies of the QKV and fc1 matrices dequantise to the bf16
+    weights within e4m3 rounding (half a unit in the last place, 3 mantissa
+    bits: at most 1/16 of each value) with one scale per output row."""
+    p = pack_weights(weights, BASE, "cpu", "fp8")
+    H, L, F = BASE.hidden, BASE.layers, BASE.ffn
+    assert p["qkv_w8"].shape == (L, 3 * H, H) and p["qkv_w8"].dtype == torch.uint8
+    assert p["fc1_w8"].shape == (L, F, H) and p["fc1_ws"].shape == (L, F)
+    for name in ("qkv", "fc1"):
+        w = p[f"{name}_w"][:2].float()
+        deq = p[f"{name}_w8"][:2].view(torch.float8_e4m3fn).float() * p[f"{name}_ws"][:2, :, None]
+        assert (deq - w).abs().le(w.abs() / 16 + p[f"{name}_ws"][:2, :, None] * 2 ** -9).all()
+        # the row absmax maps to 448 exactly
+        assert torch.allclose(deq.abs().amax(-1), w.abs().amax(-1), rtol=1e-6)
+    with pytest.raises(ValueError):
+        pack_weights(weights, BASE, "cpu", "int4")
