@@ -26,7 +26,7 @@ import weakref
 
 import torch
 
-from .fm_head import B200FMHead
+from .fm_head import B200FMHead, FMRequest
 
 
 class B200FMDispatch:
@@ -65,19 +65,43 @@ class B200FMDispatch:
             rid = self._rid(p)
             s = self._cached[rid]
             e = L - c.hidden_patch
-            if e - s > c.stride:
-                raise RuntimeError(f"{e - s} FM history rows to graduate in one tick (max "
-                                   f"{c.stride}); prime the cache first")
             if e < s:
                 raise RuntimeError("FM history shrank below the cached prefix")
             plans.append((rid, s, e))
         return plans
 
+    @staticmethod
+    def _g_cond(p):
+        return p.g_cond if p.g_cond is not None else getattr(p.gen_state, "fm_null_g_cond", None)
+
+    def _prime_backlog(self, payloads, plans):
+        """Requests with more history rows pending than one tick graduates
+        (a voice-clone prompt, a request switched in mid-stream) get all but
+        the last ``stride`` of them bulk-prefilled first (``B200FMHead.prime``)."""
+        c, head = self.cfg, self.head
+        rids, rows, gs, out = [], [], [], []
+        for p, (rid, s, e) in zip(payloads, plans):
+            if e - s > c.stride:
+                cut = e - c.stride
+                rids.append(rid)
+                rows.append(p.gen_state.fm_sequence[0, s:cut])
+                gc = self._g_cond(p)
+                gs.append(torch.zeros(c.hidden) if gc is None else gc.float().reshape(-1).cpu())
+                self._cached[rid] = cut
+                out.append((rid, cut, e))
+            else:
+                out.append((rid, s, e))
+        if rids:
+            for rid in rids:
+                head.requests.setdefault(rid, FMRequest(rid))
+            head.prime(rids, rows, g_cond=torch.stack(gs).to(torch.bfloat16))
+        return out
+
     @torch.no_grad()
     def __call__(self, payloads) -> torch.Tensor:
         c, head = self.cfg, self.head
         dev = head.device
-        plans = self.plan(payloads)
+        plans = self._prime_backlog(payloads, self.plan(payloads))
         n = len(payloads)
         H = c.hidden
         act = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
@@ -90,7 +114,7 @@ class B200FMDispatch:
             if e > s:
                 ext[i, : e - s] = seq[0, s:e]
             n_ext.append(e - s)
-            gc = p.g_cond if p.g_cond is not None else getattr(p.gen_state, "fm_null_g_cond", None)
+            gc = self._g_cond(p)
             if gc is not None:
                 g[i] = gc.to(dev, torch.bfloat16).reshape(-1)
         # same draw as batched_meanflow (batched_fm.py:110-111) so seeded runs line up

@@ -223,8 +223,10 @@ class B200FMHead:
         req.cache_len = P
 
     def release(self, rid) -> None:
-        """Free a finished request's pages (``engine.py:460-473`` cancel/finish)."""
+        """Free a finished request's pages and state (``engine.py:460-473``
+        cancel/finish)."""
         self.pages.release(rid)
+        self.requests.pop(rid, None)
         self.requests.pop(rid, None)
 
     # ------------------------------------------------------------- ticks
@@ -289,6 +291,42 @@ class B200FMHead:
         for rid, e in zip(rids, n_extend):
             self.requests[rid].cache_len += int(e)
         return out
+
+    @torch.no_grad()
+    def prime(self, rids, rows, g_cond=None) -> None:
+        """Bulk prefill of the caches (``prime_to``, ``flash_cached_fm.py:279-313``,
+        used for voice-clone prompts and late switch-in, ``engine.py:440-458``):
+        graduate request ``rids[i]``'s projected history rows ``rows[i]``
+        (bf16 [P_i, hidden] device tensor; lengths may differ) into its cache
+        after the rows it already holds.  Attention over the cache is causal by
+        position, so this equals graduating the rows tick by tick; it runs
+        ticks of up to ``stride`` graduating rows per request, all requests in
+        the same ticks, and discards their latents.  ``g_cond`` [n, hidden]
+        (or None) is each request's speaker condition, which the cached K/V
+        depend on."""
+        c = self.cfg
+        H = c.hidden
+        rows = [r.to(self.device, torch.bfloat16) for r in rows]
+        done = [0] * len(rids)
+        while True:
+            live = [i for i in range(len(rids)) if done[i] < rows[i].shape[0]]
+            if not live:
+                return
+            live = live[: self.max_requests]
+            n = len(live)
+            ext = torch.zeros(n, c.stride, H, dtype=torch.bfloat16, device=self.device)
+            n_ext = []
+            for j, i in enumerate(live):
+                take = min(c.stride, rows[i].shape[0] - done[i])
+                ext[j, :take] = rows[i][done[i]:done[i] + take]
+                n_ext.append(take)
+                done[i] += take
+            act = torch.zeros(n, H, dtype=torch.bfloat16, device=self.device)
+            noise = torch.zeros(n, c.latent_patch, c.latent_dim, dtype=torch.bfloat16,
+                                device=self.device)
+            g = None if g_cond is None else g_cond[live].to(self.device, torch.bfloat16)
+            self.tick([rids[i] for i in live], noise=noise, act_row=act, ext_rows=ext,
+                      n_extend=n_ext, g_cond=g)
 
     def graph(self, n: int, *, raw_inputs: bool = True, with_g: bool = False) -> "TickGraph":
         """A CUDA graph of one ``dfm_step`` for n requests over static buffers

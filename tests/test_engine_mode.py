@@ -1,0 +1,72 @@
+"""The engine-side drop-in (``fm_accel="b200"``) on duck-typed payloads shaped
+like the reference's DotsSeqState (``engine.py:48-77``): which history rows
+graduate each tick, and the bulk prefill of a backlog (``prime_to``)."""
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from nanovllm_dots_b200 import synthetic as syn
+from nanovllm_dots_b200.engine_mode import B200FMDispatch
+from nanovllm_dots_b200.fm_head import FMRequest
+
+H = syn.BASE.hidden
+
+
+class _FakeHead:
+    """Records the calls the dispatch makes (no GPU)."""
+
+    def __init__(self):
+        self.cfg = syn.BASE
+        self.device = torch.device("cpu")
+        self.requests = {}
+        self.calls = []
+
+    def prime(self, rids, rows, g_cond=None):
+        self.calls.append(("prime", list(rids), [r.shape[0] for r in rows]))
+        for rid, r in zip(rids, rows):
+            self.requests.setdefault(rid, FMRequest(rid)).cache_len += r.shape[0]
+
+    def tick(self, rids, *, noise, act_row, ext_rows, n_extend, g_cond):
+        self.calls.append(("tick", list(rids), list(n_extend)))
+        for rid, e in zip(rids, n_extend):
+            self.requests.setdefault(rid, FMRequest(rid)).cache_len += e
+        return torch.zeros(len(rids), syn.BASE.latent_patch, syn.BASE.latent_dim)
+
+    def release(self, rid):
+        self.requests.pop(rid, None)
+
+
+class _Payload:
+    """Stands in for DotsSeqState (a plain object, so weak references work)."""
+
+    def __init__(self, rows: int, seed: int):
+        g = torch.Generator().manual_seed(seed)
+        seq = torch.randn(1, 400, H, generator=g).to(torch.bfloat16)
+        self.gen_state = SimpleNamespace(fm_sequence=seq, fm_seq_len=rows, fm_null_g_cond=None)
+        self.g_cond = None
+        self.num_steps = syn.BASE.nfe
+
+
+def _payload(rows: int, seed: int):
+    return _Payload(rows, seed)
+
+
+def test_dispatch_graduates_history_and_primes_backlog():
+    head = _FakeHead()
+    d = B200FMDispatch(head)
+    a, b = _payload(1, 0), _payload(100, 1)      # a: first patch; b: 100-row prompt
+    d([a, b])
+    # b's backlog: rows [0, 99) pending; all but the last 17 are bulk-prefilled
+    assert head.calls[0] == ("prime", [id(b)], [99 - 17])
+    assert head.calls[1] == ("tick", [id(a), id(b)], [0, 17])
+    assert head.requests[id(b)].cache_len == 99
+    a.gen_state.fm_seq_len = 18                  # one patch later
+    b.gen_state.fm_seq_len = 117
+    d([a, b])
+    assert head.calls[2] == ("tick", [id(a), id(b)], [17, 17])
+    b.gen_state.fm_seq_len = 50
+    with pytest.raises(RuntimeError, match="shrank"):
+        d([b])

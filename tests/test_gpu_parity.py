@@ -193,3 +193,28 @@ def test_device_error_on_bad_block_table(head):
     with pytest.raises(RuntimeError, match="page"):
         head.check_errors()
     head.check_errors()   # cleared
+
+
+def test_prime_equals_tick_by_tick(head):
+    """Bulk prefill (``prime``) of three patches of history rows leaves the
+    same cache as graduating them over three ticks: the next tick's latents
+    are identical."""
+    cfg = syn.BASE
+    g = torch.Generator().manual_seed(5)
+    rows = (torch.randn(51, cfg.hidden, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    act = (torch.randn(1, cfg.hidden, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    noise = torch.randn(1, cfg.latent_patch, cfg.latent_dim, generator=g).to(torch.bfloat16).to(DEV)
+    for rid in ("pr", "tt"):
+        head.release(rid)
+    head.prime(["pr"], [rows])
+    zero_noise = torch.zeros(1, cfg.latent_patch, cfg.latent_dim, dtype=torch.bfloat16, device=DEV)
+    zero_act = torch.zeros(1, cfg.hidden, dtype=torch.bfloat16, device=DEV)
+    for t in range(3):
+        head.tick(["tt"], noise=zero_noise, act_row=zero_act,
+                  ext_rows=rows[17 * t:17 * t + 17].unsqueeze(0), n_extend=[17])
+    assert head.requests["pr"].cache_len == head.requests["tt"].cache_len == 51
+    a = head.tick(["pr"], noise=noise, act_row=act)
+    b = head.tick(["tt"], noise=noise, act_row=act)
+    head.check_errors()
+    assert torch.isfinite(a.float()).all()
+    assert torch.equal(a, b)
