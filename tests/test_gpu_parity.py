@@ -218,3 +218,18 @@ def test_prime_equals_tick_by_tick(head):
     head.check_errors()
     assert torch.isfinite(a.float()).all()
     assert torch.equal(a, b)
+
+
+def test_long_requests_split_over_attention_units(weights):
+    """Config-4 lengths: a request longer than one attention work unit (4096
+    keys) is split over two units whose partials are merged, next to short
+    requests in the same tick; checked against the oracle."""
+    b = syn.make_batch(3, [247, 2, 60], seed=44)         # 4199, 34 and 1020 cached rows
+    h = B200FMHead(weights, syn.BASE, num_pages=400, max_pages_per_req=270, max_requests=4,
+                   device=DEV)
+    try:
+        out = _run(h, b, ["L0", "L1", "L2"])
+    finally:
+        h.close()
+    ref = O.tick_batch(weights, b, syn.BASE)
+    _assert_close(out, ref, "long split")
