@@ -46,10 +46,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2",
-                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64"],
+                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe"],
                     help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
                          "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
-                         "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool)")
+                         "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool); "
+                         "pe = the patch encoder (the step after the FM head): one batched "
+                         "decode_patch for 64 requests with cfg2's history lengths")
     ap.add_argument("--cpu-sample", type=int, default=64,
                     help="requests in the CPU baseline sample (64 = one whole tick)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -441,6 +443,160 @@ def run_b200(args, rank, world):
     head.close()
 
 
+# --------------------------------------------------------------------------- #
+# Patch encoder (``--workload pe``)                                            #
+# --------------------------------------------------------------------------- #
+PE_METRIC = "patch-encoder xRT (audio-s/s) at conc 64 per GPU"
+
+
+def pe_histories(rank: int) -> list[int]:
+    """History patches per request: cfg2's draw (U{0..120} patches, the same
+    count the FM head's prefix holds), an independent draw per rank."""
+    g = torch.Generator().manual_seed(2 if rank == 0 else 1000 + rank)
+    return torch.randint(0, 121, (64,), generator=g).tolist()
+
+
+def pe_cpu_seconds(w, cfg, hist, idx, patches):
+    from oracle import pe_oracle as PO
+    states = []
+    for i in idx:
+        st = PO.PEState(cfg)
+        g = torch.Generator().manual_seed(77 + i)
+        S = hist[i] * cfg.rows
+        for l in range(cfg.layers):
+            st.k[l] = torch.randn(S, cfg.heads, cfg.head_dim, generator=g) * 0.5
+            st.v[l] = torch.randn(S, cfg.heads, cfg.head_dim, generator=g) * 0.5
+        states.append(st)
+    t0 = time.perf_counter()
+    for j, i in enumerate(idx):
+        PO.decode_patch(w, cfg, states[j], patches[i])
+    return time.perf_counter() - t0
+
+
+def run_pe(args, rank, world):
+    from nanovllm_dots_b200 import synthetic as syn
+    from nanovllm_dots_b200.patch_encoder import B200PatchEncoder
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = syn.PE_BASE
+    hist = pe_histories(rank)
+    n = len(hist)
+    w = syn.make_pe_weights(cfg)
+    pe = B200PatchEncoder(w, cfg, max_batch=n, max_seq_len=256 * cfg.rows, device=dev)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    chunk = 1 << 28
+    for s0 in range(0, pe.pool.numel(), chunk):
+        e = min(pe.pool.numel(), s0 + chunk)
+        pe.pool[s0:e] = (torch.randn(e - s0, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    seq0 = torch.tensor([h * cfg.rows for h in hist], dtype=torch.int32, device=dev)
+    patches = syn.make_pe_patches(n, 1, seed=5 + rank)[0]
+    stream = torch.cuda.current_stream(dev)
+    dg = pe.graph(n)
+    dg.inputs["patches"].copy_(patches.to(dev))
+    pe.seqlens.copy_(seq0)
+
+    def step():
+        pe.seqlens.copy_(seq0)      # every step decodes at the same history lengths
+        dg.replay()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    pe.check_errors()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    pe.check_errors()
+
+    # end to end: pinned host patches and rows in, embeddings out, every step
+    h_patches = patches.contiguous().pin_memory()
+    h_rows = torch.arange(n, dtype=torch.int32).pin_memory()
+    h_out = torch.empty(n, cfg.out_dim, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        dg.inputs["patches"].copy_(h_patches, non_blocking=True)
+        dg.inputs["rows"].copy_(h_rows, non_blocking=True)
+        step()
+        h_out.copy_(dg.out, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record(stream)
+    f1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+    pe.check_errors()
+
+    hbm, tflops, peak_kind = load_peaks()
+    H, F_, Lyr = cfg.hidden, cfg.ffn, cfg.layers
+    kv_bytes = sum((h * cfg.rows + cfg.rows) for h in hist) * Lyr * 2 * H * 2
+    w_bytes = 2 * (Lyr * (4 * H * H + 2 * H * F_) + cfg.out_dim * cfg.rows * H
+                   + H * cfg.latent_dim + 2 * cfg.latent_dim * cfg.latent_dim)
+    flops = 2.0 * n * cfg.rows * Lyr * (4 * H * H + 2 * H * F_) + 2.0 * n * cfg.rows * H * cfg.out_dim
+    achieved = (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        idx = list(range(min(8, n)))
+        secs = pe_cpu_seconds(w, cfg, hist, idx, patches)
+        cpu = {"value": round(len(idx) * AUDIO_S_PER_PATCH / secs, 4), "unit": "audio-s/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{len(idx)} request decode_patch calls of the same workload, fp32 "
+                         f"eager torch on the host, {secs:.2f} s"}
+    value = n * world * AUDIO_S_PER_PATCH / (ms / 1000)
+    if rank == 0:
+        line = {"metric": PE_METRIC, "value": round(value, 2), "unit": "audio-s/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random-init encoder, N(0,1) patches, N(0,0.5^2) cached K/V)",
+                "config": {"workload": "pe", "requests_per_gpu": n,
+                           "mean_history_positions": round(sum(hist) * cfg.rows / n, 1),
+                           "layers": Lyr, "capacity_positions": pe.cap,
+                           "l2": "K/V read per step (~0.8 GB) larger than L2, no flush",
+                           "parallelism": f"request-sharded x{world}"},
+                "e2e": {"value": round(n * world * AUDIO_S_PER_PATCH / (e2e_ms / 1000), 2),
+                        "unit": "audio-s/s",
+                        "h2d_bytes_per_step": h_patches.numel() * 2 + h_rows.numel() * 4,
+                        "d2h_bytes_per_step": h_out.numel() * 2, "ms_per_step": round(e2e_ms, 4)},
+                "gpu_launches": (6 + 7 * Lyr) * args.steps,
+                "roofline": {"kernel": "whole decode call (K/V + weights streamed once)",
+                             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                             "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                             "algorithmic_per_launch": kv_bytes + w_bytes,
+                             "gemm_tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                             "peak_source": f"{peak_kind} (hbm_gbs)"},
+                "clocks": clk.summary(), "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    pe.close()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -453,7 +609,10 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
     try:
-        run_b200(args, rank, world)
+        if args.workload == "pe":
+            run_pe(args, rank, world)
+        else:
+            run_b200(args, rank, world)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

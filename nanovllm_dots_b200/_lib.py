@@ -1,4 +1,5 @@
-"""ctypes binding of ``libdfm.so`` (declarations in ``include/dfm.h``).
+"""ctypes binding of ``libdfm.so`` (declarations in ``include/dfm.h`` for the FM
+head and ``include/dpe.h`` for the patch encoder).
 
 The library is built in-tree by ``nanovllm_dots_b200.build``.  There is no
 fallback: if the shared object is missing or fails to load, every entry point
@@ -18,7 +19,9 @@ DEVERR_BITS = {1: "timeout", 2: "page", 4: "len"}
 
 EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "dfm_read_error",
            "dfm_destroy", "dfm_error_string", "dfm_linear", "dfm_attention_workspace_size",
-           "dfm_paged_attention", "dfm_paged_attention_noalloc")
+           "dfm_paged_attention", "dfm_paged_attention_noalloc",
+           "dpe_create", "dpe_workspace_size", "dpe_pool_bytes", "dpe_decode", "dpe_read_error",
+           "dpe_destroy")
 
 
 class DfmConfig(ctypes.Structure):
@@ -47,6 +50,26 @@ class DfmBatch(ctypes.Structure):
                 ("ext_rows", c_void_p), ("g_cond", c_void_p), ("cache_len", c_void_p),
                 ("n_extend", c_void_p), ("block_table", c_void_p), ("kv_pool", c_void_p),
                 ("out", c_void_p)]
+
+
+class DpeConfig(ctypes.Structure):
+    _fields_ = [("layers", c_int32), ("hidden", c_int32), ("heads", c_int32),
+                ("head_dim", c_int32), ("ffn", c_int32), ("latent_dim", c_int32),
+                ("patch", c_int32), ("out_dim", c_int32), ("max_rows", c_int32),
+                ("max_pages_per_row", c_int32), ("max_batch", c_int32), ("ln_eps", c_float)]
+
+
+PE_WEIGHT_FIELDS = ("conv_w", "conv_b", "in_w", "in_b", "attn_norm", "ffn_norm", "qkv_w", "o_w",
+                    "o_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "out_w", "out_b")
+
+
+class DpeWeights(ctypes.Structure):
+    _fields_ = [(f, c_void_p) for f in PE_WEIGHT_FIELDS]
+
+
+class DpeBatch(ctypes.Structure):
+    _fields_ = [("n", c_int32), ("patches", c_void_p), ("rows", c_void_p), ("seqlens", c_void_p),
+                ("conv_tail", c_void_p), ("kv_pool", c_void_p), ("out", c_void_p)]
 
 
 _lib = None
@@ -88,6 +111,18 @@ def lib() -> ctypes.CDLL:
                                               c_int32, c_int32, c_int32, c_void_p, c_void_p,
                                               c_void_p, c_int32, c_int32, c_void_p, c_void_p]
     L.dfm_paged_attention_noalloc.restype = c_int32
+    L.dpe_create.argtypes = [POINTER(DpeConfig), POINTER(DpeWeights), POINTER(c_void_p)]
+    L.dpe_create.restype = c_int32
+    L.dpe_workspace_size.argtypes = [c_void_p]
+    L.dpe_workspace_size.restype = c_size_t
+    L.dpe_pool_bytes.argtypes = [POINTER(DpeConfig)]
+    L.dpe_pool_bytes.restype = c_size_t
+    L.dpe_decode.argtypes = [c_void_p, POINTER(DpeBatch), c_void_p, c_size_t, c_void_p]
+    L.dpe_decode.restype = c_int32
+    L.dpe_read_error.argtypes = [c_void_p, c_void_p, c_void_p, POINTER(c_uint32)]
+    L.dpe_read_error.restype = c_int32
+    L.dpe_destroy.argtypes = [c_void_p]
+    L.dpe_destroy.restype = c_int32
     _lib = L
     return L
 

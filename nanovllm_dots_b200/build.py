@@ -1,4 +1,5 @@
-"""Build the FM-head shared library (``libdfm.so``) in-tree with nvcc for sm_100a.
+"""Build the shared library (``libdfm.so``: FM head and patch encoder) in-tree
+with nvcc for sm_100a.
 
     python -m nanovllm_dots_b200.build
 
@@ -16,8 +17,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdfm.so")
 SOURCES = ["dfm_api.cu"]
-DEPS = ["dfm_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh"]
-HEADER = os.path.join(os.path.dirname(PKG), "include", "dfm.h")
+DEPS = ["dfm_api.cu", "dpe_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh", "pe.cuh"]
+HEADERS = [os.path.join(os.path.dirname(PKG), "include", h) for h in ("dfm.h", "dpe.h")]
 
 
 def nvcc() -> str:
@@ -39,7 +40,7 @@ def stale() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    deps = [os.path.join(CSRC, d) for d in DEPS] + [HEADER]
+    deps = [os.path.join(CSRC, d) for d in DEPS] + HEADERS
     return any(os.path.getmtime(d) > t for d in deps)
 
 

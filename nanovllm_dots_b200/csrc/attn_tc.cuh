@@ -4,8 +4,11 @@
 // ``cached_fm.py:124-197``), per request with cache length P and n_ext
 // graduating rows:
 //   graduating row j (j < n_ext): keys [0, P + j + 1)
-//   every other row:              keys [0, P + n_ext + 17)
-// softmax(q k^T / 8) v in fp32 with bf16 operands.
+//   every other row:              keys [0, P + n_ext + 34 - ext_slots)
+// softmax(q k^T / 8) v in fp32 with bf16 operands.  The FM head has
+// ext_slots = 17 (the active block of 17 rows sees itself); the patch encoder
+// (``layers.py:210-245``, a causal block of 8 new rows) passes ext_slots = 34
+// and n_ext = 8, so every row is causal.
 //
 // Work unit: (request, chunk of up to 4096 keys, head), units ordered longest
 // request first.  The kernel is persistent: a grid of two CTAs per SM, CTA b
@@ -76,8 +79,8 @@ constexpr int TA_MAX_PAGES = (TA_CH / TA_KT + 1) * (TA_KT / 16);  // pages of on
 constexpr int TA_MAX_ORDER = 256;                  // requests ordered longest-first
 
 struct AttnParams {
-  const __nv_bfloat16* q;    // [n*34, H]
-  __nv_bfloat16* out;        // [n*34, H]
+  const __nv_bfloat16* q;    // [n*q_rows, H]
+  __nv_bfloat16* out;        // [n*q_rows, H]
   float* part_o;             // [n*MC*heads][34][64]
   float* part_ml;            // [n*MC*heads][34][2]
   int* sem;                  // [n*heads] chunk-completion counters (zero between launches)
@@ -86,7 +89,10 @@ struct AttnParams {
   const int* block_table;
   int n, max_pages, num_pages, heads, H, MC;
   int plane_k, plane_v;
-  int ext_slots;             // 17
+  int ext_slots;             // 17 (34: every row is causal, none sees a fixed block)
+  int q_rows;                // rows per request in q and out: 34, or fewer (the patch
+                             // encoder's 8); the 40-row query box then also carries
+                             // the next requests' rows, whose outputs are not written
   uint32_t* err;
 };
 
@@ -368,7 +374,7 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
           if (lane == 0) {
             mbar_arrive_expect_tx(&q_full[ck.seq & 1], TA_Q_BYTES);
             tma_load_2d(sQ + (ck.seq & 1) * TA_Q_BYTES, &tm_q, &q_full[ck.seq & 1], ck.f.h * 64,
-                        ck.f.i * TA_ROWS);
+                        ck.f.i * p.q_rows);
           }
         }
         load_tile(sK + (gk % TA_KSLOTS) * TA_KV_BYTES, &k_full[gk % TA_KSLOTS], ck, p.plane_k);
@@ -637,12 +643,12 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
 #pragma unroll
           for (int q = 0; q < 32; ++q) o[half * 32 + q] = __uint_as_float(o32[q]);
         }
-        if (qrow < TA_ROWS) {
+        if (qrow < TA_ROWS && qrow < p.q_rows) {
           const float L = vals[qrow];
           if (f.nchunks == 1) {
             const float il = L > 0.f ? 1.f / L : 0.f;
             uint4* dst = reinterpret_cast<uint4*>(
-                p.out + (static_cast<size_t>(f.i) * TA_ROWS + qrow) * p.H + f.h * 64);
+                p.out + (static_cast<size_t>(f.i) * p.q_rows + qrow) * p.H + f.h * 64);
 #pragma unroll
             for (int q8 = 0; q8 < 8; ++q8)
               dst[q8] = make_uint4(pack_bf16(o[8 * q8] * il, o[8 * q8 + 1] * il),
@@ -680,7 +686,8 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
         if (*last_flag) {
           __threadfence();
           const size_t base = (static_cast<size_t>(f.i) * p.MC) * p.heads + f.h;
-          for (int w = sw * 32 + lane; w < TA_ROWS * 4; w += 128) {
+          const int rows_out = p.q_rows < TA_ROWS ? p.q_rows : TA_ROWS;
+          for (int w = sw * 32 + lane; w < rows_out * 4; w += 128) {
             const int rr = w >> 2, seg = (w & 3) * 16;
             float M = -INFINITY;
             for (int cc = 0; cc < f.nchunks; ++cc)
@@ -704,7 +711,7 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
             }
             const float il = L > 0.f ? 1.f / L : 0.f;
             uint4* dst = reinterpret_cast<uint4*>(
-                p.out + (static_cast<size_t>(f.i) * TA_ROWS + rr) * p.H + f.h * 64 + seg);
+                p.out + (static_cast<size_t>(f.i) * p.q_rows + rr) * p.H + f.h * 64 + seg);
             dst[0] = make_uint4(pack_bf16(acc[0] * il, acc[1] * il), pack_bf16(acc[2] * il, acc[3] * il),
                                 pack_bf16(acc[4] * il, acc[5] * il), pack_bf16(acc[6] * il, acc[7] * il));
             dst[1] = make_uint4(pack_bf16(acc[8] * il, acc[9] * il), pack_bf16(acc[10] * il, acc[11] * il),

@@ -199,11 +199,13 @@ bool map_out(CUtensorMap* m, void* base, bool f32, uint64_t rows, uint64_t cols,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+constexpr int kActNone = 0, kActGelu = 1, kActSilu = 2;
+
 template <bool F32>
-EpiStoreT<F32> store_t(const float* bias, bool gelu) {
+EpiStoreT<F32> store_t(const float* bias, int act) {
   EpiStoreT<F32> e;
   e.bias = bias;
-  e.gelu = gelu ? 1 : 0;
+  e.act = act;
   return e;
 }
 
@@ -587,6 +589,7 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   ap.H = H;
   ap.MC = hd->mc;
   ap.ext_slots = kStride;
+  ap.q_rows = kSlot;
   ap.err = err;
 
   float* hbuf = f32(hd->ws.h);
@@ -603,7 +606,8 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
                 float* out_scale = nullptr) {
     return launch_pdl(ln_mod_kernel, dim3((M * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp,
                       subp ? sub_plane : size_t{0}, gate, M, map, shift, scale,
-                      static_cast<int>(modw), rows_per_req, out, c.ln_eps, out8, out_scale);
+                      static_cast<int>(modw), rows_per_req, out, c.ln_eps, out8, out_scale,
+                      static_cast<int>(LN_ADALN));
   };
   for (int k = 0; k < NFE; ++k) {
     const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;
@@ -649,10 +653,10 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
       CK(launch_attention(hd->pool, hd->q_att, ap, s));
       // attention out projection -> sub; h += gate_a * sub inside the next LN
       CK(gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, kOutSplit,
-                               store_t<true>(w.o_b + static_cast<size_t>(l) * H, false), err, s));
+                               store_t<true>(w.o_b + static_cast<size_t>(l) * H, kActNone), err, s));
       CK(ln(R, kIdentity, sub, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, xm, fp8 ? xm8 : nullptr,
             xs));
-      auto e1 = store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, true);
+      auto e1 = store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, kActGelu);
       if (fp8) {
         e1.a_scale = xs;
         e1.w_scale = w.fc1_ws + static_cast<size_t>(l) * c.ffn;
@@ -662,7 +666,7 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
         CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1, e1, err, s));
       }
       CK(gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, H, c.ffn, kOutSplit,
-                               store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, false), err, s));
+                               store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, kActNone), err, s));
       pending_gate = mb + 5 * H;
     }
     // final layer on the 16 latent rows of each request (after the last MLP
@@ -699,15 +703,16 @@ int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* Wt,
   if (pair && !map_out(&mo, out, out_f32 != 0, M, N, 1, static_cast<uint64_t>(M) * N * 4))
     return DFM_ERR_CUDA;
   EpiStore e = store(out, N, out_f32 != 0, bias, gelu != 0);
+  const int act = gelu ? kActGelu : kActNone;
   cudaError_t r;
   if (pair && bn == 256 && out_f32)
-    r = gemm2<256, 5>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
+    r = gemm2<256, 5>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, act), nullptr, s);
   else if (pair && bn == 256)
-    r = gemm2<256, 5>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
+    r = gemm2<256, 5>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, act), nullptr, s);
   else if (pair && out_f32)
-    r = gemm2<128, 6>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, gelu), nullptr, s);
+    r = gemm2<128, 6>(ma, mw, mo, M, N, K, 1, store_t<true>(bias, act), nullptr, s);
   else if (pair)
-    r = gemm2<128, 6>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, gelu), nullptr, s);
+    r = gemm2<128, 6>(ma, mw, mo, M, N, K, 1, store_t<false>(bias, act), nullptr, s);
   else if (bn == 256)
     r = gemm<256, 4>(ma, mw, M, N, K, e, nullptr, s);
   else if (bn == 128)
@@ -774,6 +779,7 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
   p.plane_k = plane_k;
   p.plane_v = plane_v;
   p.ext_slots = kStride;
+  p.q_rows = kSlot;
   return launch_attention(pm, qm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
 
@@ -853,5 +859,11 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
   p.plane_k = plane_k;
   p.plane_v = plane_v;
   p.ext_slots = kStride;
+  p.q_rows = kSlot;
   return launch_attention(pm, qm, p, s) == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------- patch encoder
+// The patch encoder's entry points (include/dpe.h) share this translation
+// unit's helpers and kernels.
+#include "dpe_api.cu"

@@ -6,6 +6,8 @@
 
 namespace dfm {
 
+enum LnMode : int { LN_ADALN = 0, LN_AFFINE = 1, LN_NONE = 2 };
+
 // Residual update + adaLN LayerNorm + modulate, one warp per row:
 //   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h; with
 //   sub_plane != 0, sub is the sum of two split-K partials sub[.] + sub[. + sub_plane])
@@ -15,12 +17,18 @@ namespace dfm {
 // residual add of the previous sublayer (``dit.py:102-107``: x + gate * f(x))
 // is applied here, on coalesced rows, instead of in that sublayer's GEMM
 // epilogue.  h is the fp32 residual stream, out the bf16 GEMM operand.
+// `mode` selects the row transform after the residual add:
+//   LN_ADALN   LN(x) * (1 + scale) + shift  (the DiT's modulate)
+//   LN_AFFINE  LN(x) * scale + shift        (nn.LayerNorm with affine, the patch
+//              encoder's attn_norm / ffn_norm, ``patch_encoder.py:34-38``; mod_ld = 0)
+//   LN_NONE    x                            (the residual stream itself)
+// A null gate is a gate of ones (the encoder's plain residual, ``patch_encoder.py:82-86``).
 __global__ void __launch_bounds__(256)
     ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub, size_t sub_plane,
                   const float* __restrict__ gate, int M, RowMap in_map,
                   const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
                   int rows_per_req, __nv_bfloat16* __restrict__ out, float eps,
-                  uint8_t* __restrict__ out8, float* __restrict__ out_scale) {
+                  uint8_t* __restrict__ out8, float* __restrict__ out_scale, int mode) {
   constexpr int H = 1024;
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -45,13 +53,22 @@ __global__ void __launch_bounds__(256)
         const float4 a2 = *reinterpret_cast<const float4*>(sr + sub_plane + col);
         a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
       }
-      const float4 g = *reinterpret_cast<const float4*>(gr + col);
+      const float4 g = gate ? *reinterpret_cast<const float4*>(gr + col)
+                            : make_float4(1.f, 1.f, 1.f, 1.f);
       x[j].x += g.x * a.x;
       x[j].y += g.y * a.y;
       x[j].z += g.z * a.z;
       x[j].w += g.w * a.w;
       *reinterpret_cast<float4*>(hr + col) = x[j];
     }
+  }
+  if (mode == LN_NONE) {
+    __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint2*>(o + j * 128 + lane * 4) =
+          make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
+    return;
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) s += x[j].x + x[j].y + x[j].z + x[j].w;
@@ -65,15 +82,16 @@ __global__ void __launch_bounds__(256)
   const float rstd = rsqrtf(warp_sum(v) * (1.0f / H) + eps);
   const float* sh = shift + req * mod_ld;
   const float* sc = scale + req * mod_ld;
+  const float one = mode == LN_ADALN ? 1.f : 0.f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int col = j * 128 + lane * 4;
     const float4 a = *reinterpret_cast<const float4*>(sh + col);
     const float4 b = *reinterpret_cast<const float4*>(sc + col);
-    x[j].x = (x[j].x - mean) * rstd * (1.f + b.x) + a.x;
-    x[j].y = (x[j].y - mean) * rstd * (1.f + b.y) + a.y;
-    x[j].z = (x[j].z - mean) * rstd * (1.f + b.z) + a.z;
-    x[j].w = (x[j].w - mean) * rstd * (1.f + b.w) + a.w;
+    x[j].x = (x[j].x - mean) * rstd * (one + b.x) + a.x;
+    x[j].y = (x[j].y - mean) * rstd * (one + b.y) + a.y;
+    x[j].z = (x[j].z - mean) * rstd * (one + b.z) + a.z;
+    x[j].w = (x[j].w - mean) * rstd * (one + b.w) + a.w;
   }
   if (out8) {
     // e4m3 row with one fp32 scale per row (row absmax / 448)

@@ -105,7 +105,7 @@ struct EpiStoreT {
   static constexpr int kEpiWarps = 8;
   static constexpr int CW = F32 ? 32 : 64;  // columns per 128-byte line
   const float* bias;
-  int gelu;
+  int act;                         // 0 none, 1 GELU(tanh) (the DiT MLP), 2 SiLU (the patch encoder's)
   const float* a_scale = nullptr;  // FP8 operands: per-row scale of A ...
   const float* w_scale = nullptr;  // ... and per-output-column scale of W
 
@@ -172,9 +172,12 @@ struct EpiStoreT {
 #pragma unroll
         for (int j = 0; j < CW; ++j) v[j] += __shfl_sync(0xffffffffu, bsel[j & 3], (c + j) >> 2);
       }
-      if (gelu) {
+      if (act == 1) {
 #pragma unroll
         for (int j = 0; j < CW; ++j) v[j] = gelu_tanh(v[j]);
+      } else if (act == 2) {
+#pragma unroll
+        for (int j = 0; j < CW; ++j) v[j] = silu(v[j]);
       }
       uint8_t* buf = rowp + (it & 1) * 4096;
       if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
@@ -203,9 +206,11 @@ struct EpiStoreT {
 };
 
 // Fused QKV epilogue.  Output columns [0,H) are q, [H,2H) k, [2H,3H) v, 64
-// per head.  q and k get LayerNorm(head_dim) with affine, then NeoX rotary at
-// the row's position; q goes to q_out, k and v are written into the paged
-// K/V pool at (page = block_table[req][pos/16], row pos%16).
+// per head.  With kNormRope (the FM head) q and k get LayerNorm(head_dim)
+// with affine, then NeoX rotary at the row's position; without it (the patch
+// encoder, whose attention has neither, ``patch_encoder.py:31-32``) they pass
+// through.  q goes to q_out, k and v are written into the paged K/V pool at
+// (page = block_table[req][pos/16], row pos%16).
 //
 // Row layout: request i owns rows [slot*i, slot*(i+1)); the first ext_slots
 // rows are graduating rows (live when j < n_ext[i], position P_i + j), the
@@ -216,7 +221,8 @@ struct EpiStoreT {
 // then copies its 32 rows out through a shared-memory box so that every store
 // instruction writes four whole 128-byte rows instead of 32 scattered
 // 16-byte pieces.
-struct EpiQKV {
+template <bool kNormRope>
+struct EpiQKVT {
   static constexpr int kStageBytes = 4096;  // per epilogue warp: 32 rows x 128 bytes
   static constexpr int kEpiWarps = 4;       // the row state needs the registers
   __nv_bfloat16* q_out;
@@ -282,7 +288,7 @@ struct EpiQKV {
         st.whi = __ldg(reinterpret_cast<const float4*>(w_scale + n0) + 2 * lane + 1);
       }
     }
-    if (n0 < 2 * H) {  // q or k columns: rotary at this row's position
+    if (kNormRope && n0 < 2 * H) {  // q or k columns: rotary at this row's position
       const float2* cs = rope + (st.pos < 0 ? 0 : (st.pos < max_pos ? st.pos : max_pos - 1));
 #pragma unroll
       for (int d = 0; d < 32; ++d) st.cs[d] = __ldg(cs + static_cast<size_t>(d) * max_pos);
@@ -326,7 +332,7 @@ struct EpiQKV {
       else if (sec > 0 && st.page >= 0)
         dst = pool + static_cast<size_t>(sec == 1 ? plane_k : plane_v) * plane_elems +
               (static_cast<size_t>(st.page) * heads + head) * 1024 + (st.pos & 15) * 64;
-      if (dst && sec < 2) {
+      if (kNormRope && dst && sec < 2) {
         // LayerNorm(64) with four partial sums (short dependency chains)
         float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -376,6 +382,8 @@ struct EpiQKV {
     }
   }
 };
+
+using EpiQKV = EpiQKVT<true>;
 
 // MeanFlow update fused into the final projection (N = latent_dim = 64):
 // z[row] += dt * (acc + bias); zb[row] = bf16(z[row]).  Loads are batched per

@@ -227,7 +227,6 @@ class B200FMHead:
         cancel/finish)."""
         self.pages.release(rid)
         self.requests.pop(rid, None)
-        self.requests.pop(rid, None)
 
     # ------------------------------------------------------------- ticks
     def prepare(self, rids, n_extend) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:

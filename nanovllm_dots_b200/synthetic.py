@@ -205,3 +205,91 @@ def time_grid(nfe: int) -> tuple[list[float], list[float]]:
     ts = np.linspace(0.0, 1.0, nfe + 1, dtype=np.float32)
     ts = torch.tensor(ts).to(torch.bfloat16).float().tolist()
     return ts[:-1], [ts[k + 1] - ts[k] for k in range(nfe)]
+
+
+# --------------------------------------------------------------------------- #
+# Patch encoder (the step after the FM head)                                   #
+# --------------------------------------------------------------------------- #
+@dataclasses.dataclass(frozen=True)
+class PEConfig:
+    """Shape of the patch encoder (``VAESemanticEncoder``,
+    ``nanovllm_dots/models/dots/native/patch_encoder.py:139-150``).
+
+    The reference reads these from the checkpoint's config.json, which is not
+    published; the defaults are synthetic choices consistent with the FM head
+    above: the 16-frame latent patch of 64 channels, the causal stride-2
+    downsampling conv (so 8 encoder rows per patch), a 1024-wide encoder with
+    16 heads of 64, FFN 4096, the ``SuperviseEncoder`` default of 6 layers
+    (``patch_encoder.py:99``), and the LLM hidden size 1536 (the FM head's
+    ``cond_dim``) as the output width (``native/loader.py:85-87``).
+    """
+    layers: int = 6
+    hidden: int = 1024
+    heads: int = 16
+    head_dim: int = 64
+    ffn: int = 4096
+    latent_dim: int = 64
+    patch: int = 16
+    in_ds: int = 2
+    out_dim: int = 1536
+    page_rows: int = 16
+    ln_eps: float = 1e-5
+
+    @property
+    def rows(self) -> int:
+        """Encoder rows one patch adds (``out_ds_rate``, ``patch_encoder.py:148``)."""
+        return self.patch // self.in_ds
+
+
+PE_BASE = PEConfig()
+
+
+def make_pe_weights(cfg: PEConfig = PE_BASE, seed: int = 0,
+                    ln_jitter: float = 0.1) -> dict[str, torch.Tensor]:
+    """Seeded patch-encoder weights (fp32 CPU tensors holding bf16 values).
+
+    Modules are created in the reference constructor's order
+    (``patch_encoder.py:142-150``: ds_proj, in_proj, the encoder layers with
+    ``attn`` {q,k,v,o}_proj, ``attn_norm``, ``ffn`` fc1/fc2, ``ffn_norm``
+    (``patch_encoder.py:28-38``, ``layers.py:146-161``), then out_proj) with
+    torch's default initialisation, so the reference module built under the
+    same seed holds the same values.  LayerNorm weights and biases default to
+    1 and 0; they are then jittered (seed + 1) so the affine path is exercised.
+    Keys are the reference state-dict names.
+    """
+    H, F = cfg.hidden, cfg.ffn
+    torch.manual_seed(seed)
+    sd: dict[str, torch.Tensor] = {}
+
+    def put(prefix: str, mod: nn.Module) -> None:
+        for n, p in mod.named_parameters():
+            sd[f"{prefix}.{n}"] = p.detach()
+
+    with torch.no_grad():
+        put("ds_proj", nn.Conv1d(cfg.latent_dim, cfg.latent_dim, cfg.in_ds, stride=cfg.in_ds))
+        put("in_proj", _lin(cfg.latent_dim, H))
+        for l in range(cfg.layers):
+            b = f"encoder.layers.{l}"
+            put(f"{b}.attn.q_proj", _lin(H, H, bias=False))
+            put(f"{b}.attn.k_proj", _lin(H, H, bias=False))
+            put(f"{b}.attn.v_proj", _lin(H, H, bias=False))
+            put(f"{b}.attn.o_proj", _lin(H, H))
+            put(f"{b}.attn_norm", nn.LayerNorm(H))
+            put(f"{b}.ffn.fc1", _lin(H, F))
+            put(f"{b}.ffn.fc2", _lin(F, H))
+            put(f"{b}.ffn_norm", nn.LayerNorm(H))
+        put("out_proj", _lin(H * cfg.rows, cfg.out_dim))
+        g = torch.Generator().manual_seed(seed + 1)
+        for k in sorted(sd):
+            if "_norm." in k:
+                base = 1.0 if k.endswith("weight") else 0.0
+                sd[k] = base + ln_jitter * torch.randn(sd[k].shape, generator=g)
+    return {k: v.to(torch.bfloat16).float() for k, v in sd.items()}
+
+
+def make_pe_patches(n: int, count: int, seed: int, cfg: PEConfig = PE_BASE) -> torch.Tensor:
+    """``count`` successive latent patches for n requests: bf16 [count, n, patch,
+    latent_dim], N(0, 1) (the engine feeds denormalised latents,
+    ``engine.py:750-752``)."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(count, n, cfg.patch, cfg.latent_dim, generator=g).to(torch.bfloat16)

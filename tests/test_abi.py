@@ -1,5 +1,6 @@
 """The C-ABI library builds, loads without a GPU and exports every entry point
-``include/dfm.h`` declares; host-side bookkeeping that needs no GPU."""
+``include/dfm.h`` and ``include/dpe.h`` declare; host-side bookkeeping that
+needs no GPU."""
 from __future__ import annotations
 
 import ctypes
@@ -11,23 +12,30 @@ import torch
 
 from nanovllm_dots_b200 import _lib, build
 from nanovllm_dots_b200.fm_head import PageAllocator, abi_config, pack_weights
-from nanovllm_dots_b200.synthetic import BASE
+from nanovllm_dots_b200.patch_encoder import pack_pe_weights, pe_abi_config
+from nanovllm_dots_b200.synthetic import BASE, PE_BASE, PEConfig, make_pe_weights
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "dfm.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADER = os.path.join(INCLUDE, "dfm.h")
+PE_HEADER = os.path.join(INCLUDE, "dpe.h")
 
 
 def declared_functions():
-    src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(dfm_\w+)\s*\(", src, re.M)))
+    names = set()
+    for path, prefix in ((HEADER, "dfm_"), (PE_HEADER, "dpe_")):
+        src = open(path).read()
+        found = re.findall(rf"^\s*(?:int|size_t|const char\*)\s+({prefix}\w+)\s*\(", src, re.M)
+        assert found, f"no declarations parsed from {path}"
+        names |= set(found)
+    return sorted(names)
 
 
 def test_library_builds_and_exports_every_declared_symbol():
     path = build.build()
     L = ctypes.CDLL(path)
     decl = declared_functions()
-    assert decl, "no declarations parsed from dfm.h"
     for name in decl:
-        assert hasattr(L, name), f"{name} declared in dfm.h but not exported"
+        assert hasattr(L, name), f"{name} declared in include/ but not exported"
     assert set(decl) == set(_lib.EXPORTS)
 
 
@@ -105,3 +113,35 @@ def test_pack_weights_fp8_rowwise(weights):
         assert torch.allclose(deq.abs().amax(-1), w.abs().amax(-1), rtol=1e-6)
     with pytest.raises(ValueError):
         pack_weights(weights, BASE, "cpu", "int4")
+
+
+def test_pe_struct_layouts_and_pool_bytes():
+    src = open(PE_HEADER).read()
+    body = src[src.index("typedef struct DpeWeights"):src.index("} DpeWeights;")]
+    assert len(re.findall(r"const (?:void|float)\*\s+\w+", body)) == len(_lib.PE_WEIGHT_FIELDS)
+    assert ctypes.sizeof(_lib.DpeConfig) == 12 * 4
+    assert ctypes.sizeof(_lib.DpeBatch) == 8 + 6 * 8
+    L = _lib.lib()
+    cfg = pe_abi_config(PE_BASE, max_rows=3, max_pages_per_row=4, max_batch=2)
+    assert L.dpe_pool_bytes(cfg) == 6 * 2 * (3 * 4) * 16 * 16 * 64 * 2
+    w = _lib.DpeWeights()
+    h = ctypes.c_void_p()
+    assert L.dpe_create(cfg, w, h) == 1            # null weight pointers
+    cfg.hidden = 768
+    assert L.dpe_create(cfg, w, h) == 2            # unsupported width
+    assert L.dpe_pool_bytes(cfg) == 0
+    assert L.dpe_decode(None, None, None, 0, None) == 1
+
+
+def test_pack_pe_weights_layout():
+    cfg = PEConfig(layers=2, hidden=128, heads=2, ffn=256, out_dim=192)
+    sd = make_pe_weights(cfg)
+    p = pack_pe_weights(sd, cfg, "cpu")
+    assert set(p) == set(_lib.PE_WEIGHT_FIELDS)
+    assert p["conv_w"].shape == (64, 128) and p["conv_w"].dtype == torch.bfloat16
+    assert torch.equal(p["conv_w"][:, 64:].float(), sd["ds_proj.weight"][:, :, 1])
+    assert p["qkv_w"].shape == (2, 3 * 128, 128)
+    assert torch.equal(p["qkv_w"][1, 256:].float(), sd["encoder.layers.1.attn.v_proj.weight"])
+    assert p["attn_norm"].shape == (2, 2, 128)
+    assert torch.equal(p["ffn_norm"][0, 1], sd["encoder.layers.0.ffn_norm.bias"])
+    assert p["out_w"].shape == (192, 8 * 128)
