@@ -492,6 +492,24 @@ def run_pe(args, rank, world):
     seq0 = torch.tensor([h * cfg.rows for h in hist], dtype=torch.int32, device=dev)
     patches = syn.make_pe_patches(n, 1, seed=5 + rank)[0]
     stream = torch.cuda.current_stream(dev)
+    if args.profile_tick:
+        rows = torch.arange(n, dtype=torch.int32, device=dev)
+        out = torch.empty(n, cfg.out_dim, dtype=torch.bfloat16, device=dev)
+        p_dev = patches.to(dev).contiguous()
+        for prof in (False, True):
+            pe.seqlens.copy_(seq0)
+            if prof:
+                torch.cuda.cudart().cudaProfilerStart()
+            pe.launch(p_dev, rows, out)
+            torch.cuda.synchronize()
+            if prof:
+                torch.cuda.cudart().cudaProfilerStop()
+        pe.check_errors()
+        if rank == 0:
+            print(json.dumps({"profile_tick": True, "workload": "pe", "requests": n,
+                              "launches": 6 + 7 * cfg.layers}), flush=True)
+        pe.close()
+        return
     dg = pe.graph(n)
     dg.inputs["patches"].copy_(patches.to(dev))
     pe.seqlens.copy_(seq0)

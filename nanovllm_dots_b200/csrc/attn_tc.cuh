@@ -528,20 +528,6 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
         ok = __all_sync(0xffffffffu, mbar_wait(&s_empty[sb], (g >> 1) & 1, abort_flag, p.err));
         if (!ok) break;
         const bool need = flags[sb * 4] | flags[sb * 4 + 1] | flags[sb * 4 + 2] | flags[sb * 4 + 3];
-        // the PV product that last read this P buffer must be done before it is rewritten
-        if (g >= TA_PSLOTS) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[g % TA_PSLOTS],
-                                                 ((g / TA_PSLOTS) & 1) ^ 1, abort_flag, p.err));
-          if (!ok) break;
-          tc_fence_after();
-        }
-        if (need && TA_PSLOTS > 1 && t >= 1) {
-          // every earlier PV product of the unit must be done before O is rescaled
-          ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[(g - 1) % TA_PSLOTS],
-                                                 ((g - 1) / TA_PSLOTS) & 1, abort_flag, p.err));
-          if (!ok) break;
-          tc_fence_after();
-        }
         if (need) {
           // new running max: the old one raised by this tile's scores (x + max_old)
           const float* mc = m_s + (ver & 1) * TA_ROWS;
@@ -572,24 +558,10 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
             x[j] = mn[j] == -INFINITY ? -INFINITY : x[j] + (mc[j] - mn[j]);
             l[j] *= vals[j];
           }
-          if (t >= 1 && q4 <= 1) {
-            // rescale this unit's O rows (TMEM lane = query) by their query's factor
-            const int qrow = q4 * 32 + lane;
-            const float a = qrow < TA_ROWS ? vals[qrow] : 1.f;
-            const uint32_t oc = tmem + TA_O_COL + (seq & 1) * 64 + lane_off;
-            uint32_t o32[32];
-#pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-              tmem_ld32(oc + half * 32, o32);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) o32[e] = __float_as_uint(__uint_as_float(o32[e]) * a);
-              tmem_st32(oc + half * 32, o32);
-            }
-            tmem_wait_st();
-          }
         }
-        // probabilities: this key's row of P (queries 0..39), row sums
+        // probabilities: this key's row of P (queries 0..39), row sums.  They
+        // depend only on S and the running max, so they are computed while the
+        // previous tile's PV product may still be running.
         float e[40];
 #pragma unroll
         for (int j = 0; j < TA_ROWS; ++j) {
@@ -598,6 +570,37 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
         }
 #pragma unroll
         for (int j = TA_ROWS; j < 40; ++j) e[j] = 0.f;
+        // the PV product that last read this P buffer (and, for the rescale,
+        // every earlier PV product of the unit) must be done before P is
+        // rewritten and O rescaled
+        if (g >= TA_PSLOTS) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[g % TA_PSLOTS],
+                                                 ((g / TA_PSLOTS) & 1) ^ 1, abort_flag, p.err));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        if (need && TA_PSLOTS > 1 && t >= 1) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[(g - 1) % TA_PSLOTS],
+                                                 ((g - 1) / TA_PSLOTS) & 1, abort_flag, p.err));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        if (need && t >= 1 && q4 <= 1) {
+          // rescale this unit's O rows (TMEM lane = query) by their query's factor
+          const int qrow = q4 * 32 + lane;
+          const float a = qrow < TA_ROWS ? vals[qrow] : 1.f;
+          const uint32_t oc = tmem + TA_O_COL + (seq & 1) * 64 + lane_off;
+          uint32_t o32[32];
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            tmem_ld32(oc + half * 32, o32);
+            tmem_wait_ld();
+#pragma unroll
+            for (int ee = 0; ee < 32; ++ee) o32[ee] = __float_as_uint(__uint_as_float(o32[ee]) * a);
+            tmem_st32(oc + half * 32, o32);
+          }
+          tmem_wait_st();
+        }
 #pragma unroll
         for (int c = 0; c < 5; ++c)
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(

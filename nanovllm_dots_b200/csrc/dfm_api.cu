@@ -222,6 +222,18 @@ EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMa
   return e;
 }
 
+// Residual + LayerNorm launch (ln_mod_kernel: two rows per block).
+template <int NSUB, int MODE>
+cudaError_t launch_ln(cudaStream_t s, int M, float* h, const float* sub, size_t sub_plane,
+                      const float* gate, RowMap map, const float* shift, const float* scale,
+                      int mod_ld, int rows_per_req, __nv_bfloat16* out, float eps, uint8_t* out8,
+                      float* out_scale) {
+  return launch_pdl(ln_mod_kernel<NSUB, MODE>,
+                    dim3((M + LN_ROWS_PER_BLOCK - 1) / LN_ROWS_PER_BLOCK), dim3(LN_THREADS), 0, s,
+                    h, sub, sub_plane, gate, M, map, shift, scale, mod_ld, rows_per_req, out, eps,
+                    out8, out_scale);
+}
+
 int attn_chunks(int max_pages) { return (max_pages * 16 + kSlot + TA_CH - 1) / TA_CH; }
 
 // The attention kernel is persistent: two CTAs per SM (its register bound
@@ -604,10 +616,9 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   auto ln = [&](int M, RowMap map, const float* subp, const float* gate, const float* shift,
                 const float* scale, int rows_per_req, __nv_bfloat16* out, uint8_t* out8 = nullptr,
                 float* out_scale = nullptr) {
-    return launch_pdl(ln_mod_kernel, dim3((M * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp,
-                      subp ? sub_plane : size_t{0}, gate, M, map, shift, scale,
-                      static_cast<int>(modw), rows_per_req, out, c.ln_eps, out8, out_scale,
-                      static_cast<int>(LN_ADALN));
+    return launch_ln<kOutSplit, LN_ADALN>(s, M, hbuf, subp, sub_plane, gate, map, shift, scale,
+                                          static_cast<int>(modw), rows_per_req, out, c.ln_eps,
+                                          out8, out_scale);
   };
   for (int k = 0; k < NFE; ++k) {
     const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;

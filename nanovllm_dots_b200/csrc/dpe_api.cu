@@ -12,6 +12,12 @@ namespace {
 constexpr int kPeRows = PE_ROWS;      // encoder rows per patch (out_ds_rate)
 constexpr int kPeOutBN = 128, kPeOutST = 6;
 constexpr int kPeOutSplit = 8;        // split-K of out_proj (K = 8 * hidden, M = n is small)
+// Calls of at most this many encoder rows (128 requests) run the layer GEMMs
+// on 256 x 128 tiles and the O-projection / fc2 as four split-K partials:
+// at M = 512 the 256 x 256 tiles would give 24-32 work units for 74 SM pairs.
+constexpr int kPeNarrowRows = 1024;
+constexpr int kPeNarrowBN = 128, kPeNarrowST = 6, kPeNarrowSplit = 4;
+constexpr int kPeSubPlanes = 4;
 
 struct PeLayout {
   size_t err, cl, nn, bt, xc, xd, h, sub, xm, qb, ob, u, part_o, part_ml, sem, outp, total;
@@ -28,6 +34,7 @@ struct PeHandle {
   CUtensorMap* m_o;
   CUtensorMap* m_fc1;
   CUtensorMap* m_fc2;
+  CUtensorMap* m_n;   // per layer: qkv, o, fc1, fc2 with box rows kPeNarrowBN / 2
   const void* plan_ws = nullptr;
   const void* plan_pool = nullptr;
   CUtensorMap a_xc, a_xd, a_xm, a_ob, a_u, a_xo, pool, q_att, o_sub, o_u, o_outp;
@@ -49,7 +56,7 @@ PeLayout pe_layout(const DpeConfig& c, int mc) {
   L.xc = take(R * 2 * c.latent_dim * 2);
   L.xd = take(R * c.latent_dim * 2);
   L.h = take(R * H * 4);
-  L.sub = take(2 * R * H * 4);
+  L.sub = take(kPeSubPlanes * R * H * 4);
   L.xm = take(R * H * 2);
   L.qb = take(R * H * 2);
   L.ob = take(R * H * 2);
@@ -90,7 +97,7 @@ bool pe_plan(PeHandle* h, void* ws, void* pool) {
             // the final rows of request i, concatenated: [NR, 8 * H] over xm
             map_2d(&h->a_xo, b + h->ws.xm, NR, kPeRows * H, kPeRows * H, 128) &&
             map_q(&h->q_att, b + h->ws.qb, R, c.heads) &&
-            map_out(&h->o_sub, b + h->ws.sub, true, R, H, 2, R * H * 4) &&
+            map_out(&h->o_sub, b + h->ws.sub, true, R, H, kPeSubPlanes, R * H * 4) &&
             map_out(&h->o_u, b + h->ws.u, false, R, c.ffn, 1, R * c.ffn * 2) &&
             map_out(&h->o_outp, b + h->ws.outp, true, NR, c.out_dim, kPeOutSplit,
                     NR * c.out_dim * 4) &&
@@ -127,6 +134,7 @@ int dpe_destroy(void* handle) {
   delete[] h->m_o;
   delete[] h->m_fc1;
   delete[] h->m_fc2;
+  delete[] h->m_n;
   delete h;
   return DFM_OK;
 }
@@ -158,6 +166,7 @@ int dpe_create(const DpeConfig* cfg, const DpeWeights* w, void** out) {
   h->m_o = new CUtensorMap[L];
   h->m_fc1 = new CUtensorMap[L];
   h->m_fc2 = new CUtensorMap[L];
+  h->m_n = new CUtensorMap[4 * L];
   auto bw = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
   bool ok = map_2d(&h->m_conv, w->conv_w, c.latent_dim, 2 * c.latent_dim, 2 * c.latent_dim, 64) &&
             map_2d(&h->m_in, w->in_w, H, c.latent_dim, c.latent_dim, 128) &&
@@ -168,6 +177,11 @@ int dpe_create(const DpeConfig* cfg, const DpeWeights* w, void** out) {
          map_2d(&h->m_o[l], bw(w->o_w) + l * HH, H, H, H, kOutBN / 2) &&
          map_2d(&h->m_fc1[l], bw(w->fc1_w) + l * HF, c.ffn, H, H, kFc1BN / 2) &&
          map_2d(&h->m_fc2[l], bw(w->fc2_w) + l * HF, H, c.ffn, c.ffn, kOutBN / 2);
+    CUtensorMap* mn = h->m_n + 4 * l;
+    ok = ok && map_2d(&mn[0], bw(w->qkv_w) + l * 3 * HH, 3 * H, H, H, kPeNarrowBN / 2) &&
+         map_2d(&mn[1], bw(w->o_w) + l * HH, H, H, H, kPeNarrowBN / 2) &&
+         map_2d(&mn[2], bw(w->fc1_w) + l * HF, c.ffn, H, H, kPeNarrowBN / 2) &&
+         map_2d(&mn[3], bw(w->fc2_w) + l * HF, H, c.ffn, c.ffn, kPeNarrowBN / 2);
   }
   if (!ok) {
     dpe_destroy(h);
@@ -255,18 +269,33 @@ int dpe_decode(void* handle, const DpeBatch* b, void* workspace, size_t workspac
 
   float* sub = f32(hd->ws.sub);
   __nv_bfloat16* xm = bf(hd->ws.xm);
-  const size_t sub_plane = kOutSplit > 1 ? static_cast<size_t>(kPeRows) * c.max_batch * H : 0;
-  auto ln = [&](const float* subp, const float* norm, int mode) {
-    return launch_pdl(ln_mod_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, s, hbuf, subp,
-                      subp ? sub_plane : size_t{0}, static_cast<const float*>(nullptr), R,
-                      kIdentity, norm ? norm + H : nullptr, norm, 0, kPeRows, xm, c.ln_eps,
-                      static_cast<uint8_t*>(nullptr), static_cast<float*>(nullptr), mode);
+  const size_t sub_plane = static_cast<size_t>(kPeRows) * c.max_batch * H;
+  const bool narrow = R <= kPeNarrowRows;
+  const int nsub = narrow ? kPeNarrowSplit : kOutSplit;
+  // x += the pending sublayer (nsub split-K partials) inside the LayerNorm; norm = the
+  // [weight | bias] pair of an affine LayerNorm, or null for the plain residual rows
+  auto ln = [&](const float* subp, const float* norm) {
+    const float* shift = norm ? norm + H : nullptr;
+    if (norm && nsub == kPeNarrowSplit)
+      return launch_ln<kPeNarrowSplit, LN_AFFINE>(s, R, hbuf, subp, sub_plane, nullptr, kIdentity,
+                                                  shift, norm, 0, kPeRows, xm, c.ln_eps, nullptr,
+                                                  nullptr);
+    if (norm)
+      return launch_ln<kOutSplit, LN_AFFINE>(s, R, hbuf, subp, sub_plane, nullptr, kIdentity,
+                                             shift, norm, 0, kPeRows, xm, c.ln_eps, nullptr,
+                                             nullptr);
+    if (nsub == kPeNarrowSplit)
+      return launch_ln<kPeNarrowSplit, LN_NONE>(s, R, hbuf, subp, sub_plane, nullptr, kIdentity,
+                                                nullptr, nullptr, 0, kPeRows, xm, c.ln_eps,
+                                                nullptr, nullptr);
+    return launch_ln<kOutSplit, LN_NONE>(s, R, hbuf, subp, sub_plane, nullptr, kIdentity, nullptr,
+                                         nullptr, 0, kPeRows, xm, c.ln_eps, nullptr, nullptr);
   };
+
   const size_t plane_elems = static_cast<size_t>(num_pages) * c.heads * 16 * 64;
   for (int l = 0; l < L; ++l) {
     // x += previous MLP (inside the LayerNorm), h = attn_norm(x)
-    CK(ln(l > 0 ? sub : nullptr, w.attn_norm + static_cast<size_t>(l) * 2 * H,
-          static_cast<int>(LN_AFFINE)));
+    CK(ln(l > 0 ? sub : nullptr, w.attn_norm + static_cast<size_t>(l) * 2 * H));
     EpiQKVT<false> eq{};
     eq.q_out = bf(hd->ws.qb);
     eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
@@ -287,22 +316,34 @@ int dpe_decode(void* handle, const DpeBatch* b, void* workspace, size_t workspac
     eq.max_pos = 1;
     eq.eps = c.ln_eps;
     eq.err = err;
-    CK(gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s));
+    const CUtensorMap* mn = hd->m_n + 4 * l;
+    const auto e_o = store_t<true>(w.o_b + static_cast<size_t>(l) * H, kActNone);
+    const auto e_fc1 = store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, kActSilu);
+    const auto e_fc2 = store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, kActNone);
+    if (narrow)
+      CK((gemm2<kPeNarrowBN, kPeNarrowST>(hd->a_xm, mn[0], hd->a_xm, R, 3 * H, H, 1, eq, err, s)));
+    else
+      CK(gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s));
     ap.plane_k = eq.plane_k;
     ap.plane_v = eq.plane_v;
     CK(launch_attention(hd->pool, hd->q_att, ap, s));
-    CK(gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, kOutSplit,
-                             store_t<true>(w.o_b + static_cast<size_t>(l) * H, kActNone), err, s));
+    if (narrow)
+      CK((gemm2<kPeNarrowBN, kPeNarrowST>(hd->a_ob, mn[1], hd->o_sub, R, H, H, nsub, e_o, err, s)));
+    else
+      CK(gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, nsub, e_o, err, s));
     // x += attention (inside the LayerNorm), h = ffn_norm(x)
-    CK(ln(sub, w.ffn_norm + static_cast<size_t>(l) * 2 * H, static_cast<int>(LN_AFFINE)));
-    CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1,
-                             store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, kActSilu),
-                             err, s));
-    CK(gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, H, c.ffn, kOutSplit,
-                             store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, kActNone), err, s));
+    CK(ln(sub, w.ffn_norm + static_cast<size_t>(l) * 2 * H));
+    if (narrow) {
+      CK((gemm2<kPeNarrowBN, kPeNarrowST>(hd->a_xm, mn[2], hd->o_u, R, c.ffn, H, 1, e_fc1, err, s)));
+      CK((gemm2<kPeNarrowBN, kPeNarrowST>(hd->a_u, mn[3], hd->o_sub, R, H, c.ffn, nsub, e_fc2, err,
+                                          s)));
+    } else {
+      CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1, e_fc1, err, s));
+      CK(gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, H, c.ffn, nsub, e_fc2, err, s));
+    }
   }
   // x += last MLP; the bf16 rows, 8 per request, are out_proj's [n, 8H] operand
-  CK(ln(sub, nullptr, static_cast<int>(LN_NONE)));
+  CK(ln(sub, nullptr));
   CK(gemm2<kPeOutBN, kPeOutST>(hd->a_xo, hd->m_out, hd->o_outp, n, c.out_dim, kPeRows * H,
                                kPeOutSplit, store_t<true>(w.out_b, kActNone), err, s));
   const int cnt = n * c.out_dim / 4;

@@ -7,114 +7,146 @@
 namespace dfm {
 
 enum LnMode : int { LN_ADALN = 0, LN_AFFINE = 1, LN_NONE = 2 };
+constexpr int LN_ROWS_PER_BLOCK = 2;
+constexpr int LN_THREADS = 128 * LN_ROWS_PER_BLOCK;
 
-// Residual update + adaLN LayerNorm + modulate, one warp per row:
-//   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h; with
-//   sub_plane != 0, sub is the sum of two split-K partials sub[.] + sub[. + sub_plane])
+// Residual update + adaLN LayerNorm + modulate, one row per 128 threads:
+//   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h; sub is
+//   the sum of NSUB split-K partial planes sub[. + p * sub_plane], p < NSUB)
 //   out[r] = LN(x) * (1 + scale[req]) + shift[req],   req = r / rows_per_req
 //   (bf16; or, with out8, e4m3 values out8[r] with out[r] = out8[r] * out_scale[r])
 // LayerNorm without affine over H = 1024 (``native/dit.py:70-71,19-20``).  The
 // residual add of the previous sublayer (``dit.py:102-107``: x + gate * f(x))
 // is applied here, on coalesced rows, instead of in that sublayer's GEMM
 // epilogue.  h is the fp32 residual stream, out the bf16 GEMM operand.
-// `mode` selects the row transform after the residual add:
+// MODE selects the row transform after the residual add:
 //   LN_ADALN   LN(x) * (1 + scale) + shift  (the DiT's modulate)
 //   LN_AFFINE  LN(x) * scale + shift        (nn.LayerNorm with affine, the patch
 //              encoder's attn_norm / ffn_norm, ``patch_encoder.py:34-38``; mod_ld = 0)
 //   LN_NONE    x                            (the residual stream itself)
-// A null gate is a gate of ones (the encoder's plain residual, ``patch_encoder.py:82-86``).
-__global__ void __launch_bounds__(256)
+// Only LN_ADALN reads a gate; the others add sub with a gate of ones (the
+// encoder's plain residual, ``patch_encoder.py:82-86``).
+template <int NSUB, int MODE>
+__global__ void __launch_bounds__(LN_THREADS)
     ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub, size_t sub_plane,
                   const float* __restrict__ gate, int M, RowMap in_map,
                   const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
                   int rows_per_req, __nv_bfloat16* __restrict__ out, float eps,
-                  uint8_t* __restrict__ out8, float* __restrict__ out_scale, int mode) {
+                  uint8_t* __restrict__ out8, float* __restrict__ out_scale) {
+  // 128 threads (4 warps) per row, two rows per block: thread t of a row owns
+  // the 16-byte column groups t and t + 128 (each warp's accesses are 512
+  // contiguous bytes), and the shift / scale vectors are loaded with the row.
+  // One warp per row left the kernel latency-bound (few warps per SM, each
+  // waiting on its own chain of loads).
   constexpr int H = 1024;
-  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  __shared__ float red[LN_ROWS_PER_BLOCK][3][4];   // [row][sum | centred squares | absmax][warp]
+  const int rb = threadIdx.x >> 7;
+  const int t = threadIdx.x & 127;
+  const int w = t >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * LN_ROWS_PER_BLOCK + rb;
   pdl_trigger();
   pdl_wait();
-  if (r >= M) return;
-  const size_t hrow = static_cast<size_t>(in_map(r)) * H;
-  const size_t req = static_cast<size_t>(r / rows_per_req);
+  const bool valid = r < M;
+  const size_t hrow = valid ? static_cast<size_t>(in_map(r)) * H : 0;
+  const size_t req = valid ? static_cast<size_t>(r / rows_per_req) : 0;
   float* hr = h + hrow;
-  float4 x[8];
-  float s = 0.f;
+  float4 x[2], a_sh[2], b_sc[2];
+  constexpr bool norm = MODE != LN_NONE;
+  if (valid) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = *reinterpret_cast<const float4*>(hr + j * 128 + lane * 4);
-  if (sub) {
-    const float* sr = sub + hrow;
-    const float* gr = gate + req * mod_ld;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = j * 128 + lane * 4;
-      float4 a = *reinterpret_cast<const float4*>(sr + col);
-      if (sub_plane) {  // split-K: the second partial sum
-        const float4 a2 = *reinterpret_cast<const float4*>(sr + sub_plane + col);
-        a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
+    for (int j = 0; j < 2; ++j) {
+      const int col = j * 512 + t * 4;
+      x[j] = *reinterpret_cast<const float4*>(hr + col);
+      if constexpr (norm) {   // the modulation / affine vectors, loaded before they are needed
+        a_sh[j] = *reinterpret_cast<const float4*>(shift + req * mod_ld + col);
+        b_sc[j] = *reinterpret_cast<const float4*>(scale + req * mod_ld + col);
       }
-      const float4 g = gate ? *reinterpret_cast<const float4*>(gr + col)
-                            : make_float4(1.f, 1.f, 1.f, 1.f);
-      x[j].x += g.x * a.x;
-      x[j].y += g.y * a.y;
-      x[j].z += g.z * a.z;
-      x[j].w += g.w * a.w;
-      *reinterpret_cast<float4*>(hr + col) = x[j];
     }
+    if (sub) {
+      const float* sr = sub + hrow;
+      const float* gr = gate + req * mod_ld;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int col = j * 512 + t * 4;
+        float4 a = *reinterpret_cast<const float4*>(sr + col);
+#pragma unroll
+        for (int p = 1; p < NSUB; ++p) {  // split-K: the other partial sums
+          const float4 a2 = *reinterpret_cast<const float4*>(sr + p * sub_plane + col);
+          a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
+        }
+        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
+        if constexpr (MODE == LN_ADALN) g = *reinterpret_cast<const float4*>(gr + col);
+        x[j].x += g.x * a.x;
+        x[j].y += g.y * a.y;
+        x[j].z += g.z * a.z;
+        x[j].w += g.w * a.w;
+        *reinterpret_cast<float4*>(hr + col) = x[j];
+      }
+    }
+  } else {
+    x[0] = x[1] = a_sh[0] = a_sh[1] = b_sc[0] = b_sc[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if (mode == LN_NONE) {
+  if constexpr (!norm) {
+    if (valid) {
+      __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        *reinterpret_cast<uint2*>(o + j * 512 + t * 4) =
+            make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
+    }
+  } else {
+    float s = (x[0].x + x[0].y) + (x[0].z + x[0].w) + (x[1].x + x[1].y) + (x[1].z + x[1].w);
+    s = warp_sum(s);
+    if (lane == 0) red[rb][0][w] = s;
+    __syncthreads();
+    const float mean = ((red[rb][0][0] + red[rb][0][1]) + (red[rb][0][2] + red[rb][0][3])) * (1.0f / H);
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float a = x[j].x - mean, b = x[j].y - mean, c = x[j].z - mean, d = x[j].w - mean;
+      v += a * a + b * b + c * c + d * d;
+    }
+    v = warp_sum(v);
+    if (lane == 0) red[rb][1][w] = v;
+    __syncthreads();
+    const float var = ((red[rb][1][0] + red[rb][1][1]) + (red[rb][1][2] + red[rb][1][3])) * (1.0f / H);
+    const float rstd = rsqrtf(var + eps);
+    constexpr float one = MODE == LN_ADALN ? 1.f : 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      x[j].x = (x[j].x - mean) * rstd * (one + b_sc[j].x) + a_sh[j].x;
+      x[j].y = (x[j].y - mean) * rstd * (one + b_sc[j].y) + a_sh[j].y;
+      x[j].z = (x[j].z - mean) * rstd * (one + b_sc[j].z) + a_sh[j].z;
+      x[j].w = (x[j].w - mean) * rstd * (one + b_sc[j].w) + a_sh[j].w;
+    }
+    if (out8) {
+      // e4m3 row with one fp32 scale per row (row absmax / 448)
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(x[j].x), fabsf(x[j].y)), fmaxf(fabsf(x[j].z), fabsf(x[j].w))));
+      m = warp_max(m);
+      if (lane == 0) red[rb][2][w] = m;
+      __syncthreads();
+      m = fmaxf(fmaxf(red[rb][2][0], red[rb][2][1]), fmaxf(red[rb][2][2], red[rb][2][3]));
+      if (!valid) return;
+      const float sc = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
+      const float inv = 1.0f / sc;
+      uint8_t* o8 = out8 + static_cast<size_t>(r) * H;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        *reinterpret_cast<uint32_t*>(o8 + j * 512 + t * 4) =
+            pack_e4m3x4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
+      if (t == 0) out_scale[r] = sc;
+      return;
+    }
+    if (!valid) return;
     __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<uint2*>(o + j * 128 + lane * 4) =
+    for (int j = 0; j < 2; ++j)
+      *reinterpret_cast<uint2*>(o + j * 512 + t * 4) =
           make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
-    return;
   }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) s += x[j].x + x[j].y + x[j].z + x[j].w;
-  const float mean = warp_sum(s) * (1.0f / H);
-  float v = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float a = x[j].x - mean, b = x[j].y - mean, c = x[j].z - mean, d = x[j].w - mean;
-    v += a * a + b * b + c * c + d * d;
-  }
-  const float rstd = rsqrtf(warp_sum(v) * (1.0f / H) + eps);
-  const float* sh = shift + req * mod_ld;
-  const float* sc = scale + req * mod_ld;
-  const float one = mode == LN_ADALN ? 1.f : 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int col = j * 128 + lane * 4;
-    const float4 a = *reinterpret_cast<const float4*>(sh + col);
-    const float4 b = *reinterpret_cast<const float4*>(sc + col);
-    x[j].x = (x[j].x - mean) * rstd * (one + b.x) + a.x;
-    x[j].y = (x[j].y - mean) * rstd * (one + b.y) + a.y;
-    x[j].z = (x[j].z - mean) * rstd * (one + b.z) + a.z;
-    x[j].w = (x[j].w - mean) * rstd * (one + b.w) + a.w;
-  }
-  if (out8) {
-    // e4m3 row with one fp32 scale per row (row absmax / 448)
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(x[j].x), fabsf(x[j].y)), fmaxf(fabsf(x[j].z), fabsf(x[j].w))));
-    m = warp_max(m);
-    const float s = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
-    const float inv = 1.0f / s;
-    uint8_t* o8 = out8 + static_cast<size_t>(r) * H;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<uint32_t*>(o8 + j * 128 + lane * 4) =
-          pack_e4m3x4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
-    if (lane == 0) out_scale[r] = s;
-    return;
-  }
-  __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    *reinterpret_cast<uint2*>(o + j * 128 + lane * 4) =
-        make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
 }
 
 constexpr int EMB_MAX_STEPS = 8;

@@ -136,3 +136,25 @@ def install(engine, head: B200FMHead) -> B200FMDispatch:
     engine.fm_accel = "b200"
     engine._batched_fm = dispatch
     return dispatch
+
+
+def install_patch_encoder(engine, pe) -> None:
+    """Route the engine's batched patch encoder through ``B200PatchEncoder``.
+
+    The reference engine (``flash_pe=True``, ``engine.py:197-222``) keeps a
+    ``FlashPatchEncoder`` in ``engine._flash_pe`` and a free list of its cache
+    rows in ``engine._pe_free``; it calls ``reset_rows(rows)`` when a request
+    claims a row, ``prefill(prompt_latents, row)`` for a voice-clone prompt
+    (``engine.py:392-405``) and ``decode_patch(patches, rows)`` once per tick
+    for every request that emitted a patch (``engine.py:743-765``).
+    ``B200PatchEncoder`` has the same three methods with the same arguments and
+    results, so installing it is an attribute swap.  Install before the first
+    request is admitted: the free list is rebuilt over the encoder's rows.
+    """
+    for name in ("decode_patch", "prefill", "reset_rows"):
+        if not callable(getattr(pe, name, None)):
+            raise TypeError(f"patch encoder lacks {name}()")
+    engine.flash_pe = True
+    engine._flash_pe = pe
+    engine._pe_max_batch = pe.max_rows
+    engine._pe_free = list(range(pe.max_rows))

@@ -70,3 +70,33 @@ def test_dispatch_graduates_history_and_primes_backlog():
     b.gen_state.fm_seq_len = 50
     with pytest.raises(RuntimeError, match="shrank"):
         d([b])
+
+
+def test_install_patch_encoder_swaps_the_engine_encoder():
+    from nanovllm_dots_b200.engine_mode import install_patch_encoder
+
+    class _FakePE:
+        max_rows = 5
+
+        def decode_patch(self, patches, rows):
+            return torch.zeros(patches.shape[0], 1, 8)
+
+        def prefill(self, prompt_latents, row):
+            return torch.zeros(1, prompt_latents.shape[1] // 16, 8)
+
+        def reset_rows(self, rows):
+            pass
+
+    eng = SimpleNamespace(flash_pe=False)
+    pe = _FakePE()
+    install_patch_encoder(eng, pe)
+    assert eng.flash_pe and eng._flash_pe is pe
+    assert eng._pe_free == [0, 1, 2, 3, 4] and eng._pe_max_batch == 5
+    with pytest.raises(TypeError, match="decode_patch"):
+        install_patch_encoder(eng, SimpleNamespace(max_rows=1))
+
+
+def test_patch_encoder_has_no_cpu_path():
+    from nanovllm_dots_b200.patch_encoder import B200PatchEncoder
+    with pytest.raises(RuntimeError, match="CUDA"):
+        B200PatchEncoder({}, syn.PE_BASE, max_batch=1, max_seq_len=16, device="cpu")

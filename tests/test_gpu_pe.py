@@ -144,3 +144,23 @@ def test_full_row_reports_length_error(pe):
     with pytest.raises(RuntimeError, match="len"):
         pe.check_errors()
     pe.reset_rows([7])
+
+
+def test_large_batch_wide_tiles():
+    """136 requests in one call (1088 encoder rows, past the small-call
+    threshold): the layer GEMMs take the 256 x 256 tiles with two split-K
+    partials; rows in a shuffled order."""
+    w = _weights()
+    n = 136
+    enc = B200PatchEncoder(w, CFG, max_batch=n, max_seq_len=256, device=DEV)
+    try:
+        rows = torch.randperm(n, generator=torch.Generator().manual_seed(3)).tolist()
+        states = [PO.PEState(CFG) for _ in range(n)]
+        patches = syn.make_pe_patches(n, 2, seed=50)
+        for p in range(2):
+            got = enc.decode_patch(patches[p], rows)
+            enc.check_errors()
+            ref = PO.decode_batch(w, CFG, states, patches[p])
+            _check(got[:, 0], ref, f"wide patch {p}")
+    finally:
+        enc.close()
