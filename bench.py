@@ -46,12 +46,14 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2",
-                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe"],
+                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe", "llmattn"],
                     help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
                          "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool); "
                          "pe = the patch encoder (the step after the FM head): one batched "
-                         "decode_patch for 64 requests with cfg2's history lengths")
+                         "decode_patch for 64 requests with cfg2's history lengths; "
+                         "llmattn = the LLM backbone's paged decode attention (one layer, 64 "
+                         "sequences, Qwen2 GQA 12/2 x 128)")
     ap.add_argument("--cpu-sample", type=int, default=64,
                     help="requests in the CPU baseline sample (64 = one whole tick)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -615,6 +617,100 @@ def run_pe(args, rank, world):
     pe.close()
 
 
+# --------------------------------------------------------------------------- #
+# LLM decode attention (``--workload llmattn``)                                #
+# --------------------------------------------------------------------------- #
+LLM_METRIC = "LLM paged decode attention: layer-steps/s (64 sequences)"
+
+
+def run_llmattn(args, rank, world):
+    from nanovllm_dots_b200.llm_attention import B200DecodeAttention
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    H, KVH, D, bs = 12, 2, 128, 256
+    g = torch.Generator().manual_seed(11 + rank)
+    n = 64
+    # contexts: text prompt (~U{100..300} tokens) + one token per generated patch
+    # (cfg2's U{0..120} history patches)
+    ctx = (torch.randint(100, 301, (n,), generator=g) + torch.randint(0, 121, (n,), generator=g)
+           + 1).tolist()
+    nblk = [(c + bs - 1) // bs for c in ctx]
+    width = max(nblk)
+    num_blocks = sum(nblk)
+    table = torch.full((n, width), -1, dtype=torch.int32)
+    perm = torch.randperm(num_blocks, generator=g)
+    o = 0
+    for i, b in enumerate(nblk):
+        table[i, :b] = perm[o:o + b].to(torch.int32)
+        o += b
+    kc = (torch.randn(num_blocks, bs, KVH, D, device=dev) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(num_blocks, bs, KVH, D, device=dev) * 0.5).to(torch.bfloat16)
+    q = torch.randn(n, H, D, device=dev).to(torch.bfloat16)
+    k = torch.randn(n, KVH, D, device=dev).to(torch.bfloat16)
+    v = torch.randn(n, KVH, D, device=dev).to(torch.bfloat16)
+    slot = torch.tensor([int(table[i, (c - 1) // bs]) * bs + (c - 1) % bs for i, c in enumerate(ctx)],
+                        dtype=torch.int32, device=dev)
+    cl = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    td = table.to(dev)
+    dec = B200DecodeAttention(H, D, D ** -0.5, KVH, max_batch=n, max_blocks=width, device=dev)
+    out = torch.empty(n, H, D, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    # the per-layer caches of a 28-layer backbone do not fit in L2; cycle over
+    # enough copies of the pool that every call reads from HBM
+    copies = max(2, math.ceil(4 * 126e6 / (kc.numel() * 4)))
+    pools = [(kc, vc)] + [(kc.clone(), vc.clone()) for _ in range(copies - 1)]
+
+    def step(j):
+        a, b = pools[j % copies]
+        dec.decode(q, k, v, a, b, slot, cl, td, out=out)
+
+    for j in range(max(args.warmup, 3)):
+        step(j)
+    torch.cuda.synchronize()
+    dec.check_errors()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for j in range(args.steps):
+            step(j)
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    dec.check_errors()
+    hbm, _, peak_kind = load_peaks()
+    kv_bytes = sum(ctx) * KVH * D * 2 * 2
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import llm_attn_oracle as LO
+        idx = list(range(8))
+        kcc, vcc = kc.cpu(), vc.cpu()
+        t0 = time.perf_counter()
+        LO.decode_attention(q[idx].cpu(), kcc, vcc, cl[idx].cpu(), table[idx].tolist(), D ** -0.5)
+        secs = time.perf_counter() - t0
+        cpu = {"value": round(len(idx) / n / secs, 3), "unit": "layer-steps/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{len(idx)} of the {n} sequences, fp32 eager torch, {secs:.3f} s"}
+    if rank == 0:
+        line = {"metric": LLM_METRIC, "value": round(1000.0 / ms, 1), "unit": "layer-steps/s",
+                "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (N(0,1) q, N(0,0.5^2) cache)",
+                "config": {"workload": "llmattn", "sequences": n, "heads": H, "kv_heads": KVH,
+                           "head_dim": D, "block_size": bs,
+                           "mean_context": round(sum(ctx) / n, 1),
+                           "l2": f"{copies} cache copies cycled (each call reads from HBM)"},
+                "gpu_launches": 3 * args.steps,
+                "roofline": {"kernel": "llm_decode_attn_kernel + store + combine", "bound": "hbm",
+                             "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(achieved / hbm, 4), "traffic": None,
+                             "algorithmic_per_launch": kv_bytes,
+                             "peak_source": f"{peak_kind} (hbm_gbs)"},
+                "clocks": clk.summary(), "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -629,6 +725,8 @@ def main():
     try:
         if args.workload == "pe":
             run_pe(args, rank, world)
+        elif args.workload == "llmattn":
+            run_llmattn(args, rank, world)
         else:
             run_b200(args, rank, world)
     finally:

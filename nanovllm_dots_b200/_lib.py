@@ -1,5 +1,6 @@
 """ctypes binding of ``libdfm.so`` (declarations in ``include/dfm.h`` for the FM
-head and ``include/dpe.h`` for the patch encoder).
+head, ``include/dpe.h`` for the patch encoder and ``include/dllm.h`` for the LLM
+decode attention).
 
 The library is built in-tree by ``nanovllm_dots_b200.build``.  There is no
 fallback: if the shared object is missing or fails to load, every entry point
@@ -21,7 +22,7 @@ EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "df
            "dfm_destroy", "dfm_error_string", "dfm_linear", "dfm_attention_workspace_size",
            "dfm_paged_attention", "dfm_paged_attention_noalloc",
            "dpe_create", "dpe_workspace_size", "dpe_pool_bytes", "dpe_decode", "dpe_read_error",
-           "dpe_destroy")
+           "dpe_destroy", "dllm_decode_workspace_size", "dllm_decode_attention", "dllm_read_error")
 
 
 class DfmConfig(ctypes.Structure):
@@ -123,6 +124,13 @@ def lib() -> ctypes.CDLL:
     L.dpe_read_error.restype = c_int32
     L.dpe_destroy.argtypes = [c_void_p]
     L.dpe_destroy.restype = c_int32
+    L.dllm_decode_workspace_size.argtypes = [c_int32] * 5
+    L.dllm_decode_workspace_size.restype = c_size_t
+    L.dllm_decode_attention.argtypes = ([c_void_p] * 8 + [c_int32] * 7
+                                        + [c_float, c_void_p, c_void_p, c_size_t, c_void_p])
+    L.dllm_decode_attention.restype = c_int32
+    L.dllm_read_error.argtypes = [c_void_p, c_void_p, POINTER(c_uint32)]
+    L.dllm_read_error.restype = c_int32
     _lib = L
     return L
 

@@ -1,4 +1,5 @@
-"""Build the shared library (``libdfm.so``: FM head and patch encoder) in-tree
+"""Build the shared library (``libdfm.so``: FM head, patch encoder, LLM decode
+attention) in-tree
 with nvcc for sm_100a.
 
     python -m nanovllm_dots_b200.build
@@ -17,8 +18,9 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdfm.so")
 SOURCES = ["dfm_api.cu"]
-DEPS = ["dfm_api.cu", "dpe_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh", "pe.cuh"]
-HEADERS = [os.path.join(os.path.dirname(PKG), "include", h) for h in ("dfm.h", "dpe.h")]
+DEPS = ["dfm_api.cu", "dpe_api.cu", "llm_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh",
+        "pe.cuh", "llm_attn.cuh"]
+HEADERS = [os.path.join(os.path.dirname(PKG), "include", h) for h in ("dfm.h", "dpe.h", "dllm.h")]
 
 
 def nvcc() -> str:

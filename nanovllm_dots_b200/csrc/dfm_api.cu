@@ -878,3 +878,7 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
 // The patch encoder's entry points (include/dpe.h) share this translation
 // unit's helpers and kernels.
 #include "dpe_api.cu"
+
+// ---------------------------------------------------------------- LLM decode attention
+// The LLM backbone's paged decode attention (include/dllm.h) shares them too.
+#include "llm_api.cu"

@@ -1,6 +1,6 @@
 """The C-ABI library builds, loads without a GPU and exports every entry point
-``include/dfm.h`` and ``include/dpe.h`` declare; host-side bookkeeping that
-needs no GPU."""
+``include/dfm.h``, ``include/dpe.h`` and ``include/dllm.h`` declare; host-side
+bookkeeping that needs no GPU."""
 from __future__ import annotations
 
 import ctypes
@@ -18,11 +18,12 @@ from nanovllm_dots_b200.synthetic import BASE, PE_BASE, PEConfig, make_pe_weight
 INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
 HEADER = os.path.join(INCLUDE, "dfm.h")
 PE_HEADER = os.path.join(INCLUDE, "dpe.h")
+LLM_HEADER = os.path.join(INCLUDE, "dllm.h")
 
 
 def declared_functions():
     names = set()
-    for path, prefix in ((HEADER, "dfm_"), (PE_HEADER, "dpe_")):
+    for path, prefix in ((HEADER, "dfm_"), (PE_HEADER, "dpe_"), (LLM_HEADER, "dllm_")):
         src = open(path).read()
         found = re.findall(rf"^\s*(?:int|size_t|const char\*)\s+({prefix}\w+)\s*\(", src, re.M)
         assert found, f"no declarations parsed from {path}"
@@ -145,3 +146,18 @@ def test_pack_pe_weights_layout():
     assert p["attn_norm"].shape == (2, 2, 128)
     assert torch.equal(p["ffn_norm"][0, 1], sd["encoder.layers.0.ffn_norm.bias"])
     assert p["out_w"].shape == (192, 8 * 128)
+
+
+def test_llm_decode_attention_rejects_bad_arguments_without_a_gpu():
+    L = _lib.lib()
+    assert L.dllm_decode_workspace_size(4, 12, 128, 8, 256) > 0
+    assert L.dllm_decode_workspace_size(4, 12, 96, 8, 256) == 0        # head_dim
+    args = [None] * 8 + [1, 12, 2, 128, 4, 256, 4, 0.088, None, None, 0, None]
+    assert L.dllm_decode_attention(*args) == 1                           # null pointers
+    x = ctypes.c_void_p(256)   # never dereferenced: validation fails first
+    bad_g = [x, None, None, x, x, None, x, x, 1, 18, 2, 128, 4, 256, 4, 0.088, x, x, 1 << 20, None]
+    assert L.dllm_decode_attention(*bad_g) == 2                          # 9 query heads per kv head
+    bad_bs = [x, None, None, x, x, None, x, x, 1, 12, 2, 128, 4, 100, 4, 0.088, x, x, 1 << 20, None]
+    assert L.dllm_decode_attention(*bad_bs) == 2                         # block_size not a multiple of 64
+    small = [x, None, None, x, x, None, x, x, 1, 12, 2, 128, 4, 256, 4, 0.088, x, x, 16, None]
+    assert L.dllm_decode_attention(*small) == 4                          # workspace too small
