@@ -47,11 +47,16 @@ struct LlmAttnSmem {
   static constexpr int OFF_V = OFF_K + LA_NBUF * TILE_BYTES; // [LA_NBUF] V buffers
   static constexpr int OFF_Q = OFF_V + LA_NBUF * TILE_BYTES; // float [LA_MAXG][D]
   static constexpr int OFF_S = OFF_Q + LA_MAXG * D * 4;      // float [2][LA_MAXG][LA_SUB]
-  static constexpr int OFF_P = OFF_S + 2 * LA_MAXG * LA_SUB * 4;  // float [LA_MAXG][LA_SUB]
-  static constexpr int OFF_ML = OFF_P + LA_MAXG * LA_SUB * 4;     // float [3][LA_MAXG]: m, l, alpha
+  // P [LA_MAXG][LA_SUB] overlays the first half of the score partials: each
+  // softmax lane writes the probabilities of the keys whose scores it read
+  static constexpr int OFF_P = OFF_S;
+  static constexpr int OFF_ML = OFF_S + 2 * LA_MAXG * LA_SUB * 4; // float [3][LA_MAXG]: m, l, alpha
   static constexpr int OFF_BAR = OFF_ML + 3 * LA_MAXG * 4 + 32;   // uint64 [LA_NBUF] + abort flag
   static constexpr int BYTES = OFF_BAR + 64 + 1024;               // + 1 KB alignment slack
 };
+// three CTAs per SM at head_dim 128 (dynamic shared memory + the 1 KB the
+// runtime reserves per CTA)
+static_assert(3 * (LlmAttnSmem<128>::BYTES + 1024) <= 233472, "three decode CTAs per SM");
 
 struct LlmAttnParams {
   const __nv_bfloat16* q;   // [n][H][D]
