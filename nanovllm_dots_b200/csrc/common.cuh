@@ -138,15 +138,6 @@ DFM_DEV void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c
       : "memory");
 }
 
-// Prefetch one box of a 5-D tensor into L2 (no shared memory, no completion).
-DFM_DEV void tma_prefetch_5d(const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4) {
-  asm volatile(
-      "cp.async.bulk.prefetch.tensor.5d.L2.global [%0, {%1, %2, %3, %4, %5}];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-      : "memory");
-}
-
 // ---------------------------------------------------------------- tcgen05 / TMEM
 DFM_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {  // whole warp
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
