@@ -100,3 +100,67 @@ def test_patch_encoder_has_no_cpu_path():
     from nanovllm_dots_b200.patch_encoder import B200PatchEncoder
     with pytest.raises(RuntimeError, match="CUDA"):
         B200PatchEncoder({}, syn.PE_BASE, max_batch=1, max_seq_len=16, device="cpu")
+
+
+def test_patch_encoder_prime_schedules_rows_in_shared_calls():
+    """prime(): every row is reset, then decoded one patch per call with all
+    rows that still have patches in the same call (at most max_batch)."""
+    from nanovllm_dots_b200.patch_encoder import B200PatchEncoder
+
+    calls, resets = [], []
+
+    class _PE(B200PatchEncoder):
+        def __init__(self):      # no device: only the scheduling is under test
+            self.cfg = syn.PE_BASE
+            self.device = torch.device("cpu")
+            self.max_batch = 2
+            self.out_ds_rate = self.cfg.rows
+            self.cap = 64 * self.cfg.rows
+
+        def reset_rows(self, rows):
+            resets.append(list(rows))
+
+        def decode_patch(self, latent_patches, rows):
+            calls.append((list(rows), latent_patches.shape[0]))
+            return torch.full((len(rows), 1, self.cfg.out_dim), float(len(calls)))
+
+    pe = _PE()
+    P = syn.PE_BASE.patch
+    prompts = [torch.zeros(3 * P, 64), torch.zeros(1 * P, 64), torch.zeros(2 * P, 64)]
+    outs = pe.prime([7, 3, 5], prompts)
+    assert resets == [[7, 3, 5]]
+    assert calls == [([7, 3], 2), ([5], 1), ([7, 5], 2), ([7], 1)]
+    assert [o.shape[0] for o in outs] == [3, 1, 2]
+    assert outs[0][:, 0].tolist() == [1.0, 3.0, 4.0]
+    with pytest.raises(ValueError, match="divisible"):
+        pe.prime([1], [torch.zeros(P + 1, 64)])
+
+
+def test_install_decode_attention_routes_only_decode_steps():
+    from nanovllm_dots_b200.llm_attention import install_decode_attention
+
+    class _Mod:
+        num_heads, head_dim, num_kv_heads, is_causal = 4, 8, 2, True
+        k_cache = torch.zeros(2, 16, 2, 8)
+        v_cache = torch.zeros(2, 16, 2, 8)
+
+        def forward(self, q, k, v):
+            return "flash"
+
+    seen = []
+
+    class _Dec:
+        def decode(self, q, k, v, kc, vc, slot, cl, bt):
+            seen.append((tuple(q.shape), tuple(k.shape), slot, cl, bt))
+            return "b200"
+
+    ctx = SimpleNamespace(is_prefill=True, slot_mapping="s", context_lens="c", block_tables="b")
+    m = _Mod()
+    install_decode_attention(m, lambda: ctx, _Dec())
+    q, k = torch.zeros(3, 32), torch.zeros(3, 16)
+    assert m.forward(q, k, k) == "flash"            # prefill keeps the original path
+    ctx.is_prefill = False
+    assert m.forward(q, k, k) == "b200"
+    assert seen == [((3, 4, 8), (3, 2, 8), "s", "c", "b")]
+    m.is_causal = False
+    assert m.forward(q, k, k) == "flash"
