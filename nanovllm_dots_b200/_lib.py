@@ -22,7 +22,8 @@ EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "df
            "dfm_destroy", "dfm_error_string", "dfm_linear", "dfm_attention_workspace_size",
            "dfm_paged_attention", "dfm_paged_attention_noalloc",
            "dpe_create", "dpe_workspace_size", "dpe_pool_bytes", "dpe_decode", "dpe_read_error",
-           "dpe_destroy", "dllm_decode_workspace_size", "dllm_decode_attention", "dllm_read_error")
+           "dpe_destroy", "dllm_decode_workspace_size", "dllm_decode_attention", "dllm_read_error",
+           "dllm_create", "dllm_step_workspace_size", "dllm_decode_step", "dllm_destroy")
 
 
 class DfmConfig(ctypes.Structure):
@@ -71,6 +72,28 @@ class DpeWeights(ctypes.Structure):
 class DpeBatch(ctypes.Structure):
     _fields_ = [("n", c_int32), ("patches", c_void_p), ("rows", c_void_p), ("seqlens", c_void_p),
                 ("conv_tail", c_void_p), ("kv_pool", c_void_p), ("out", c_void_p)]
+
+
+class DllmConfig(ctypes.Structure):
+    _fields_ = [("layers", c_int32), ("hidden", c_int32), ("heads", c_int32),
+                ("kv_heads", c_int32), ("head_dim", c_int32), ("inter", c_int32),
+                ("rms_eps", c_float), ("block_size", c_int32), ("max_blocks", c_int32),
+                ("max_batch", c_int32)]
+
+
+LLM_WEIGHT_FIELDS = ("in_norm", "qkv_w", "qkv_b", "o_w", "post_norm", "gate_up_w", "down_w",
+                     "final_norm", "inv_freq")
+
+
+class DllmWeights(ctypes.Structure):
+    _fields_ = [(f, c_void_p) for f in LLM_WEIGHT_FIELDS]
+
+
+class DllmStep(ctypes.Structure):
+    _fields_ = [("n", c_int32), ("embeds", c_void_p), ("positions", c_void_p),
+                ("slot_mapping", c_void_p), ("context_lens", c_void_p), ("block_table", c_void_p),
+                ("k_caches", POINTER(c_void_p)), ("v_caches", POINTER(c_void_p)),
+                ("num_blocks", c_int32), ("out", c_void_p)]
 
 
 _lib = None
@@ -131,6 +154,14 @@ def lib() -> ctypes.CDLL:
     L.dllm_decode_attention.restype = c_int32
     L.dllm_read_error.argtypes = [c_void_p, c_void_p, POINTER(c_uint32)]
     L.dllm_read_error.restype = c_int32
+    L.dllm_create.argtypes = [POINTER(DllmConfig), POINTER(DllmWeights), POINTER(c_void_p)]
+    L.dllm_create.restype = c_int32
+    L.dllm_step_workspace_size.argtypes = [c_void_p]
+    L.dllm_step_workspace_size.restype = c_size_t
+    L.dllm_decode_step.argtypes = [c_void_p, POINTER(DllmStep), c_void_p, c_size_t, c_void_p]
+    L.dllm_decode_step.restype = c_int32
+    L.dllm_destroy.argtypes = [c_void_p]
+    L.dllm_destroy.restype = c_int32
     _lib = L
     return L
 

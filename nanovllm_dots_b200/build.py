@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdfm.so")
 SOURCES = ["dfm_api.cu"]
 DEPS = ["dfm_api.cu", "dpe_api.cu", "llm_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh",
-        "pe.cuh", "llm_attn.cuh"]
+        "pe.cuh", "llm_attn.cuh", "llm_step.cuh"]
 HEADERS = [os.path.join(os.path.dirname(PKG), "include", h) for h in ("dfm.h", "dpe.h", "dllm.h")]
 
 

@@ -135,3 +135,308 @@ int dllm_read_error(void* workspace, void* stream, uint32_t* err_word) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- backbone decode step
+#include "llm_step.cuh"
+
+namespace {
+
+constexpr int kLlmQkvBN = 128, kLlmGuBN = 256;
+constexpr int kLlmOSplit = 4;     // O-projection split-K partials
+constexpr int kLlmSubPlanes = 5;  // the most partial planes a sublayer writes
+
+struct LlmStepWs {
+  size_t err, h, xn, qkv, qr, kr, vr, ao, sub, gu, act, part_o, part_ml, total;
+};
+
+struct LlmHandle {
+  DllmConfig c;
+  DllmWeights w;
+  int device;
+  int qkvw, down_split, mc;
+  LlmStepWs ws;
+  CUtensorMap* m_qkv;
+  CUtensorMap* m_o;
+  CUtensorMap* m_gu;
+  CUtensorMap* m_down;
+  CUtensorMap* m_kc;      // per layer, for the cache pointers in kc_ptr
+  CUtensorMap* m_vc;
+  const void** kc_ptr;
+  const void** vc_ptr;
+  int cache_blocks = 0;
+  const void* plan_ws = nullptr;
+  CUtensorMap a_xn, a_ao, a_act, o_qkv, o_sub, o_gu;
+};
+
+int llm_down_split(int inter) {
+  const int kb = inter / 64;
+  for (int s : {5, 4, 2}) if (kb % s == 0) return s;
+  return 1;
+}
+
+LlmStepWs llm_step_layout(const DllmConfig& c, int qkvw, int mc) {
+  LlmStepWs L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 1023) & ~static_cast<size_t>(1023);
+    return o;
+  };
+  const size_t NR = c.max_batch, Hd = c.hidden, HD = static_cast<size_t>(c.heads) * c.head_dim;
+  const size_t KD = static_cast<size_t>(c.kv_heads) * c.head_dim;
+  L.err = take(256);   // offset 0: dllm_read_error reads it
+  L.h = take(NR * Hd * 4);
+  L.xn = take(NR * Hd * 2);
+  L.qkv = take(NR * qkvw * 2);
+  L.qr = take(NR * HD * 2);
+  L.kr = take(NR * KD * 2);
+  L.vr = take(NR * KD * 2);
+  L.ao = take(NR * HD * 2);
+  L.sub = take(kLlmSubPlanes * NR * Hd * 4);
+  L.gu = take(NR * 2 * static_cast<size_t>(c.inter) * 2);
+  L.act = take(NR * static_cast<size_t>(c.inter) * 2);
+  L.part_o = take(NR * c.heads * mc * static_cast<size_t>(c.head_dim) * 4);
+  L.part_ml = take(NR * c.heads * mc * 2 * 4);
+  L.total = off;
+  return L;
+}
+
+int llm_validate(const DllmConfig& c) {
+  if (c.hidden != 1024 && c.hidden != 1536 && c.hidden != 2048) return DFM_ERR_UNSUPPORTED;
+  if (c.head_dim != 128 || c.heads < 1 || c.kv_heads < 1 || c.heads % c.kv_heads ||
+      c.heads / c.kv_heads > LA_MAXG)
+    return DFM_ERR_UNSUPPORTED;
+  if (c.inter < 64 || c.inter % 128 || (2 * c.inter) % kLlmGuBN || c.hidden % kLlmQkvBN)
+    return DFM_ERR_UNSUPPORTED;
+  if (c.block_size < LA_SUB || c.block_size % LA_SUB) return DFM_ERR_UNSUPPORTED;
+  if (c.layers < 1 || c.max_blocks < 1 || c.max_batch < 1 || !(c.rms_eps > 0.f))
+    return DFM_ERR_INVALID_ARG;
+  if ((c.heads * c.head_dim) / 64 % kLlmOSplit) return DFM_ERR_UNSUPPORTED;
+  return DFM_OK;
+}
+
+template <int NSUB>
+cudaError_t launch_rms(int hidden, cudaStream_t s, int M, float* h, const __nv_bfloat16* in,
+                       const float* sub, size_t plane, const float* w, float eps,
+                       __nv_bfloat16* out) {
+  const dim3 grid((M + LR_ROWS_PER_BLOCK - 1) / LR_ROWS_PER_BLOCK), block(LR_THREADS);
+  switch (hidden) {
+    case 1024: return launch_pdl(llm_rms_kernel<1024, NSUB>, grid, block, 0, s, h, in, sub, plane, M, w, eps, out);
+    case 1536: return launch_pdl(llm_rms_kernel<1536, NSUB>, grid, block, 0, s, h, in, sub, plane, M, w, eps, out);
+    case 2048: return launch_pdl(llm_rms_kernel<2048, NSUB>, grid, block, 0, s, h, in, sub, plane, M, w, eps, out);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_rms_n(int nsub, int hidden, cudaStream_t s, int M, float* h,
+                         const __nv_bfloat16* in, const float* sub, size_t plane, const float* w,
+                         float eps, __nv_bfloat16* out) {
+  switch (nsub) {
+    case 0: return launch_rms<0>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 1: return launch_rms<1>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 2: return launch_rms<2>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 4: return launch_rms<4>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 5: return launch_rms<5>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+bool llm_plan(LlmHandle* h, void* ws) {
+  if (h->plan_ws == ws) return true;
+  const DllmConfig& c = h->c;
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  const uint64_t NR = c.max_batch, Hd = c.hidden, HD = static_cast<uint64_t>(c.heads) * c.head_dim;
+  bool ok = map_2d(&h->a_xn, b + h->ws.xn, NR, Hd, Hd, 128) &&
+            map_2d(&h->a_ao, b + h->ws.ao, NR, HD, HD, 128) &&
+            map_2d(&h->a_act, b + h->ws.act, NR, c.inter, c.inter, 128) &&
+            map_out(&h->o_qkv, b + h->ws.qkv, false, NR, h->qkvw, 1, NR * h->qkvw * 2) &&
+            map_out(&h->o_sub, b + h->ws.sub, true, NR, Hd, kLlmSubPlanes, NR * Hd * 4) &&
+            map_out(&h->o_gu, b + h->ws.gu, false, NR, 2 * static_cast<uint64_t>(c.inter), 1,
+                    NR * 2 * static_cast<uint64_t>(c.inter) * 2);
+  if (!ok) {
+    h->plan_ws = nullptr;
+    return false;
+  }
+  if (cudaMemset(b + h->ws.err, 0, sizeof(uint32_t)) != cudaSuccess) return false;
+  h->plan_ws = ws;
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dllm_destroy(void* handle) {
+  LlmHandle* h = static_cast<LlmHandle*>(handle);
+  if (!h) return DFM_ERR_INVALID_ARG;
+  delete[] h->m_qkv;
+  delete[] h->m_o;
+  delete[] h->m_gu;
+  delete[] h->m_down;
+  delete[] h->m_kc;
+  delete[] h->m_vc;
+  delete[] h->kc_ptr;
+  delete[] h->vc_ptr;
+  delete h;
+  return DFM_OK;
+}
+
+int dllm_create(const DllmConfig* cfg, const DllmWeights* w, void** out) {
+  if (!cfg || !w || !out) return DFM_ERR_INVALID_ARG;
+  *out = nullptr;
+  int rc = llm_validate(*cfg);
+  if (rc != DFM_OK) return rc;
+  const void* req[] = {w->in_norm, w->qkv_w, w->qkv_b, w->o_w, w->post_norm, w->gate_up_w,
+                       w->down_w, w->final_norm, w->inv_freq};
+  for (const void* p : req)
+    if (!p) return DFM_ERR_INVALID_ARG;
+  if (!encode_fn()) return DFM_ERR_CUDA;
+  LlmHandle* h = new (std::nothrow) LlmHandle();
+  if (!h) return DFM_ERR_CUDA;
+  h->c = *cfg;
+  h->w = *w;
+  if (cudaGetDevice(&h->device) != cudaSuccess) {
+    delete h;
+    return DFM_ERR_CUDA;
+  }
+  const DllmConfig& c = h->c;
+  const int L = c.layers, Hd = c.hidden, HD = c.heads * c.head_dim;
+  h->qkvw = (c.heads + 2 * c.kv_heads) * c.head_dim;
+  h->down_split = llm_down_split(c.inter);
+  h->mc = llm_max_chunks(c.max_blocks, c.block_size);
+  h->ws = llm_step_layout(c, h->qkvw, h->mc);
+  h->m_qkv = new CUtensorMap[L];
+  h->m_o = new CUtensorMap[L];
+  h->m_gu = new CUtensorMap[L];
+  h->m_down = new CUtensorMap[L];
+  h->m_kc = new CUtensorMap[L];
+  h->m_vc = new CUtensorMap[L];
+  h->kc_ptr = new const void*[L]();
+  h->vc_ptr = new const void*[L]();
+  auto bw = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  bool ok = true;
+  for (int l = 0; ok && l < L; ++l) {
+    ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * h->qkvw * Hd, h->qkvw, Hd,
+                Hd, kLlmQkvBN / 2) &&
+         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * Hd * HD, Hd, HD, HD,
+                kLlmQkvBN / 2) &&
+         map_2d(&h->m_gu[l], bw(w->gate_up_w) + static_cast<size_t>(l) * 2 * c.inter * Hd,
+                2 * static_cast<uint64_t>(c.inter), Hd, Hd, kLlmGuBN / 2) &&
+         map_2d(&h->m_down[l], bw(w->down_w) + static_cast<size_t>(l) * Hd * c.inter, Hd, c.inter,
+                c.inter, kLlmQkvBN / 2);
+  }
+  if (!ok) {
+    dllm_destroy(h);
+    return DFM_ERR_CUDA;
+  }
+  *out = h;
+  return DFM_OK;
+}
+
+size_t dllm_step_workspace_size(void* handle) {
+  return handle ? static_cast<LlmHandle*>(handle)->ws.total : 0;
+}
+
+int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  LlmHandle* hd = static_cast<LlmHandle*>(handle);
+  if (!hd || !st || !workspace) return DFM_ERR_INVALID_ARG;
+  const DllmConfig& c = hd->c;
+  const DllmWeights& w = hd->w;
+  const int n = st->n;
+  if (n < 1 || n > c.max_batch) return DFM_ERR_INVALID_ARG;
+  if (!st->embeds || !st->positions || !st->slot_mapping || !st->context_lens ||
+      !st->block_table || !st->k_caches || !st->v_caches || !st->out || st->num_blocks < 1)
+    return DFM_ERR_INVALID_ARG;
+  if (workspace_bytes < hd->ws.total) return DFM_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return DFM_ERR_INVALID_ARG;
+  int dev = -1;
+  CK(cudaGetDevice(&dev));
+  if (dev != hd->device) return DFM_ERR_INVALID_ARG;
+  if (!llm_plan(hd, workspace)) return DFM_ERR_CUDA;
+  const int L = c.layers;
+  // cache descriptors: encoded when a layer's cache pointer (or the block count) changes
+  for (int l = 0; l < L; ++l) {
+    if (!st->k_caches[l] || !st->v_caches[l]) return DFM_ERR_INVALID_ARG;
+    if (hd->kc_ptr[l] != st->k_caches[l] || hd->vc_ptr[l] != st->v_caches[l] ||
+        hd->cache_blocks != st->num_blocks) {
+      if (!map_llm_cache(&hd->m_kc[l], st->k_caches[l], st->num_blocks, c.block_size, c.kv_heads,
+                         c.head_dim) ||
+          !map_llm_cache(&hd->m_vc[l], st->v_caches[l], st->num_blocks, c.block_size, c.kv_heads,
+                         c.head_dim))
+        return DFM_ERR_CUDA;
+      hd->kc_ptr[l] = st->k_caches[l];
+      hd->vc_ptr[l] = st->v_caches[l];
+    }
+  }
+  hd->cache_blocks = st->num_blocks;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws + hd->ws.err);
+  auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
+  auto f32 = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
+  const int Hd = c.hidden, H = c.heads, KVH = c.kv_heads, D = c.head_dim, I = c.inter;
+  const size_t plane = static_cast<size_t>(c.max_batch) * Hd;
+  float* h = f32(hd->ws.h);
+  __nv_bfloat16* xn = bf(hd->ws.xn);
+
+  LlmAttnParams ap{};
+  ap.q = bf(hd->ws.qr);
+  ap.context_lens = st->context_lens;
+  ap.block_table = st->block_table;
+  ap.part_o = f32(hd->ws.part_o);
+  ap.part_ml = f32(hd->ws.part_ml);
+  ap.n = n;
+  ap.H = H;
+  ap.KVH = KVH;
+  ap.G = H / KVH;
+  ap.max_blocks = c.max_blocks;
+  ap.num_blocks = st->num_blocks;
+  ap.block_size = c.block_size;
+  ap.max_chunks = hd->mc;
+  ap.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+  ap.err = err;
+
+  // the input embeddings into the fp32 residual stream, and the first RMSNorm
+  CK(launch_rms_n(0, Hd, s, n, h, static_cast<const __nv_bfloat16*>(st->embeds), nullptr, 0,
+                  w.in_norm, c.rms_eps, xn));
+  for (int l = 0; l < L; ++l) {
+    const int qkvw = hd->qkvw;
+    CK((gemm2<kLlmQkvBN, 6>(hd->a_xn, hd->m_qkv[l], hd->o_qkv, n, qkvw, Hd, 1,
+                            store_t<false>(w.qkv_b + static_cast<size_t>(l) * qkvw, kActNone),
+                            err, s)));
+    const int cnt = n * (H + 2 * KVH) * (D / 2);
+    CK(launch_pdl(llm_rope_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s,
+                  static_cast<const __nv_bfloat16*>(bf(hd->ws.qkv)), st->positions, w.inv_freq, n, H,
+                  KVH, D, bf(hd->ws.qr), bf(hd->ws.kr), bf(hd->ws.vr)));
+    const int row_elems = KVH * D;
+    const int scnt = 2 * n * (row_elems / 8);
+    CK(launch_pdl(llm_store_kv_kernel, dim3((scnt + 255) / 256), dim3(256), 0, s,
+                  static_cast<const __nv_bfloat16*>(bf(hd->ws.kr)),
+                  static_cast<const __nv_bfloat16*>(bf(hd->ws.vr)),
+                  static_cast<__nv_bfloat16*>(const_cast<void*>(hd->kc_ptr[l])),
+                  static_cast<__nv_bfloat16*>(const_cast<void*>(hd->vc_ptr[l])), st->slot_mapping, n,
+                  row_elems, static_cast<long long>(st->num_blocks) * c.block_size, err));
+    CK(launch_llm_decode<128>(hd->m_kc[l], hd->m_vc[l], ap, bf(hd->ws.ao), s));
+    CK((gemm2<kLlmQkvBN, 6>(hd->a_ao, hd->m_o[l], hd->o_sub, n, Hd, H * D, kLlmOSplit,
+                            store_t<true>(nullptr, kActNone), err, s)));
+    CK(launch_rms_n(kLlmOSplit, Hd, s, n, h, nullptr, f32(hd->ws.sub), plane,
+                    w.post_norm + static_cast<size_t>(l) * Hd, c.rms_eps, xn));
+    CK((gemm2<kLlmGuBN, 5>(hd->a_xn, hd->m_gu[l], hd->o_gu, n, 2 * I, Hd, 1,
+                           store_t<false>(nullptr, kActNone), err, s)));
+    const int acnt = n * (I / 8);
+    CK(launch_pdl(llm_silu_mul_kernel, dim3((acnt + 255) / 256), dim3(256), 0, s,
+                  static_cast<const __nv_bfloat16*>(bf(hd->ws.gu)), n, I, bf(hd->ws.act)));
+    CK((gemm2<kLlmQkvBN, 6>(hd->a_act, hd->m_down[l], hd->o_sub, n, Hd, I, hd->down_split,
+                            store_t<true>(nullptr, kActNone), err, s)));
+    // residual + the next layer's input norm, or the final norm into the output
+    const bool last = l == L - 1;
+    CK(launch_rms_n(hd->down_split, Hd, s, n, h, nullptr, f32(hd->ws.sub), plane,
+                    last ? w.final_norm : w.in_norm + static_cast<size_t>(l + 1) * Hd, c.rms_eps,
+                    last ? static_cast<__nv_bfloat16*>(st->out) : xn));
+  }
+  return DFM_OK;
+}
+
+}  // extern "C"

@@ -293,3 +293,64 @@ def make_pe_patches(n: int, count: int, seed: int, cfg: PEConfig = PE_BASE) -> t
     ``engine.py:750-752``)."""
     g = torch.Generator().manual_seed(seed)
     return torch.randn(count, n, cfg.patch, cfg.latent_dim, generator=g).to(torch.bfloat16)
+
+
+# --------------------------------------------------------------------------- #
+# LLM backbone (the step before the FM head)                                   #
+# --------------------------------------------------------------------------- #
+@dataclasses.dataclass(frozen=True)
+class LLMConfig:
+    """Shape of the dots.tts LLM backbone: Qwen2 with GQA 12 query / 2 kv heads
+    and head_dim 128 (``nanovllm_dots/models/dots/model_llm.py:1-12``), width
+    1536 (the FM head's ``cond_dim``), paged K/V in 256-position blocks
+    (``batched_llm.py:32-45``).  Depth, MLP width, RMSNorm eps and rope base are
+    the Qwen2-1.5B values (the checkpoint's llm_config.json is unpublished)."""
+    layers: int = 28
+    hidden: int = 1536
+    heads: int = 12
+    kv_heads: int = 2
+    head_dim: int = 128
+    inter: int = 8960
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    block_size: int = 256
+
+    @property
+    def qkv_width(self) -> int:
+        return (self.heads + 2 * self.kv_heads) * self.head_dim
+
+
+LLM_BASE = LLMConfig()
+
+
+def make_llm_weights(cfg: LLMConfig = LLM_BASE, seed: int = 0, device="cpu",
+                     std: float = 0.02) -> dict[str, torch.Tensor]:
+    """Seeded Qwen2 decoder weights (fp32 tensors holding bf16 values) under the
+    HuggingFace ``Qwen2Model`` state-dict names (``layers.{l}.self_attn.q_proj``,
+    ..., ``norm.weight``).  Linear weights N(0, std^2) (HF's initializer_range),
+    q/k/v biases N(0, 0.1^2) and RMSNorm weights 1 + N(0, 0.1^2), so every term
+    of the layer is exercised."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, D, I = cfg.hidden, cfg.head_dim, cfg.inter
+    sd: dict[str, torch.Tensor] = {}
+
+    def rn(*shape, s=std, base=0.0):
+        t = torch.randn(*shape, generator=g, device=device) * s + base
+        return t.to(torch.bfloat16).float()
+
+    for l in range(cfg.layers):
+        p = f"layers.{l}"
+        sd[f"{p}.input_layernorm.weight"] = rn(H, s=0.1, base=1.0)
+        sd[f"{p}.self_attn.q_proj.weight"] = rn(cfg.heads * D, H)
+        sd[f"{p}.self_attn.q_proj.bias"] = rn(cfg.heads * D, s=0.1)
+        sd[f"{p}.self_attn.k_proj.weight"] = rn(cfg.kv_heads * D, H)
+        sd[f"{p}.self_attn.k_proj.bias"] = rn(cfg.kv_heads * D, s=0.1)
+        sd[f"{p}.self_attn.v_proj.weight"] = rn(cfg.kv_heads * D, H)
+        sd[f"{p}.self_attn.v_proj.bias"] = rn(cfg.kv_heads * D, s=0.1)
+        sd[f"{p}.self_attn.o_proj.weight"] = rn(H, cfg.heads * D)
+        sd[f"{p}.post_attention_layernorm.weight"] = rn(H, s=0.1, base=1.0)
+        sd[f"{p}.mlp.gate_proj.weight"] = rn(I, H)
+        sd[f"{p}.mlp.up_proj.weight"] = rn(I, H)
+        sd[f"{p}.mlp.down_proj.weight"] = rn(H, I)
+    sd["norm.weight"] = rn(H, s=0.1, base=1.0)
+    return sd

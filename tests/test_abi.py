@@ -161,3 +161,39 @@ def test_llm_decode_attention_rejects_bad_arguments_without_a_gpu():
     assert L.dllm_decode_attention(*bad_bs) == 2                         # block_size not a multiple of 64
     small = [x, None, None, x, x, None, x, x, 1, 12, 2, 128, 4, 256, 4, 0.088, x, x, 16, None]
     assert L.dllm_decode_attention(*small) == 4                          # workspace too small
+
+
+def test_llm_decode_step_rejects_bad_configs_without_a_gpu():
+    L = _lib.lib()
+    assert ctypes.sizeof(_lib.DllmConfig) == 10 * 4
+    w = _lib.DllmWeights()
+    h = ctypes.c_void_p()
+    good = _lib.DllmConfig(2, 1536, 12, 2, 128, 8960, 1e-6, 256, 4, 8)
+    assert L.dllm_create(good, w, h) == 1              # null weight pointers
+    bad = _lib.DllmConfig(2, 1600, 12, 2, 128, 8960, 1e-6, 256, 4, 8)
+    assert L.dllm_create(bad, w, h) == 2               # width
+    bad = _lib.DllmConfig(2, 1536, 12, 2, 64, 8960, 1e-6, 256, 4, 8)
+    assert L.dllm_create(bad, w, h) == 2               # head_dim
+    assert L.dllm_decode_step(None, None, None, 0, None) == 1
+
+
+def test_pack_llm_weights_accepts_hf_and_packed_names():
+    from nanovllm_dots_b200.llm_decode import pack_llm_weights
+    from nanovllm_dots_b200.synthetic import LLMConfig, make_llm_weights
+    c = LLMConfig(layers=2, hidden=256, heads=2, kv_heads=1, inter=512)
+    hf = make_llm_weights(c)
+    packed = {}
+    for k, v in hf.items():
+        packed["model." + k] = v
+    for l in range(2):
+        a, m = f"model.layers.{l}.self_attn.", f"model.layers.{l}.mlp."
+        packed[a + "qkv_proj.weight"] = torch.cat([packed.pop(a + f"{x}_proj.weight") for x in "qkv"])
+        packed[a + "qkv_proj.bias"] = torch.cat([packed.pop(a + f"{x}_proj.bias") for x in "qkv"])
+        packed[m + "gate_up_proj.weight"] = torch.cat([packed.pop(m + "gate_proj.weight"),
+                                                       packed.pop(m + "up_proj.weight")])
+    p1, p2 = pack_llm_weights(hf, c, "cpu"), pack_llm_weights(packed, c, "cpu")
+    assert set(p1) == set(_lib.LLM_WEIGHT_FIELDS)
+    for k in p1:
+        assert torch.equal(p1[k], p2[k]), k
+    assert p1["qkv_w"].shape == (2, 512, 256) and p1["gate_up_w"].shape == (2, 1024, 256)
+    assert torch.equal(p1["qkv_w"][1, 384:].float(), hf["layers.1.self_attn.v_proj.weight"])
