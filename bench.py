@@ -46,14 +46,16 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2",
-                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe", "llmattn"],
+                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe", "llmattn",
+                             "llmdecode"],
                     help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
                          "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool); "
                          "pe = the patch encoder (the step after the FM head): one batched "
                          "decode_patch for 64 requests with cfg2's history lengths; "
                          "llmattn = the LLM backbone's paged decode attention (one layer, 64 "
-                         "sequences, Qwen2 GQA 12/2 x 128)")
+                         "sequences, Qwen2 GQA 12/2 x 128); llmdecode = the whole backbone "
+                         "decode step (28 layers, 64 sequences)")
     ap.add_argument("--cpu-sample", type=int, default=64,
                     help="requests in the CPU baseline sample (64 = one whole tick)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -661,23 +663,41 @@ def run_llmattn(args, rank, world):
     copies = max(2, math.ceil(4 * 126e6 / (kc.numel() * 4)))
     pools = [(kc, vc)] + [(kc.clone(), vc.clone()) for _ in range(copies - 1)]
 
-    def step(j):
-        a, b = pools[j % copies]
+    # one CUDA graph holds a decode call per cache copy (the layers of a decode
+    # step, as the reference's graph-captured decode replays them); a step is
+    # one layer's call, timed as graph time / calls
+    for j in range(copies):
+        a, b = pools[j]
         dec.decode(q, k, v, a, b, slot, cl, td, out=out)
-
-    for j in range(max(args.warmup, 3)):
-        step(j)
     torch.cuda.synchronize()
     dec.check_errors()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for j in range(copies):
+            a, b = pools[j]
+            dec.decode(q, k, v, a, b, slot, cl, td, out=out, stream=torch.cuda.current_stream(dev))
+    reps = max(1, args.steps // copies)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
         e0.record(stream)
-        for j in range(args.steps):
-            step(j)
+        for _ in range(reps):
+            graph.replay()
         e1.record(stream)
         e1.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / (reps * copies)
     dec.check_errors()
+    # the same calls issued eagerly from Python, for the host-side cost
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for j in range(reps * copies):
+        a, b = pools[j % copies]
+        dec.decode(q, k, v, a, b, slot, cl, td, out=out)
+    f1.record(stream)
+    f1.synchronize()
+    eager_ms = f0.elapsed_time(f1) / (reps * copies)
     hbm, _, peak_kind = load_peaks()
     kv_bytes = sum(ctx) * KVH * D * 2 * 2
     achieved = kv_bytes / (ms * 1e-3) / 1e9
@@ -695,13 +715,15 @@ def run_llmattn(args, rank, world):
     if rank == 0:
         line = {"metric": LLM_METRIC, "value": round(1000.0 / ms, 1), "unit": "layer-steps/s",
                 "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+                "ms_per_step": round(ms, 5), "eager_ms_per_step": round(eager_ms, 5),
+                "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (N(0,1) q, N(0,0.5^2) cache)",
                 "config": {"workload": "llmattn", "sequences": n, "heads": H, "kv_heads": KVH,
                            "head_dim": D, "block_size": bs,
                            "mean_context": round(sum(ctx) / n, 1),
-                           "l2": f"{copies} cache copies cycled (each call reads from HBM)"},
-                "gpu_launches": 3 * args.steps,
+                           "l2": f"{copies} cache copies cycled (each call reads from HBM)",
+                           "timing": f"CUDA graph of {copies} calls replayed {reps} times"},
+                "gpu_launches": 3 * reps * copies,
                 "roofline": {"kernel": "llm_decode_attn_kernel + store + combine", "bound": "hbm",
                              "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(achieved / hbm, 4), "traffic": None,
@@ -709,6 +731,127 @@ def run_llmattn(args, rank, world):
                              "peak_source": f"{peak_kind} (hbm_gbs)"},
                 "clocks": clk.summary(), "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- #
+# LLM backbone decode step (``--workload llmdecode``)                          #
+# --------------------------------------------------------------------------- #
+LLMDEC_METRIC = "LLM backbone decode tokens/s (64 sequences, 28 layers)"
+
+
+def llm_contexts(rank: int, n: int = 64) -> list[int]:
+    """Prompt tokens U{100..300} + one token per generated patch (cfg2's
+    U{0..120} history), + the step's own token."""
+    g = torch.Generator().manual_seed(11 + rank)
+    return (torch.randint(100, 301, (n,), generator=g) + torch.randint(0, 121, (n,), generator=g)
+            + 1).tolist()
+
+
+def run_llmdecode(args, rank, world):
+    from nanovllm_dots_b200 import synthetic as syn
+    from nanovllm_dots_b200.llm_decode import B200QwenDecoder
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = syn.LLM_BASE
+    ctx = llm_contexts(rank)
+    n, bs = len(ctx), cfg.block_size
+    nblk = [(c + bs - 1) // bs for c in ctx]
+    width, num_blocks = max(nblk), sum(nblk)
+    g = torch.Generator().manual_seed(5 + rank)
+    perm = torch.randperm(num_blocks, generator=g)
+    table = torch.full((n, width), -1, dtype=torch.int32)
+    o = 0
+    for i, b in enumerate(nblk):
+        table[i, :b] = perm[o:o + b].to(torch.int32)
+        o += b
+    w = syn.make_llm_weights(cfg, device=dev)          # drawn on the device: 1.3 B parameters
+    dec = B200QwenDecoder(w, cfg, max_batch=n, max_blocks=width, device=dev)
+    del w
+    torch.cuda.empty_cache()
+    kc, vc = dec.alloc_caches(num_blocks)
+    gd = torch.Generator(device=dev).manual_seed(7)
+    for t in kc + vc:
+        t.copy_((torch.randn(t.shape, device=dev, generator=gd) * 0.5).to(torch.bfloat16))
+    emb = torch.randn(n, cfg.hidden, device=dev, generator=gd).to(torch.bfloat16)
+    pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32, device=dev)
+    slot = torch.tensor([int(table[i, (c - 1) // bs]) * bs + (c - 1) % bs for i, c in enumerate(ctx)],
+                        dtype=torch.int32, device=dev)
+    cl = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    td = table.to(dev)
+    out = torch.empty(n, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    dec.step(emb, pos, slot, cl, td, kc, vc, out=out)     # plans the workspace and cache maps
+    torch.cuda.synchronize()
+    dec.check_errors()
+    if args.profile_tick:
+        torch.cuda.cudart().cudaProfilerStart()
+        dec.step(emb, pos, slot, cl, td, kc, vc, out=out)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        dec.check_errors()
+        if rank == 0:
+            print(json.dumps({"profile_tick": True, "workload": "llmdecode", "sequences": n,
+                              "launches": 1 + 11 * cfg.layers}), flush=True)
+        dec.close()
+        return
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec.step(emb, pos, slot, cl, td, kc, vc, out=out, stream=torch.cuda.current_stream(dev))
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    dec.check_errors()
+    # end to end: pinned-host embeddings in, hidden states out, every step
+    h_emb = emb.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        emb.copy_(h_emb, non_blocking=True)
+        graph.replay()
+        h_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+    f1.record(stream)
+    f1.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    hbm, tflops, peak_kind = load_peaks()
+    per_layer_w = (cfg.qkv_width * cfg.hidden + cfg.hidden * cfg.heads * cfg.head_dim
+                   + 3 * cfg.inter * cfg.hidden) * 2
+    kv_bytes = sum(ctx) * cfg.kv_heads * cfg.head_dim * 2 * 2 * cfg.layers
+    bytes_step = per_layer_w * cfg.layers + kv_bytes
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {"metric": LLMDEC_METRIC, "value": round(n * 1000.0 / ms, 1), "unit": "tokens/s",
+                "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded Qwen2-shaped weights, N(0,1) embeddings, N(0,0.5^2) caches)",
+                "config": {"workload": "llmdecode", "sequences": n, "layers": cfg.layers,
+                           "hidden": cfg.hidden, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
+                           "inter": cfg.inter, "mean_context": round(sum(ctx) / n, 1),
+                           "l2": "weights (2.6 GB) and caches larger than L2, no flush",
+                           "timing": "CUDA graph of one decode step"},
+                "e2e": {"value": round(n * 1000.0 / e2e_ms, 1), "unit": "tokens/s",
+                        "h2d_bytes_per_step": h_emb.numel() * 2, "d2h_bytes_per_step": h_out.numel() * 2,
+                        "ms_per_step": round(e2e_ms, 4)},
+                "gpu_launches": (1 + 11 * cfg.layers) * args.steps,
+                "roofline": {"kernel": "whole decode step (weights + K/V streamed once)",
+                             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                             "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                             "algorithmic_per_launch": bytes_step,
+                             "peak_source": f"{peak_kind} (hbm_gbs)"},
+                "clocks": clk.summary(), "cpu_baseline": None}
+        print(json.dumps(line), flush=True)
+    dec.close()
 
 
 def main():
@@ -727,6 +870,8 @@ def main():
             run_pe(args, rank, world)
         elif args.workload == "llmattn":
             run_llmattn(args, rank, world)
+        elif args.workload == "llmdecode":
+            run_llmdecode(args, rank, world)
         else:
             run_b200(args, rank, world)
     finally:

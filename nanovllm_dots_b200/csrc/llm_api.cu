@@ -143,6 +143,7 @@ namespace {
 
 constexpr int kLlmQkvBN = 128, kLlmGuBN = 256;
 constexpr int kLlmOSplit = 4;     // O-projection split-K partials
+constexpr int kLlmQkvSplit = 4;   // QKV split-K partials (N = 2048 alone gives 16 work units)
 constexpr int kLlmSubPlanes = 5;  // the most partial planes a sublayer writes
 
 struct LlmStepWs {
@@ -187,7 +188,7 @@ LlmStepWs llm_step_layout(const DllmConfig& c, int qkvw, int mc) {
   L.err = take(256);   // offset 0: dllm_read_error reads it
   L.h = take(NR * Hd * 4);
   L.xn = take(NR * Hd * 2);
-  L.qkv = take(NR * qkvw * 2);
+  L.qkv = take(kLlmQkvSplit * NR * qkvw * 4);   // fp32 split-K planes
   L.qr = take(NR * HD * 2);
   L.kr = take(NR * KD * 2);
   L.vr = take(NR * KD * 2);
@@ -211,7 +212,8 @@ int llm_validate(const DllmConfig& c) {
   if (c.block_size < LA_SUB || c.block_size % LA_SUB) return DFM_ERR_UNSUPPORTED;
   if (c.layers < 1 || c.max_blocks < 1 || c.max_batch < 1 || !(c.rms_eps > 0.f))
     return DFM_ERR_INVALID_ARG;
-  if ((c.heads * c.head_dim) / 64 % kLlmOSplit) return DFM_ERR_UNSUPPORTED;
+  if ((c.heads * c.head_dim) / 64 % kLlmOSplit || (c.hidden / 64) % kLlmQkvSplit)
+    return DFM_ERR_UNSUPPORTED;
   return DFM_OK;
 }
 
@@ -249,7 +251,7 @@ bool llm_plan(LlmHandle* h, void* ws) {
   bool ok = map_2d(&h->a_xn, b + h->ws.xn, NR, Hd, Hd, 128) &&
             map_2d(&h->a_ao, b + h->ws.ao, NR, HD, HD, 128) &&
             map_2d(&h->a_act, b + h->ws.act, NR, c.inter, c.inter, 128) &&
-            map_out(&h->o_qkv, b + h->ws.qkv, false, NR, h->qkvw, 1, NR * h->qkvw * 2) &&
+            map_out(&h->o_qkv, b + h->ws.qkv, true, NR, h->qkvw, kLlmQkvSplit, NR * h->qkvw * 4) &&
             map_out(&h->o_sub, b + h->ws.sub, true, NR, Hd, kLlmSubPlanes, NR * Hd * 4) &&
             map_out(&h->o_gu, b + h->ws.gu, false, NR, 2 * static_cast<uint64_t>(c.inter), 1,
                     NR * 2 * static_cast<uint64_t>(c.inter) * 2);
@@ -403,13 +405,14 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
                   w.in_norm, c.rms_eps, xn));
   for (int l = 0; l < L; ++l) {
     const int qkvw = hd->qkvw;
-    CK((gemm2<kLlmQkvBN, 6>(hd->a_xn, hd->m_qkv[l], hd->o_qkv, n, qkvw, Hd, 1,
-                            store_t<false>(w.qkv_b + static_cast<size_t>(l) * qkvw, kActNone),
-                            err, s)));
+    CK((gemm2<kLlmQkvBN, 6>(hd->a_xn, hd->m_qkv[l], hd->o_qkv, n, qkvw, Hd, kLlmQkvSplit,
+                            store_t<true>(nullptr, kActNone), err, s)));
     const int cnt = n * (H + 2 * KVH) * (D / 2);
     CK(launch_pdl(llm_rope_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s,
-                  static_cast<const __nv_bfloat16*>(bf(hd->ws.qkv)), st->positions, w.inv_freq, n, H,
-                  KVH, D, bf(hd->ws.qr), bf(hd->ws.kr), bf(hd->ws.vr)));
+                  static_cast<const float*>(f32(hd->ws.qkv)), kLlmQkvSplit,
+                  static_cast<size_t>(c.max_batch) * qkvw,
+                  static_cast<const float*>(w.qkv_b + static_cast<size_t>(l) * qkvw), st->positions,
+                  w.inv_freq, n, H, KVH, D, bf(hd->ws.qr), bf(hd->ws.kr), bf(hd->ws.vr)));
     const int row_elems = KVH * D;
     const int scnt = 2 * n * (row_elems / 8);
     CK(launch_pdl(llm_store_kv_kernel, dim3((scnt + 255) / 256), dim3(256), 0, s,

@@ -72,12 +72,14 @@ __global__ void __launch_bounds__(LR_THREADS)
   }
 }
 
-// qkv [n][(H + 2 KVH) D] (bias included) -> q [n][H][D], k [n][KVH][D] rotated at
-// positions[i] (NeoX halves: y1 = x1 cos - x2 sin, y2 = x2 cos + x1 sin, angle
+// qkv = bias + sum of the QKV projection's nsplit fp32 split-K planes
+// [p][n][(H + 2 KVH) D] -> q [n][H][D], k [n][KVH][D] rotated at positions[i]
+// (NeoX halves: y1 = x1 cos - x2 sin, y2 = x2 cos + x1 sin, angle
 // pos * inv_freq[d], ``layers/rotary_embedding.py:6-47``) and v [n][KVH][D].
 // One thread per (row, head, rotary pair).
 __global__ void __launch_bounds__(256)
-    llm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, const int* __restrict__ positions,
+    llm_rope_kernel(const float* __restrict__ qkv, int nsplit, size_t plane,
+                    const float* __restrict__ bias, const int* __restrict__ positions,
                     const float* __restrict__ inv_freq, int n, int H, int KVH, int D,
                     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
                     __nv_bfloat16* __restrict__ v) {
@@ -89,12 +91,17 @@ __global__ void __launch_bounds__(256)
   const int i = idx / (heads * half);
   const int rem = idx - i * heads * half;
   const int hd = rem / half, d = rem - hd * half;
-  const __nv_bfloat16* src = qkv + static_cast<size_t>(i) * heads * D + hd * D;
-  const float x1 = __bfloat162float(src[d]), x2 = __bfloat162float(src[d + half]);
-  if (hd >= H + KVH) {   // v: copied
+  const int c1 = hd * D + d, c2 = c1 + half;
+  const float* src = qkv + static_cast<size_t>(i) * heads * D;
+  float x1 = bias[c1], x2 = bias[c2];
+  for (int p = 0; p < nsplit; ++p) {
+    x1 += src[p * plane + c1];
+    x2 += src[p * plane + c2];
+  }
+  if (hd >= H + KVH) {   // v: no rotation
     __nv_bfloat16* dst = v + (static_cast<size_t>(i) * KVH + (hd - H - KVH)) * D;
-    dst[d] = src[d];
-    dst[d + half] = src[d + half];
+    dst[d] = __float2bfloat16(x1);
+    dst[d + half] = __float2bfloat16(x2);
     return;
   }
   float s, c;
