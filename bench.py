@@ -18,6 +18,11 @@ requests (weak scaling, no collective on the data path); time = max over ranks.
 ``--impl reference`` times the reference's algorithm on the host CPU (the oracle
 restatement of the reference's cache path; the reference itself is Python with
 no GPU MeanFlow cache head) on a bounded sample of the same workload.
+
+Other rows of the build, each with its own metric line (not the headline):
+``--workload pe`` (the patch encoder: one batched decode_patch of 64 requests),
+``--workload llmattn`` (the LLM backbone's paged decode attention, one layer)
+and ``--workload llmdecode`` (the whole 28-layer backbone decode step).
 """
 from __future__ import annotations
 
