@@ -79,28 +79,65 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def workload_batch(name: str, rank: int):
+def population(name: str, world: int) -> list[int]:
+    """Prefix patches of every request on the box (64 per GPU).
+
+    cfg2 / cfg3 (the default, also what the driver's 1/2/4/8-GPU runs use):
+    ``world`` copies of config 2's seeded 64-request draw, so the per-GPU work
+    is config 2's at every N (weak scaling).  cfg4: BASELINE config 4's mix (75%
+    U{0..60}, 25% U{200..320} patches) drawn once for the whole 8-GPU box (512
+    requests, seed 4); N GPUs serve its first 64*N."""
+    from nanovllm_dots_b200 import synthetic as syn
+    cfg = syn.BASE
+    if name in ("cfg1", "cfg2", "cfg3"):
+        base = syn.config_batch("cfg1" if name == "cfg1" else "cfg2")
+        return [p // cfg.stride for p in base.prefix_rows] * world
+    if name == "cfg4":
+        g = torch.Generator().manual_seed(4)
+        long_ = torch.rand(512, generator=g) < 0.25
+        short_p = torch.randint(0, 61, (512,), generator=g)
+        long_p = torch.randint(200, 321, (512,), generator=g)
+        pp = torch.where(long_, long_p, short_p).tolist()
+        if world > 8:
+            raise ValueError("cfg4 is an 8-GPU box workload")
+        return pp[: 64 * world]
+    raise ValueError(name)
+
+
+def placement(pp: list[int], world: int):
+    """Place the box's requests on ranks with ``LeastLoadedSharder`` (each
+    request for its life on the rank with the fewest K/V rows to stream,
+    longest request first, at most the per-GPU request count per rank).
+    Returns (per-rank prefix-patch lists, per-rank loads in rows)."""
+    from nanovllm_dots_b200 import synthetic as syn
+    from nanovllm_dots_b200.sharding import LeastLoadedSharder
+    cfg = syn.BASE
+    per = len(pp) // world
+    sh = LeastLoadedSharder(world, stride=cfg.stride, max_per_rank=per)
+    for rid in sorted(range(len(pp)), key=lambda i: (-pp[i], i)):
+        sh.assign(rid, cfg.stride * pp[rid])
+    shards = [[pp[r] for r in sorted(ids)] for ids in sh.by_rank(range(len(pp)))]
+    return shards, list(sh.load)
+
+
+def workload_batch(name: str, rank: int, world: int = 1):
+    """(this rank's RequestBatch, placement summary)."""
     from nanovllm_dots_b200 import synthetic as syn
     if name == "gemm64":
-        return syn.make_batch(64, [0] * 64, seed=2)
-    if name == "cfg3":
-        name = "cfg2"
+        return syn.make_batch(64, [0] * 64, seed=2), None
     if name == "prof":
         full = syn.config_batch("cfg2")
-        return syn.make_batch(16, [p // 17 for p in full.prefix_rows[:16]], seed=2)
-    b = syn.config_batch(name)
-    if rank:
-        # same distribution, an independent draw per rank
-        g = torch.Generator().manual_seed(1000 + rank)
-        hi = {"cfg1": 33, "cfg2": 121}.get(name)
-        if hi is not None:
-            pp = torch.randint(0, hi, (b.n,), generator=g).tolist()
-        else:
-            long_ = torch.rand(b.n, generator=g) < 0.25
-            pp = torch.where(long_, torch.randint(200, 321, (b.n,), generator=g),
-                             torch.randint(0, 61, (b.n,), generator=g)).tolist()
-        b = syn.make_batch(b.n, pp, seed=1000 + rank)
-    return b
+        return syn.make_batch(16, [p // 17 for p in full.prefix_rows[:16]], seed=2), None
+    if world == 1 and name in ("cfg1", "cfg2", "cfg3"):
+        return syn.config_batch("cfg1" if name == "cfg1" else "cfg2"), None
+    shards, loads = placement(population(name, world), world)
+    mine = shards[rank]
+    seed = {"cfg1": 1, "cfg4": 4}.get(name, 2)
+    b = syn.make_batch(len(mine), mine, seed=seed if rank == 0 else 1000 * seed + rank)
+    summary = {"requests_total": sum(len(x) for x in shards), "rows_per_rank": loads,
+               "load_max_over_mean": round(max(loads) / (sum(loads) / len(loads)), 4),
+               "placement": "LeastLoadedSharder (K/V rows), longest request first"}
+    return b, summary
 
 
 class ClockSampler:
@@ -171,14 +208,51 @@ def cpu_tick_seconds(weights, batch, idx):
     return time.perf_counter() - t0
 
 
+def cpu_full_path_seconds(weights, batch, idx):
+    """The reference's shipping MeanFlow path on the host: per request, 4 DiT
+    forwards over the whole padded-free history plus the latent slot with the
+    FM mask (``_pack_fm_inputs`` + ``batched_meanflow``, ``engine.py:635-709``,
+    ``batched_fm.py:82-126``; O(P^2) attention, every history row recomputed
+    at every step).  History rows are N(0,1) rows of the cached length."""
+    from nanovllm_dots_b200 import synthetic as syn
+    from oracle import dit_oracle as O
+    cfg = syn.BASE
+    ts, dts = syn.time_grid(cfg.nfe)
+    hists = {}
+    for i in idx:
+        g = torch.Generator().manual_seed(55 + i)
+        hists[i] = torch.randn(batch.prefix_rows[i] + cfg.stride + 1, cfg.hidden, generator=g)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for i in idx:
+            x = hists[i]
+            z = batch.noise[i].float()
+            for k in range(cfg.nfe):
+                inp = torch.cat([x, O.linear(z, weights, "coordinate_proj")], dim=0)
+                v = O.dit_forward_full(weights, cfg, inp, ts[k], dts[k], fm_seq_len=x.shape[0])
+                z = z + v[x.shape[0]:] * dts[k]
+    return time.perf_counter() - t0
+
+
 def cpu_baseline(weights, batch, n_sample):
     idx = list(range(min(n_sample, batch.n)))
     secs = cpu_tick_seconds(weights, batch, idx)
     mean_p = sum(batch.prefix_rows[i] for i in idx) / len(idx)
+    # the O(P^2) full path on two requests near the median length
+    order = sorted(range(batch.n), key=lambda i: batch.prefix_rows[i])
+    fidx = [order[batch.n // 2 - 1], order[batch.n // 2]]
+    fsecs = cpu_full_path_seconds(weights, batch, fidx)
     return {"value": round(len(idx) * AUDIO_S_PER_PATCH / secs, 4), "unit": "audio-s/s",
             "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{len(idx)} request-ticks of the same workload (mean prefix {mean_p:.0f} "
-                      f"rows), fp32 eager torch on the host, {secs:.1f} s"}
+                      f"rows) through the reference's cache path (extend + active rows), "
+                      f"fp32 eager torch on the host, {secs:.1f} s",
+            "full_path": {"value": round(len(fidx) * AUDIO_S_PER_PATCH / fsecs, 4),
+                          "unit": "audio-s/s",
+                          "sample": f"{len(fidx)} request-ticks (prefixes "
+                                    f"{[batch.prefix_rows[i] for i in fidx]} rows) through the "
+                                    f"reference's shipping full O(P^2) MeanFlow path, fp32 eager, "
+                                    f"{fsecs:.1f} s"}}
 
 
 def run_reference(args, rank):
@@ -187,7 +261,7 @@ def run_reference(args, rank):
     from nanovllm_dots_b200 import synthetic as syn
     torch.set_num_threads(os.cpu_count() or 1)
     w = syn.make_weights(syn.BASE)
-    b = workload_batch(args.workload, 0)
+    b, _ = workload_batch(args.workload, 0)
     per_step = 2
     times = []
     for s in range(args.warmup + args.steps):
@@ -228,7 +302,7 @@ def run_b200(args, rank, world):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     cfg = syn.BASE
-    b = workload_batch(args.workload, rank)
+    b, place = workload_batch(args.workload, rank, world)
     n = b.n
     max_pages = max(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows)
     num_pages = sum(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows) + 8
@@ -307,6 +381,14 @@ def run_b200(args, rank, world):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
+    def all_ranks(x):
+        if world == 1:
+            return [round(x, 4)]
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        parts = [torch.empty_like(t) for _ in range(world)]
+        torch.distributed.all_gather(parts, t)
+        return [round(float(p.item()), 4) for p in parts]
+
     # ---- device-resident timing
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -317,7 +399,9 @@ def run_b200(args, rank, world):
         e1.record(stream)
         e1.synchronize()
     barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    my_ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(my_ms)
+    per_rank_ms = all_ranks(my_ms)
     head.check_errors()
 
     # ---- end to end through the C ABI with host buffers (pinned), per-tick copies
@@ -351,76 +435,77 @@ def run_b200(args, rank, world):
     barrier()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
 
-    # ---- per-kernel timing of the dominant kernels (same shapes, same stream)
+    # ---- the tick's own kernels, one at a time (dfm_tick_launch: same kernel,
+    # tiles, epilogue and workspace as inside the tick), layers cycled so the
+    # weights stream from HBM as they do in the tick
     hbm, tflops, peak_kind = load_peaks()
-    L = _lib.lib()
-    kern = {}
     R = 2 * cfg.stride * n
-    ws = head.workspace
-    wsb = L.dfm_attention_workspace_size(n, max_pages, cfg.heads)
-    aws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
-    q = torch.randn(R, cfg.hidden, device=dev).to(torch.bfloat16)
-    ao = torch.empty_like(q)
-    planes = cfg.layers * cfg.nfe * 2
-
-    def attn_once():
-        _lib.check(L.dfm_paged_attention(q.data_ptr(), ao.data_ptr(), head.pool.data_ptr(),
-                                         num_pages, planes, cfg.heads, 0, 1, cl.data_ptr(),
-                                         ne.data_ptr(), bt.data_ptr(), max_pages, n,
-                                         aws.data_ptr(), wsb, _lib.c_void_p(stream.cuda_stream)),
-                   "dfm_paged_attention")
-
+    H, F_ = cfg.hidden, cfg.ffn
+    tensors = dict(noise=noise, act_hidden=cond, ext_hidden=ph, ext_latent=pl, cache_len=cl,
+                   n_extend=ne, block_table=bt, out=out)
+    eager_tick()                                 # workspace state of a full tick
+    torch.cuda.synchronize()
     keys = sum(p + 2 * cfg.stride for p in b.prefix_rows)
-    attn_bytes = keys * cfg.heads * cfg.head_dim * 2 * 2 + 2 * R * cfg.hidden * 2
-    kern["attention"] = {"fn": attn_once, "bytes": attn_bytes, "per_tick": cfg.layers * cfg.nfe,
-                         "bound": "hbm"}
-    a_x = torch.randn(R, cfg.hidden, device=dev).to(torch.bfloat16)
-    a_u = torch.randn(R, cfg.ffn, device=dev).to(torch.bfloat16)
-    shapes = {"qkv": (a_x, head.w["qkv_w"][0], 3 * cfg.hidden, cfg.hidden, False),
-              "fc1": (a_x, head.w["fc1_w"][0], cfg.ffn, cfg.hidden, True),
-              "fc2": (a_u, head.w["fc2_w"][0], cfg.hidden, cfg.ffn, False),
-              "o_proj": (a_x, head.w["o_w"][0], cfg.hidden, cfg.hidden, False)}
-    for nm, (A, Wt, N, K, gelu) in shapes.items():
-        o_buf = torch.empty(R, N, device=dev, dtype=torch.bfloat16)
-
-        def f(A=A, Wt=Wt, N=N, K=K, gelu=gelu, o_buf=o_buf):
-            _lib.check(L.dfm_linear(A.data_ptr(), K, R, K, Wt.data_ptr(), K, N, None,
-                                    o_buf.data_ptr(), 0, int(gelu),
-                                    _lib.c_void_p(stream.cuda_stream)), "dfm_linear")
-        kern[nm] = {"fn": f, "flops": 2.0 * R * N * K, "per_tick": cfg.layers * cfg.nfe,
-                    "bound": "tensor"}
-    reps = 20
-    for nm, k in kern.items():
-        for _ in range(3):
-            k["fn"]()
+    ln_bytes = R * H * (4 + 2 * 4 + 4 + 2) + n * 3 * H * 4
+    kinds = {
+        "ln_attn": {"bytes": ln_bytes, "bound": "hbm"},
+        "qkv": {"flops": 2.0 * R * 3 * H * H, "bound": "tensor"},
+        "attention": {"bytes": keys * cfg.heads * cfg.head_dim * 2 * 2 + 2 * R * H * 2,
+                      "bound": "hbm"},
+        "o_proj": {"flops": 2.0 * R * H * H, "bound": "tensor"},
+        "ln_mlp": {"bytes": ln_bytes, "bound": "hbm"},
+        "fc1": {"flops": 2.0 * R * F_ * H, "bound": "tensor"},
+        "fc2": {"flops": 2.0 * R * H * F_, "bound": "tensor"},
+    }
+    reps = 4
+    for nm, k in kinds.items():
+        def run(nm=nm):
+            for l in range(cfg.layers):
+                head.launch_kernel(nm, 0, l, stream=stream, **tensors)
+        run()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record(stream)
         for _ in range(reps):
-            k["fn"]()
+            run()
         s1.record(stream)
         s1.synchronize()
-        k["us"] = s0.elapsed_time(s1) * 1000 / reps
+        k["us"] = s0.elapsed_time(s1) * 1000 / (reps * cfg.layers)
+    head.check_errors()
+    eager_tick()                                 # leave the workspace as a tick leaves it
+    torch.cuda.synchronize()
+    per_tick = cfg.layers * cfg.nfe
     summary = {}
-    for nm, k in kern.items():
+    for nm, k in kinds.items():
         if k["bound"] == "hbm":
             ach, peak, unit = k["bytes"] / (k["us"] * 1e-6) / 1e9, hbm, "GB/s"
         else:
             ach, peak, unit = k["flops"] / (k["us"] * 1e-6) / 1e12, tflops, "TFLOP/s"
         summary[nm] = {"us": round(k["us"], 2), "achieved": round(ach, 1), "unit": unit,
                        "frac": round(ach / peak, 4),
-                       "tick_share_est": round(k["us"] * k["per_tick"] / (ms * 1000), 4)}
-    dom = max(summary, key=lambda x: summary[x]["tick_share_est"])
+                       "tick_share_est": round(k["us"] * per_tick / (ms * 1000), 4)}
+    gemm_us = sum(kinds[g]["us"] for g in ("qkv", "o_proj", "fc1", "fc2"))
+    gemm_fl = sum(kinds[g]["flops"] for g in ("qkv", "o_proj", "fc1", "fc2"))
+    summary["per_layer_gemms"] = {"us": round(gemm_us, 2),
+                                  "achieved": round(gemm_fl / (gemm_us * 1e-6) / 1e12, 1),
+                                  "unit": "TFLOP/s",
+                                  "frac": round(gemm_fl / (gemm_us * 1e-6) / 1e12 / tflops, 4),
+                                  "note": "QKV + O-proj + fc1 + fc2, FLOP-weighted"}
+    summary["sum_of_shares"] = round(sum(v["tick_share_est"] for kk, v in summary.items()
+                                         if kk in kinds), 4)
+    dom = max(kinds, key=lambda x: summary[x]["tick_share_est"])
     traffic = None
     tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
             traffic = json.load(f).get(dom)
-    dk = kern[dom]
+    dk = kinds[dom]
     roof = {"kernel": dom, "bound": dk["bound"], "achieved": summary[dom]["achieved"],
             "peak": hbm if dk["bound"] == "hbm" else tflops, "unit": summary[dom]["unit"],
             "frac": summary[dom]["frac"], "traffic": traffic,
             "algorithmic_per_launch": dk.get("bytes", dk.get("flops")),
-            "peak_source": f"{peak_kind} ({'hbm_gbs' if dk['bound'] == 'hbm' else 'bf16_tflops'})"}
+            "peak_source": f"{peak_kind} ({'hbm_gbs' if dk['bound'] == 'hbm' else 'bf16_tflops'})",
+            "timing": "the tick's own launch (dfm_tick_launch), CUDA events, 12 layers x "
+                      f"{reps} on the tick's stream"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -440,7 +525,11 @@ def run_b200(args, rank, world):
                            "nfe": cfg.nfe, "layers": cfg.layers, "page_rows": cfg.page_rows,
                            "l2": "inputs larger than L2 (K/V pool and weights), no flush",
                            "parallelism": f"request-sharded x{world}",
-                           "precision": "fp8" if args.workload == "cfg3" else "bf16"},
+                           "precision": "fp8" if args.workload == "cfg3" else "bf16",
+                           "per_rank_ms": per_rank_ms,
+                           "rank_ms_max_over_mean": round(max(per_rank_ms)
+                                                          / (sum(per_rank_ms) / world), 4),
+                           **({"placement": place} if place else {})},
                 "e2e": {"value": round(e2e_val, 2), "unit": "audio-s/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": round(e2e_ms, 4)},

@@ -148,11 +148,31 @@ int dfm_step(void* handle, const DfmBatch* batch, void* workspace, size_t worksp
              void* stream);
 
 /* Synchronise `stream` and read (then clear) the device error word the kernels
- * of the last dfm_step on this workspace set (DFM_DEVERR_* bits). */
+ * of the last dfm_step on this workspace set (DFM_DEVERR_* bits).  When the
+ * word was non-zero it also zeroes the workspace's attention completion
+ * counters, which a launch that stopped on an error may have left set. */
 int dfm_read_error(void* handle, void* workspace, void* stream, uint32_t* err_word);
 
 int dfm_destroy(void* handle);
 const char* dfm_error_string(int code);
+
+/* One of the per-layer launches of dfm_step, alone, with exactly the
+ * arguments the tick gives it (same kernel, tiles, epilogue and workspace
+ * buffers), for timing the tick's own kernels one at a time.  The inputs the
+ * launch reads must hold what a dfm_step on the same batch and workspace left
+ * there; a LayerNorm launch adds the pending sublayer into the residual stream
+ * again, so run a full dfm_step before using its results.  No reference
+ * counterpart: the reference times its stages with CUDA events around torch
+ * calls (scripts/profile_mf_stages.py:25-48). */
+#define DFM_TICK_LN_ATTN 0    /* residual + adaLN LayerNorm before the attention */
+#define DFM_TICK_QKV 1        /* QKV GEMM + qk-norm + rotary + K/V append */
+#define DFM_TICK_ATTENTION 2  /* paged prefix attention */
+#define DFM_TICK_OPROJ 3      /* attention output projection (split-K partials) */
+#define DFM_TICK_LN_MLP 4     /* residual + adaLN LayerNorm before the MLP */
+#define DFM_TICK_FC1 5        /* fc1 + GELU(tanh) */
+#define DFM_TICK_FC2 6        /* fc2 (split-K partials) */
+int dfm_tick_launch(void* handle, const DfmBatch* batch, void* workspace, size_t workspace_bytes,
+                    int32_t kernel, int32_t step, int32_t layer, void* stream);
 
 /* ------------------------------------------------------------------ ops
  * Building blocks of the head, exported for unit tests and for callers that
@@ -167,13 +187,27 @@ int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* W, 
                int32_t N, const float* bias, void* out, int32_t out_f32, int32_t gelu,
                void* stream);
 
+/* The engine dispatch's per-tick input rows, gathered from each request's own
+ * FM history buffer (gen_state.fm_sequence, engine.py:635-688 reads the same
+ * rows) in one launch.  table: device int64 [n][4] = {address of the request's
+ * history row 0 (bf16, row stride `hidden` elements, 16-byte aligned), first
+ * graduating row, graduating row count (0..stride), address of its bf16
+ * g_cond row or 0}.  Writes ext [n, stride, hidden] (rows past the count are
+ * zero), act [n, hidden] (the row after the graduating rows: the active hidden
+ * row) and g_cond [n, hidden] (zeros where the address is 0).  The caller
+ * guarantees every row it names lies inside its buffer. */
+int dfm_gather_rows(const int64_t* table, int32_t n, int32_t hidden, int32_t stride, void* act,
+                    void* ext, void* g_cond, void* stream);
+
 /* Paged prefix attention of one (layer, step) plane pair.  Replaces
  * flash_attn_with_kvcache in the cached FM head (flash_cached_fm.py:158-161)
  * and the SDPA calls of cached_fm.extend_cache/active_forward
  * (cached_fm.py:162,194).  q, out: bf16 [n*34, heads*64] in the 34-row
  * request layout (17 graduating rows, then 17 active rows); keys and values
  * come from pool planes plane_k / plane_v.  workspace holds split-key
- * partials: at least dfm_attention_workspace_size(n, max_pages, heads) bytes. */
+ * partials: at least dfm_attention_workspace_size(n, max_pages, heads) bytes;
+ * its first word is the device error word (DFM_DEVERR_* bits, ORed, never
+ * cleared by the call); the call zeroes its completion counters itself. */
 size_t dfm_attention_workspace_size(int32_t n, int32_t max_pages, int32_t heads);
 int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t num_pages,
                         int32_t num_planes, int32_t heads, int32_t plane_k, int32_t plane_v,
@@ -199,8 +233,10 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
  *   - All calls share the one array, which keeps the last call's contents:
  *     calls that overlap on the GPU (different streams, no ordering between
  *     them) race and corrupt each other's results.
- *   - err_word (device, may be NULL) receives the DFM_DEVERR_* bits; it is not
- *     cleared by the call. */
+ *   - err_word (a device word, required: NULL returns DFM_ERR_INVALID_ARG)
+ *     receives the DFM_DEVERR_* bits of the launch, e.g. a block-table entry
+ *     outside the pool; the call ORs bits into it and never clears it, so the
+ *     caller zeroes it and reads it back after the stream has reached the call. */
 #define DFM_NOALLOC_SCRATCH_BYTES (8u << 20)
 int dfm_paged_attention_noalloc(const void* q, void* out, const void* kv_pool, int32_t num_pages,
                                 int32_t num_planes, int32_t heads, int32_t plane_k, int32_t plane_v,

@@ -16,11 +16,13 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libdfm.so")
 
 DFM_OK = 0
-DEVERR_BITS = {1: "timeout", 2: "page", 4: "len"}
+TICK_KERNELS = ("ln_attn", "qkv", "attention", "o_proj", "ln_mlp", "fc1", "fc2")  # DFM_TICK_* order
+DEVERR_TIMEOUT, DEVERR_PAGE, DEVERR_LEN = 1, 2, 4    # DFM_DEVERR_* bits of the error word
+DEVERR_BITS = {DEVERR_TIMEOUT: "timeout", DEVERR_PAGE: "page", DEVERR_LEN: "len"}
 
 EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "dfm_read_error",
            "dfm_destroy", "dfm_error_string", "dfm_linear", "dfm_attention_workspace_size",
-           "dfm_paged_attention", "dfm_paged_attention_noalloc",
+           "dfm_paged_attention", "dfm_paged_attention_noalloc", "dfm_gather_rows", "dfm_tick_launch",
            "dpe_create", "dpe_workspace_size", "dpe_pool_bytes", "dpe_decode", "dpe_read_error",
            "dpe_destroy", "dllm_decode_workspace_size", "dllm_decode_attention", "dllm_read_error",
            "dllm_create", "dllm_step_workspace_size", "dllm_decode_step", "dllm_destroy")
@@ -135,6 +137,12 @@ def lib() -> ctypes.CDLL:
                                               c_int32, c_int32, c_int32, c_void_p, c_void_p,
                                               c_void_p, c_int32, c_int32, c_void_p, c_void_p]
     L.dfm_paged_attention_noalloc.restype = c_int32
+    L.dfm_gather_rows.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                  c_void_p, c_void_p]
+    L.dfm_gather_rows.restype = c_int32
+    L.dfm_tick_launch.argtypes = [c_void_p, POINTER(DfmBatch), c_void_p, c_size_t, c_int32,
+                                  c_int32, c_int32, c_void_p]
+    L.dfm_tick_launch.restype = c_int32
     L.dpe_create.argtypes = [POINTER(DpeConfig), POINTER(DpeWeights), POINTER(c_void_p)]
     L.dpe_create.restype = c_int32
     L.dpe_workspace_size.argtypes = [c_void_p]

@@ -497,16 +497,159 @@ int dfm_read_error(void* handle, void* workspace, void* stream, uint32_t* err_wo
   CK(cudaMemcpyAsync(&v, e, sizeof(v), cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   CK(cudaMemsetAsync(e, 0, sizeof(uint32_t), s));
+  // a launch that stopped on an error may leave attention completion counters
+  // set; the next tick on this workspace must start them at zero
+  if (v) CK(cudaMemsetAsync(static_cast<uint8_t*>(workspace) + h->ws.sem, 0, h->ws.rope - h->ws.sem, s));
   *err_word = v;
   return DFM_OK;
 }
 
-int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_bytes,
-             void* stream) {
-  Handle* hd = static_cast<Handle*>(handle);
+}  // extern "C"
+
+namespace {
+
+// The per-layer launches of one tick for a given batch and workspace.  dfm_step
+// runs them in order; dfm_tick_launch runs a single one (for timing the tick's
+// own kernels in isolation).
+struct Tick {
+  Handle* hd;
+  const DfmBatch* b;
+  uint8_t* ws;
+  cudaStream_t s;
+  uint32_t* err;
+  int n, R, RL;
+  size_t modw, plane_elems, sub_plane;
+  bool fp8;
+  AttnParams ap;
+
+  Tick(Handle* h, const DfmBatch* bb, void* workspace, cudaStream_t st) : hd(h), b(bb), s(st) {
+    const DfmConfig& c = hd->c;
+    ws = static_cast<uint8_t*>(workspace);
+    err = reinterpret_cast<uint32_t*>(ws + hd->ws.err);
+    n = b->n;
+    R = kSlot * n;
+    RL = c.latent_patch * n;
+    modw = hd->mod_w;
+    plane_elems = static_cast<size_t>(c.num_pages) * c.heads * 16 * 64;
+    // the second split-K partial of `sub` (O-projection and fc2 outputs)
+    sub_plane = kOutSplit > 1 ? static_cast<size_t>(kSlot) * c.max_requests * c.hidden : 0;
+    fp8 = c.precision == DFM_PRECISION_FP8;
+    ap = AttnParams{};
+    ap.q = bf(hd->ws.qb);
+    ap.out = bf(hd->ws.ob);
+    ap.part_o = f32(hd->ws.part_o);
+    ap.part_ml = f32(hd->ws.part_ml);
+    ap.sem = reinterpret_cast<int*>(ws + hd->ws.sem);
+    ap.cache_len = b->cache_len;
+    ap.n_ext = b->n_extend;
+    ap.block_table = b->block_table;
+    ap.n = n;
+    ap.max_pages = c.max_pages_per_req;
+    ap.num_pages = c.num_pages;
+    ap.heads = c.heads;
+    ap.H = c.hidden;
+    ap.MC = hd->mc;
+    ap.ext_slots = kStride;
+    ap.q_rows = kSlot;
+    ap.err = err;
+  }
+  __nv_bfloat16* bf(size_t off) const { return reinterpret_cast<__nv_bfloat16*>(ws + off); }
+  float* f32(size_t off) const { return reinterpret_cast<float*>(ws + off); }
+  const float* mod(int k, int l) const {   // layer l's six modulation vectors at step k
+    return f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw + static_cast<size_t>(l) * 6 * hd->c.hidden;
+  }
+  float* sub() const { return f32(hd->ws.sub); }
+
+  // Residual add of the pending sublayer (gate * (sub0 + sub1), when `gate`)
+  // and adaLN LayerNorm + modulate into the next GEMM's operand rows.
+  cudaError_t ln(int M, RowMap map, const float* gate, const float* shift, const float* scale,
+                 int rows_per_req, __nv_bfloat16* out, bool to_fp8) const {
+    return launch_ln<kOutSplit, LN_ADALN>(s, M, f32(hd->ws.h), gate ? sub() : nullptr, sub_plane,
+                                          gate, map, shift, scale, static_cast<int>(modw),
+                                          rows_per_req, out, hd->c.ln_eps,
+                                          to_fp8 ? ws + hd->ws.xm8 : nullptr, f32(hd->ws.xs));
+  }
+  // LayerNorm before the attention of layer l (after layer l-1's MLP residual)
+  cudaError_t ln_attn(int k, int l) const {
+    const float* mb = mod(k, l);
+    return ln(R, kIdentity, l > 0 ? mod(k, l - 1) + 5 * hd->c.hidden : nullptr, mb,
+              mb + hd->c.hidden, kSlot, bf(hd->ws.xm), fp8);
+  }
+  // LayerNorm before the MLP of layer l (after its attention residual)
+  cudaError_t ln_mlp(int k, int l) const {
+    const int H = hd->c.hidden;
+    const float* mb = mod(k, l);
+    return ln(R, kIdentity, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, bf(hd->ws.xm), fp8);
+  }
+  cudaError_t qkv(int k, int l) const {
+    const DfmConfig& c = hd->c;
+    const DfmWeights& w = hd->w;
+    const int H = c.hidden;
+    EpiQKV eq;
+    eq.q_out = bf(hd->ws.qb);
+    eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
+    eq.plane_elems = plane_elems;
+    eq.plane_k = (l * c.nfe + k) * 2;
+    eq.plane_v = eq.plane_k + 1;
+    eq.cache_len = b->cache_len;
+    eq.n_ext = b->n_extend;
+    eq.block_table = b->block_table;
+    eq.max_pages = c.max_pages_per_req;
+    eq.num_pages = c.num_pages;
+    eq.heads = c.heads;
+    eq.H = H;
+    eq.slot = kSlot;
+    eq.ext_slots = kStride;
+    eq.qk_norm = w.qk_norm + static_cast<size_t>(l) * 4 * c.head_dim;
+    eq.rope = reinterpret_cast<const float2*>(ws + hd->ws.rope);
+    eq.max_pos = c.max_pages_per_req * 16;
+    eq.eps = c.ln_eps;
+    eq.err = err;
+    if (fp8) {
+      eq.a_scale = f32(hd->ws.xs);
+      eq.w_scale = w.qkv_ws + static_cast<size_t>(l) * 3 * H;
+      return gemm2<kQkvBN, kQkvST, EpiQKV, true>(hd->a_xm8, hd->m_qkv8[l], hd->a_xm8, R, 3 * H, H, 1,
+                                                 eq, err, s);
+    }
+    return gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s);
+  }
+  cudaError_t attention(int k, int l) {
+    ap.plane_k = (l * hd->c.nfe + k) * 2;
+    ap.plane_v = ap.plane_k + 1;
+    return launch_attention(hd->pool, hd->q_att, ap, s);
+  }
+  // attention out projection -> sub (two split-K planes); h += gate_a * sub inside the next LN
+  cudaError_t oproj(int l) const {
+    const int H = hd->c.hidden;
+    return gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, kOutSplit,
+                                 store_t<true>(hd->w.o_b + static_cast<size_t>(l) * H, kActNone),
+                                 err, s);
+  }
+  cudaError_t fc1(int l) const {
+    const DfmConfig& c = hd->c;
+    auto e1 = store_t<false>(hd->w.fc1_b + static_cast<size_t>(l) * c.ffn, kActGelu);
+    if (fp8) {
+      e1.a_scale = f32(hd->ws.xs);
+      e1.w_scale = hd->w.fc1_ws + static_cast<size_t>(l) * c.ffn;
+      return gemm2<kFc1BN, kFc1ST, EpiStoreT<false>, true>(hd->a_xm8, hd->m_fc18[l], hd->o_u, R,
+                                                          c.ffn, c.hidden, 1, e1, err, s);
+    }
+    return gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, c.hidden, 1, e1, err, s);
+  }
+  cudaError_t fc2(int l) const {
+    const DfmConfig& c = hd->c;
+    return gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, c.hidden, c.ffn, kOutSplit,
+                                 store_t<true>(hd->w.fc2_b + static_cast<size_t>(l) * c.hidden,
+                                               kActNone),
+                                 err, s);
+  }
+};
+
+// Validation shared by dfm_step and dfm_tick_launch; plans the workspace.
+int check_tick(Handle* hd, const DfmBatch* b, void* workspace, size_t workspace_bytes,
+               void* stream) {
   if (!hd || !b || !workspace) return DFM_ERR_INVALID_ARG;
   const DfmConfig& c = hd->c;
-  const DfmWeights& w = hd->w;
   const int n = b->n;
   if (n < 1 || n > c.max_requests) return DFM_ERR_INVALID_ARG;
   if (!b->noise || !b->out || !b->cache_len || !b->n_extend || !b->block_table || !b->kv_pool)
@@ -520,15 +663,31 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   CK(cudaGetDevice(&dev));
   if (dev != hd->device) return DFM_ERR_INVALID_ARG;
   if (!ensure_plan(hd, workspace, b->kv_pool, static_cast<cudaStream_t>(stream))) return DFM_ERR_CUDA;
+  return DFM_OK;
+}
 
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  uint32_t* err = reinterpret_cast<uint32_t*>(ws + hd->ws.err);
+}  // namespace
+
+extern "C" {
+
+int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_bytes,
+             void* stream) {
+  Handle* hd = static_cast<Handle*>(handle);
+  const int rc = check_tick(hd, b, workspace, workspace_bytes, stream);
+  if (rc != DFM_OK) return rc;
+  const DfmConfig& c = hd->c;
+  const DfmWeights& w = hd->w;
+  Tick tk(hd, b, workspace, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = tk.s;
+  uint8_t* ws = tk.ws;
+  uint32_t* err = tk.err;
+  const int n = b->n;
   const int H = c.hidden, L = c.layers, NFE = c.nfe, LD = c.latent_dim, LPAT = c.latent_patch;
-  const int R = kSlot * n, RL = LPAT * n;
+  const int R = tk.R, RL = tk.RL;
   const size_t modw = hd->mod_w;
-  auto bf = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
-  auto f32 = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
+  const bool ext_raw = b->ext_hidden != nullptr;
+  auto bf = [&](size_t off) { return tk.bf(off); };
+  auto f32 = [&](size_t off) { return tk.f32(off); };
   auto W = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
 
   // ---- stage inputs into fixed workspace slots (fixed TMA descriptors)
@@ -584,107 +743,26 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
     CK(cudaMemset2DAsync(xrows, kSlot * H * 2, 0, kStride * H * 2, n, s));
   }
 
-  const size_t plane_elems = static_cast<size_t>(c.num_pages) * c.heads * 16 * 64;
-  AttnParams ap{};
-  ap.q = bf(hd->ws.qb);
-  ap.out = bf(hd->ws.ob);
-  ap.part_o = f32(hd->ws.part_o);
-  ap.part_ml = f32(hd->ws.part_ml);
-  ap.sem = reinterpret_cast<int*>(ws + hd->ws.sem);
-  ap.cache_len = b->cache_len;
-  ap.n_ext = b->n_extend;
-  ap.block_table = b->block_table;
-  ap.n = n;
-  ap.max_pages = c.max_pages_per_req;
-  ap.num_pages = c.num_pages;
-  ap.heads = c.heads;
-  ap.H = H;
-  ap.MC = hd->mc;
-  ap.ext_slots = kStride;
-  ap.q_rows = kSlot;
-  ap.err = err;
-
   float* hbuf = f32(hd->ws.h);
-  float* sub = f32(hd->ws.sub);   // the last sublayer's output, added to h by the next LN
-  __nv_bfloat16* xm = bf(hd->ws.xm);
-  // the second split-K partial of `sub` (O-projection and fc2 outputs)
-  const size_t sub_plane = kOutSplit > 1 ? static_cast<size_t>(kSlot) * c.max_requests * H : 0;
-  // precision 1: the LayerNorm outputs that feed QKV and fc1 are e4m3 rows
-  const bool fp8 = c.precision == DFM_PRECISION_FP8;
-  uint8_t* xm8 = ws + hd->ws.xm8;
-  float* xs = f32(hd->ws.xs);
-  auto ln = [&](int M, RowMap map, const float* subp, const float* gate, const float* shift,
-                const float* scale, int rows_per_req, __nv_bfloat16* out, uint8_t* out8 = nullptr,
-                float* out_scale = nullptr) {
-    return launch_ln<kOutSplit, LN_ADALN>(s, M, hbuf, subp, sub_plane, gate, map, shift, scale,
-                                          static_cast<int>(modw), rows_per_req, out, c.ln_eps,
-                                          out8, out_scale);
-  };
   for (int k = 0; k < NFE; ++k) {
-    const float* mod_k = f32(hd->ws.mod) + static_cast<size_t>(k) * n * modw;
     // active latent rows = coordinate_proj(z) (batched_fm.py:117-119)
     CK(gemm<128, 6>(hd->a_zb, hd->m_coord, RL, H, LD,
                     store(xrows, H, false, w.coord_b, false, RowMap{LPAT, kSlot, kStride + 1}), err, s));
     CK(gemm<128, 6>(hd->a_xrows, hd->m_in, R, H, H, store(hbuf, H, true, w.input_b, false), err, s));
-    const float* pending_gate = nullptr;   // gate of the sublayer whose output sits in `sub`
     for (int l = 0; l < L; ++l) {
-      const float* mb = mod_k + static_cast<size_t>(l) * 6 * H;
-      CK(ln(R, kIdentity, pending_gate ? sub : nullptr, pending_gate, mb, mb + H, kSlot, xm,
-            fp8 ? xm8 : nullptr, xs));
-      EpiQKV eq;
-      eq.q_out = bf(hd->ws.qb);
-      eq.pool = static_cast<__nv_bfloat16*>(b->kv_pool);
-      eq.plane_elems = plane_elems;
-      eq.plane_k = (l * NFE + k) * 2;
-      eq.plane_v = eq.plane_k + 1;
-      eq.cache_len = b->cache_len;
-      eq.n_ext = b->n_extend;
-      eq.block_table = b->block_table;
-      eq.max_pages = c.max_pages_per_req;
-      eq.num_pages = c.num_pages;
-      eq.heads = c.heads;
-      eq.H = H;
-      eq.slot = kSlot;
-      eq.ext_slots = kStride;
-      eq.qk_norm = w.qk_norm + static_cast<size_t>(l) * 4 * c.head_dim;
-      eq.rope = reinterpret_cast<const float2*>(ws + hd->ws.rope);
-      eq.max_pos = c.max_pages_per_req * 16;
-      eq.eps = c.ln_eps;
-      eq.err = err;
-      if (fp8) {
-        eq.a_scale = xs;
-        eq.w_scale = w.qkv_ws + static_cast<size_t>(l) * 3 * H;
-        CK((gemm2<kQkvBN, kQkvST, EpiQKV, true>(hd->a_xm8, hd->m_qkv8[l], hd->a_xm8, R, 3 * H, H, 1,
-                                                eq, err, s)));
-      } else {
-        CK(gemm2<kQkvBN, kQkvST>(hd->a_xm, hd->m_qkv[l], hd->a_xm, R, 3 * H, H, 1, eq, err, s));
-      }
-      ap.plane_k = eq.plane_k;
-      ap.plane_v = eq.plane_v;
-      CK(launch_attention(hd->pool, hd->q_att, ap, s));
-      // attention out projection -> sub; h += gate_a * sub inside the next LN
-      CK(gemm2<kOutBN, kOutST>(hd->a_ob, hd->m_o[l], hd->o_sub, R, H, H, kOutSplit,
-                               store_t<true>(w.o_b + static_cast<size_t>(l) * H, kActNone), err, s));
-      CK(ln(R, kIdentity, sub, mb + 2 * H, mb + 3 * H, mb + 4 * H, kSlot, xm, fp8 ? xm8 : nullptr,
-            xs));
-      auto e1 = store_t<false>(w.fc1_b + static_cast<size_t>(l) * c.ffn, kActGelu);
-      if (fp8) {
-        e1.a_scale = xs;
-        e1.w_scale = w.fc1_ws + static_cast<size_t>(l) * c.ffn;
-        CK((gemm2<kFc1BN, kFc1ST, EpiStoreT<false>, true>(hd->a_xm8, hd->m_fc18[l], hd->o_u, R,
-                                                          c.ffn, H, 1, e1, err, s)));
-      } else {
-        CK(gemm2<kFc1BN, kFc1ST>(hd->a_xm, hd->m_fc1[l], hd->o_u, R, c.ffn, H, 1, e1, err, s));
-      }
-      CK(gemm2<kOutBN, kOutST>(hd->a_u, hd->m_fc2[l], hd->o_sub, R, H, c.ffn, kOutSplit,
-                               store_t<true>(w.fc2_b + static_cast<size_t>(l) * H, kActNone), err, s));
-      pending_gate = mb + 5 * H;
+      CK(tk.ln_attn(k, l));
+      CK(tk.qkv(k, l));
+      CK(tk.attention(k, l));
+      CK(tk.oproj(l));
+      CK(tk.ln_mlp(k, l));
+      CK(tk.fc1(l));
+      CK(tk.fc2(l));
     }
     // final layer on the 16 latent rows of each request (after the last MLP
     // residual), then z += dt * v
-    const float* mf = mod_k + static_cast<size_t>(L) * 6 * H;
-    CK(ln(RL, RowMap{LPAT, kSlot, kStride + 1}, pending_gate ? sub : nullptr, pending_gate, mf, mf + H,
-          LPAT, bf(hd->ws.xmf)));
+    const float* mf = tk.mod(k, L);
+    CK(tk.ln(RL, RowMap{LPAT, kSlot, kStride + 1}, tk.mod(k, L - 1) + 5 * H, mf, mf + H, LPAT,
+             bf(hd->ws.xmf), false));
     EpiSolver es;
     es.z = f32(hd->ws.z);
     es.zb = k == NFE - 1 ? static_cast<__nv_bfloat16*>(b->out) : bf(hd->ws.zb);
@@ -692,7 +770,29 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
     es.dt = grid.dt[k];
     CK(gemm<64, 8>(hd->a_xmf, hd->m_final, RL, LD, H, es, err, s));
   }
+  (void)modw;
   return DFM_OK;
+}
+
+int dfm_tick_launch(void* handle, const DfmBatch* b, void* workspace, size_t workspace_bytes,
+                    int32_t kernel, int32_t step, int32_t layer, void* stream) {
+  Handle* hd = static_cast<Handle*>(handle);
+  const int rc = check_tick(hd, b, workspace, workspace_bytes, stream);
+  if (rc != DFM_OK) return rc;
+  if (step < 0 || step >= hd->c.nfe || layer < 0 || layer >= hd->c.layers) return DFM_ERR_INVALID_ARG;
+  Tick tk(hd, b, workspace, static_cast<cudaStream_t>(stream));
+  cudaError_t r;
+  switch (kernel) {
+    case DFM_TICK_LN_ATTN: r = tk.ln_attn(step, layer); break;
+    case DFM_TICK_QKV: r = tk.qkv(step, layer); break;
+    case DFM_TICK_ATTENTION: r = tk.attention(step, layer); break;
+    case DFM_TICK_OPROJ: r = tk.oproj(layer); break;
+    case DFM_TICK_LN_MLP: r = tk.ln_mlp(step, layer); break;
+    case DFM_TICK_FC1: r = tk.fc1(layer); break;
+    case DFM_TICK_FC2: r = tk.fc2(layer); break;
+    default: return DFM_ERR_INVALID_ARG;
+  }
+  return r == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
 
 // ---------------------------------------------------------------- ops
@@ -733,6 +833,16 @@ int dfm_linear(const void* A, int64_t lda, int32_t M, int32_t K, const void* Wt,
   return r == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
 }
 
+int dfm_gather_rows(const int64_t* table, int32_t n, int32_t hidden, int32_t stride, void* act,
+                    void* ext, void* g_cond, void* stream) {
+  if (!table || !act || !ext || !g_cond || n < 1 || stride < 1 || hidden < 8 || hidden % 8)
+    return DFM_ERR_INVALID_ARG;
+  gather_rows_kernel<<<dim3(n, stride + 2), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const long long*>(table), hidden, stride, static_cast<__nv_bfloat16*>(act),
+      static_cast<__nv_bfloat16*>(ext), static_cast<__nv_bfloat16*>(g_cond));
+  return cudaGetLastError() == cudaSuccess ? DFM_OK : DFM_ERR_CUDA;
+}
+
 // Standalone attention workspace: [error word | partial O | partial (m, l) | counters].
 struct AttnWs {
   size_t part_o, part_ml, sem, total;
@@ -770,11 +880,14 @@ int dfm_paged_attention(const void* q, void* out, const void* kv_pool, int32_t n
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int mc = attn_chunks(max_pages);
+  const AttnWs aw = attn_ws(n, max_pages, heads);
+  // The kernel resets each completion counter it uses, but a launch that
+  // stopped early (a timed-out wait) can leave one set: start from zero.
+  if (cudaMemsetAsync(ws + aw.sem, 0, aw.total - aw.sem, s) != cudaSuccess) return DFM_ERR_CUDA;
   AttnParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.out = static_cast<__nv_bfloat16*>(out);
   p.err = reinterpret_cast<uint32_t*>(ws);
-  const AttnWs aw = attn_ws(n, max_pages, heads);
   p.part_o = reinterpret_cast<float*>(ws + aw.part_o);
   p.part_ml = reinterpret_cast<float*>(ws + aw.part_ml);
   p.sem = reinterpret_cast<int*>(ws + aw.sem);
@@ -834,7 +947,8 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
                                            const int32_t* cache_len, const int32_t* n_extend,
                                            const int32_t* block_table, int32_t max_pages,
                                            int32_t n, uint32_t* err_word, void* stream) {
-  if (!q || !out || !kv_pool || !cache_len || !n_extend || !block_table) return DFM_ERR_INVALID_ARG;
+  if (!q || !out || !kv_pool || !cache_len || !n_extend || !block_table || !err_word)
+    return DFM_ERR_INVALID_ARG;
   if (n < 1 || heads < 1 || num_pages < 1 || max_pages < 1 || plane_k < 0 || plane_v < 0 ||
       plane_k >= num_planes || plane_v >= num_planes)
     return DFM_ERR_INVALID_ARG;
@@ -847,14 +961,13 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
   if (!map_q(&qm, q, static_cast<uint64_t>(n) * TA_ROWS, heads)) return DFM_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(scratch);
-  // the array keeps the previous call's contents: clear the counters (and the
-  // internal error word) this call relies on starting at zero
+  // the array keeps the previous call's contents: clear the counters this
+  // call relies on starting at zero
   if (cudaMemsetAsync(ws + aw.sem, 0, aw.total - aw.sem, s) != cudaSuccess) return DFM_ERR_CUDA;
-  if (!err_word && cudaMemsetAsync(ws, 0, sizeof(uint32_t), s) != cudaSuccess) return DFM_ERR_CUDA;
   AttnParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.out = static_cast<__nv_bfloat16*>(out);
-  p.err = err_word ? err_word : reinterpret_cast<uint32_t*>(ws);
+  p.err = err_word;
   p.part_o = reinterpret_cast<float*>(ws + aw.part_o);
   p.part_ml = reinterpret_cast<float*>(ws + aw.part_ml);
   p.sem = reinterpret_cast<int*>(ws + aw.sem);

@@ -264,6 +264,41 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int max_po
   tab[idx] = make_float2(co, sn);
 }
 
+// The engine dispatch's per-tick inputs gathered from every request's own FM
+// history buffer in one launch.  table[i] = {row0 pointer of request i's bf16
+// history rows (row stride H), first graduating row, graduating count (<=
+// stride), g_cond pointer or 0}; then
+//   ext[i][j] = rows[first + j]   (j < count; zero rows up to stride)
+//   act[i]    = rows[first + count]       (the active hidden row)
+//   g[i]      = g_cond (or zeros)
+// (``DotsBatchEngine._pack_fm_inputs``, ``engine.py:635-688``, reads the same
+// rows of ``gen_state.fm_sequence``).  Block (i, r): one 2 KB row, 16 bytes
+// per thread.
+__global__ void __launch_bounds__(128)
+    gather_rows_kernel(const long long* __restrict__ table, int H, int stride,
+                       __nv_bfloat16* __restrict__ act, __nv_bfloat16* __restrict__ ext,
+                       __nv_bfloat16* __restrict__ g) {
+  const int i = blockIdx.x, r = blockIdx.y;
+  const long long* t = table + 4 * static_cast<size_t>(i);
+  const int count = static_cast<int>(t[2]);
+  const __nv_bfloat16* src = nullptr;
+  __nv_bfloat16* dst;
+  if (r < stride) {
+    dst = ext + (static_cast<size_t>(i) * stride + r) * H;
+    if (r < count) src = reinterpret_cast<const __nv_bfloat16*>(t[0]) + (t[1] + r) * H;
+  } else if (r == stride) {
+    dst = act + static_cast<size_t>(i) * H;
+    src = reinterpret_cast<const __nv_bfloat16*>(t[0]) + (t[1] + count) * H;
+  } else {
+    dst = g + static_cast<size_t>(i) * H;
+    src = reinterpret_cast<const __nv_bfloat16*>(t[3]);
+  }
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    const uint4 v = src ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(dst + c) = v;
+  }
+}
+
 // z = float(noise), zb = noise (the solver state and its bf16 GEMM copy).
 __global__ void init_z_kernel(const __nv_bfloat16* __restrict__ noise, int count,
                               float* __restrict__ z, __nv_bfloat16* __restrict__ zb) {

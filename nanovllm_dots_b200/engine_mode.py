@@ -22,20 +22,28 @@ Usage with the reference engine:
 """
 from __future__ import annotations
 
+import contextlib
 import weakref
 
 import torch
 
+from . import _lib
 from .fm_head import B200FMHead, FMRequest
 
 
 class B200FMDispatch:
-    """Batched FM dispatch over one ``B200FMHead`` (one per GPU/process)."""
+    """Batched FM dispatch over one ``B200FMHead`` (one per GPU/process).
 
-    def __init__(self, head: B200FMHead):
+    ``noise_fn(n)``, when set, supplies the tick's solver noise (bf16 [n, lp,
+    ld] on the head's device) instead of the reference's own draw; tests use it
+    to feed the noise a golden run used."""
+
+    def __init__(self, head: B200FMHead, noise_fn=None):
         self.head = head
         self.cfg = head.cfg
+        self.noise_fn = noise_fn
         self._cached: dict[int, int] = {}     # rid -> history rows already in the cache
+        self._g_dev: dict[int, tuple[int, torch.Tensor]] = {}   # rid -> (source id, device g_cond)
 
     def _rid(self, payload) -> int:
         rid = id(payload)
@@ -46,6 +54,7 @@ class B200FMDispatch:
 
     def _forget(self, rid: int) -> None:
         self._cached.pop(rid, None)
+        self._g_dev.pop(rid, None)
         self.head.release(rid)
 
     def plan(self, payloads):
@@ -97,34 +106,71 @@ class B200FMDispatch:
             head.prime(rids, rows, g_cond=torch.stack(gs).to(torch.bfloat16))
         return out
 
+    def _g_row(self, rid: int, p) -> int:
+        """Device address of the request's bf16 g_cond row (0 = none).  A
+        condition held elsewhere (host memory, another dtype) is copied to the
+        device once per request and reused while the payload keeps it."""
+        gc = self._g_cond(p)
+        if gc is None:
+            return 0
+        c, dev = self.cfg, self.head.device
+        if (gc.device == dev and gc.dtype == torch.bfloat16 and gc.is_contiguous()
+                and gc.numel() == c.hidden):
+            return gc.data_ptr()
+        have = self._g_dev.get(rid)
+        if have is None or have[0] != id(gc):
+            have = (id(gc), gc.reshape(-1).to(dev, torch.bfloat16).contiguous())
+            self._g_dev[rid] = have
+        return have[1].data_ptr()
+
+    def pack(self, payloads, plans):
+        """This tick's device inputs: the active hidden rows act [n, H], the
+        graduating rows ext [n, stride, H] (zero past each request's count) and
+        g_cond [n, H], gathered from every request's ``fm_sequence`` by one
+        kernel from a table of row addresses (one host-to-device copy)."""
+        c, head = self.cfg, self.head
+        dev, H, n = head.device, c.hidden, len(payloads)
+        table = []
+        for p, (rid, s, e) in zip(payloads, plans):
+            seq = p.gen_state.fm_sequence
+            if (seq.device != dev or seq.dtype != torch.bfloat16 or seq.stride(-1) != 1
+                    or seq.stride(-2) != H or seq.shape[-1] != H or seq.shape[-2] <= e):
+                raise RuntimeError("fm_sequence: expected bf16 rows of width "
+                                   f"{H} on {dev} covering the active row")
+            table.append((seq[0].data_ptr(), s, e - s, self._g_row(rid, p)))
+        tab = torch.tensor(table, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        act = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        ext = torch.empty(n, c.stride, H, dtype=torch.bfloat16, device=dev)
+        g = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        s = torch.cuda.current_stream(dev)
+        _lib.check(head.L.dfm_gather_rows(tab.data_ptr(), n, H, c.stride, act.data_ptr(),
+                                          ext.data_ptr(), g.data_ptr(),
+                                          _lib.c_void_p(s.cuda_stream)), "dfm_gather_rows")
+        return act, ext, g
+
     @torch.no_grad()
     def __call__(self, payloads) -> torch.Tensor:
         c, head = self.cfg, self.head
         dev = head.device
         plans = self._prime_backlog(payloads, self.plan(payloads))
         n = len(payloads)
-        H = c.hidden
-        act = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
-        ext = torch.zeros(n, c.stride, H, dtype=torch.bfloat16, device=dev)
-        g = torch.zeros(n, H, dtype=torch.bfloat16, device=dev)
-        n_ext = []
-        for i, (p, (rid, s, e)) in enumerate(zip(payloads, plans)):
-            seq = p.gen_state.fm_sequence
-            act[i] = seq[0, e]
-            if e > s:
-                ext[i, : e - s] = seq[0, s:e]
-            n_ext.append(e - s)
-            gc = self._g_cond(p)
-            if gc is not None:
-                g[i] = gc.to(dev, torch.bfloat16).reshape(-1)
-        # same draw as batched_meanflow (batched_fm.py:110-111) so seeded runs line up
-        noise = torch.randn((n, c.latent_patch, c.latent_dim), device=dev, dtype=torch.bfloat16)
-        rids = [r for r, _, _ in plans]
-        for rid, s, _ in plans:
-            req = head.requests.get(rid)
-            if req is not None and req.cache_len != s:
-                raise RuntimeError("FM cache out of step with the request history")
-        out = head.tick(rids, noise=noise, act_row=act, ext_rows=ext, n_extend=n_ext, g_cond=g)
+        # the head's device is current for the gather and the tick (a head on
+        # cuda:1 works while cuda:0 is the caller's current device)
+        with torch.cuda.device(dev) if dev.type == "cuda" else contextlib.nullcontext():
+            act, ext, g = self.pack(payloads, plans)
+            # same draw as batched_meanflow (batched_fm.py:110-111) so seeded runs line up
+            if self.noise_fn is not None:
+                noise = self.noise_fn(n)
+            else:
+                noise = torch.randn((n, c.latent_patch, c.latent_dim), device=dev,
+                                    dtype=torch.bfloat16)
+            rids = [r for r, _, _ in plans]
+            for rid, s, _ in plans:
+                req = head.requests.get(rid)
+                if req is not None and req.cache_len != s:
+                    raise RuntimeError("FM cache out of step with the request history")
+            out = head.tick(rids, noise=noise, act_row=act, ext_rows=ext,
+                            n_extend=[e - s for _, s, e in plans], g_cond=g)
         for rid, _, e in plans:
             self._cached[rid] = e
         return out

@@ -17,6 +17,7 @@ from __future__ import annotations
 import dataclasses
 import math
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -231,43 +232,65 @@ class B200FMHead:
     # ------------------------------------------------------------- ticks
     def prepare(self, rids, n_extend) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """Host bookkeeping for one tick: allocate pages for the graduating and
-        active rows, build (cache_len, n_extend, block_table) device tensors."""
+        active rows, build (cache_len, n_extend, block_table) device tensors
+        (packed in one buffer: one host-to-device copy)."""
         c = self.cfg
         n = len(rids)
         if not 1 <= n <= self.max_requests:
             raise RuntimeError(f"tick with {n} requests (max {self.max_requests})")
-        bt = torch.full((n, self.max_pages_per_req), -1, dtype=torch.int32)
-        cl = torch.empty(n, dtype=torch.int32)
-        for i, (rid, ne) in enumerate(zip(rids, n_extend)):
-            if not 0 <= ne <= c.stride:
-                raise RuntimeError(f"request {rid!r}: n_extend={ne} outside [0, {c.stride}]")
+        W = self.max_pages_per_req
+        buf = np.empty(2 * n + n * W, dtype=np.int32)
+        cl, ne, bt = buf[:n], buf[n:2 * n], buf[2 * n:].reshape(n, W)
+        bt.fill(-1)
+        for i, (rid, e) in enumerate(zip(rids, n_extend)):
+            if not 0 <= e <= c.stride:
+                raise RuntimeError(f"request {rid!r}: n_extend={e} outside [0, {c.stride}]")
             req = self.requests.setdefault(rid, FMRequest(rid))
-            pages = self.pages.ensure(rid, req.cache_len + ne + c.stride)
-            bt[i, : len(pages)] = torch.tensor(pages, dtype=torch.int32)
+            pages = self.pages.ensure(rid, req.cache_len + e + c.stride)
+            bt[i, :len(pages)] = pages
             cl[i] = req.cache_len
-        ne_t = torch.tensor(list(n_extend), dtype=torch.int32)
-        dev = self.device
-        return (cl.to(dev, non_blocking=True), ne_t.to(dev, non_blocking=True),
-                bt.to(dev, non_blocking=True))
+            ne[i] = e
+        d = torch.from_numpy(buf).pin_memory().to(self.device, non_blocking=True)
+        return d[:n], d[n:2 * n], d[2 * n:].view(n, W)
 
-    def launch(self, *, noise, cache_len, n_extend, block_table, out, act_hidden=None,
-               act_row=None, ext_hidden=None, ext_latent=None, ext_rows=None, g_cond=None,
-               stream=None) -> None:
-        """One ``dfm_step`` on device tensors (no host bookkeeping)."""
+    def _batch(self, *, noise, cache_len, n_extend, block_table, out, act_hidden=None,
+               act_row=None, ext_hidden=None, ext_latent=None, ext_rows=None, g_cond=None):
         for name, t in (("noise", noise), ("out", out), ("act_hidden", act_hidden),
                         ("act_row", act_row), ("ext_hidden", ext_hidden),
                         ("ext_latent", ext_latent), ("ext_rows", ext_rows), ("g_cond", g_cond)):
             if t is not None:
                 if t.dtype != torch.bfloat16 or t.device != self.device or not t.is_contiguous():
                     raise RuntimeError(f"{name}: expected a contiguous bf16 tensor on {self.device}")
+        for name, t in (("cache_len", cache_len), ("n_extend", n_extend),
+                        ("block_table", block_table)):
+            if t.dtype != torch.int32 or t.device != self.device or not t.is_contiguous():
+                raise RuntimeError(f"{name}: expected a contiguous int32 tensor on {self.device}")
         n = noise.shape[0]
-        b = _lib.DfmBatch(n, _lib.ptr(noise), _lib.ptr(act_hidden), _lib.ptr(act_row),
-                          _lib.ptr(ext_hidden), _lib.ptr(ext_latent), _lib.ptr(ext_rows),
-                          _lib.ptr(g_cond), _lib.ptr(cache_len), _lib.ptr(n_extend),
-                          _lib.ptr(block_table), _lib.ptr(self.pool), _lib.ptr(out))
+        if block_table.shape != (n, self.max_pages_per_req):
+            raise RuntimeError(f"block_table must be [n, {self.max_pages_per_req}]")
+        return _lib.DfmBatch(n, _lib.ptr(noise), _lib.ptr(act_hidden), _lib.ptr(act_row),
+                             _lib.ptr(ext_hidden), _lib.ptr(ext_latent), _lib.ptr(ext_rows),
+                             _lib.ptr(g_cond), _lib.ptr(cache_len), _lib.ptr(n_extend),
+                             _lib.ptr(block_table), _lib.ptr(self.pool), _lib.ptr(out))
+
+    def launch(self, *, stream=None, **tensors) -> None:
+        """One ``dfm_step`` on device tensors (no host bookkeeping); keyword
+        tensors as ``DfmBatch`` names them (noise, cache_len, n_extend,
+        block_table, out, and the row inputs)."""
+        b = self._batch(**tensors)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         _lib.check(self.L.dfm_step(self.handle, b, _lib.ptr(self.workspace), self.ws_bytes,
                                    _lib.c_void_p(s.cuda_stream)), "dfm_step")
+
+    def launch_kernel(self, kernel: str, step: int, layer: int, *, stream=None, **tensors) -> None:
+        """One per-layer launch of the tick (``_lib.TICK_KERNELS`` names it) with
+        the tick's own arguments, on the workspace a ``launch`` with the same
+        tensors filled (for timing the tick's kernels one at a time)."""
+        b = self._batch(**tensors)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _lib.check(self.L.dfm_tick_launch(self.handle, b, _lib.ptr(self.workspace), self.ws_bytes,
+                                          _lib.TICK_KERNELS.index(kernel), step, layer,
+                                          _lib.c_void_p(s.cuda_stream)), "dfm_tick_launch")
 
     def tick(self, rids, *, noise, act_hidden=None, act_row=None, ext_hidden=None,
              ext_latent=None, ext_rows=None, n_extend=None, g_cond=None) -> torch.Tensor:

@@ -118,6 +118,15 @@ class B200QwenDecoder:
                 raise RuntimeError(f"{name}: expected a contiguous {dt} tensor on {self.device}")
         if len(k_caches) != c.layers or len(v_caches) != c.layers:
             raise RuntimeError(f"expected {c.layers} K and V caches")
+        # every layer's cache must have the first one's block count: the kernels
+        # bound slot_mapping and the block table by it
+        shape = (k_caches[0].shape[0], c.block_size, c.kv_heads, c.head_dim)
+        for name, caches in (("k_caches", k_caches), ("v_caches", v_caches)):
+            for l, t in enumerate(caches):
+                if (t.dtype != torch.bfloat16 or t.device != self.device or not t.is_contiguous()
+                        or tuple(t.shape) != shape):
+                    raise RuntimeError(f"{name}[{l}]: expected a contiguous bf16 tensor of shape "
+                                       f"{shape} on {self.device}")
         if out is None:
             out = torch.empty(n, c.hidden, dtype=torch.bfloat16, device=self.device)
         kp = (ctypes.c_void_p * c.layers)(*[t.data_ptr() for t in k_caches])
@@ -126,15 +135,18 @@ class B200QwenDecoder:
                            _lib.ptr(context_lens), _lib.ptr(block_tables), kp, vp,
                            k_caches[0].shape[0], _lib.ptr(out))
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
-        _lib.check(self.L.dllm_decode_step(self.handle, st, _lib.ptr(self.workspace), self.ws_bytes,
-                                           _lib.c_void_p(s.cuda_stream)), "dllm_decode_step")
+        with torch.cuda.device(self.device):
+            _lib.check(self.L.dllm_decode_step(self.handle, st, _lib.ptr(self.workspace),
+                                               self.ws_bytes, _lib.c_void_p(s.cuda_stream)),
+                       "dllm_decode_step")
         return out
 
     def check_errors(self) -> None:
         v = _lib.c_uint32(0)
         s = torch.cuda.current_stream(self.device)
-        _lib.check(self.L.dllm_read_error(_lib.ptr(self.workspace), _lib.c_void_p(s.cuda_stream), v),
-                   "dllm_read_error")
+        with torch.cuda.device(self.device):
+            _lib.check(self.L.dllm_read_error(_lib.ptr(self.workspace),
+                                              _lib.c_void_p(s.cuda_stream), v), "dllm_read_error")
         if v.value:
             names = [nm for bit, nm in _lib.DEVERR_BITS.items() if v.value & bit]
             raise RuntimeError(f"LLM decode device error: {', '.join(names)} (0x{v.value:x})")

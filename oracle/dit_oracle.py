@@ -229,3 +229,26 @@ def tick_batch(w, batch, cfg: FMConfig = BASE, kv_fn=None, indices=None):
                             kv=kv_fn(i).float(), g_cond=g)
         outs.append(z)
     return torch.stack(outs, 0)
+
+
+def history_tick(w, cfg: FMConfig, rows: torch.Tensor, noise, g_cond=None):
+    """One engine tick of ONE request from its whole FM history, the way the
+    reference engine feeds ``_pack_fm_inputs`` + ``batched_meanflow``
+    (``engine.py:635-709``): ``rows`` [L, H] are the projected history rows
+    (``gen_state.fm_sequence[0, :fm_seq_len]``, ``model.py:101-120``), the last
+    one being the active hidden row.  The prefix rows [0, L-1) are causal
+    among themselves (``model.py:57-75``), so their K/V are built here by
+    graduating them through the cache path in chunks of at most ``stride``
+    rows (any chunking gives the same cache), then the active rows run against
+    it.  Returns z [lp, ld]."""
+    L = rows.shape[0]
+    kv = torch.zeros(cfg.nfe, cfg.layers, 2, 0, cfg.heads, cfg.head_dim)
+    dummy_noise = torch.zeros(cfg.latent_patch, cfg.latent_dim)
+    for s in range(0, L - 1, cfg.stride):
+        e = min(L - 1, s + cfg.stride)
+        _, new = tick_request(w, cfg, noise=dummy_noise, act_row=torch.zeros(cfg.hidden),
+                              ext_rows=rows[s:e].float(), kv=kv, g_cond=g_cond)
+        kv = torch.cat([kv, new], dim=3)
+    z, _ = tick_request(w, cfg, noise=noise, act_row=rows[L - 1].float(), ext_rows=None, kv=kv,
+                        g_cond=g_cond)
+    return z

@@ -182,7 +182,9 @@ def traj_inputs(cfg, seed, ticks):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("DFM_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("DFM_REFERENCE"),
+                    required=os.environ.get("DFM_REFERENCE") is None,
+                    help="reference checkout (or set DFM_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)

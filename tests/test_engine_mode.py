@@ -54,9 +54,19 @@ def _payload(rows: int, seed: int):
     return _Payload(rows, seed)
 
 
+def _cpu_dispatch(head):
+    """The dispatch with its device gather replaced by zero rows (no GPU here)."""
+    d = B200FMDispatch(head, noise_fn=lambda n: torch.zeros(n, syn.BASE.latent_patch,
+                                                            syn.BASE.latent_dim))
+    d.pack = lambda payloads, plans: (torch.zeros(len(plans), H),
+                                      torch.zeros(len(plans), syn.BASE.stride, H),
+                                      torch.zeros(len(plans), H))
+    return d
+
+
 def test_dispatch_graduates_history_and_primes_backlog():
     head = _FakeHead()
-    d = B200FMDispatch(head)
+    d = _cpu_dispatch(head)
     a, b = _payload(1, 0), _payload(100, 1)      # a: first patch; b: 100-row prompt
     d([a, b])
     # b's backlog: rows [0, 99) pending; all but the last 17 are bulk-prefilled

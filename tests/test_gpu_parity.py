@@ -109,15 +109,63 @@ def test_trajectory_matches_full_path(head, weights, golden):
             _assert_close(out[j].float().cpu(), gold[r][tick], f"traj{r} tick{tick}")
 
 
-def test_cfg2_scale_against_oracle(head, weights):
-    """64 requests with config-2 prefixes in one tick; a sample of requests is
-    checked against the oracle (requests are independent)."""
+def _run_checked(head, weights, batch, rids, check):
+    """One tick of every request of ``batch`` (cached prefixes installed
+    first), and the oracle's result for the requests in ``check``; each
+    request's cached K/V is drawn once and used by both."""
+    cfg = syn.BASE
+    for rid in list(head.requests):
+        head.release(rid)
+    refs = {}
+    for i, rid in enumerate(rids):
+        kv = syn.request_kv(batch, i)
+        head.write_prefix(rid, kv)
+        if i in check:
+            act, ext = O.project_rows(weights, cfg, cond=batch.cond[i],
+                                      prev_hidden=batch.prev_hidden[i],
+                                      prev_latent=batch.prev_latent[i],
+                                      n_extend=batch.n_extend[i])
+            g = None if batch.g_cond is None else batch.g_cond[i]
+            refs[i], _ = O.tick_request(weights, cfg, noise=batch.noise[i], act_row=act,
+                                        ext_rows=ext, kv=kv.float(), g_cond=g)
+        del kv
+    d = lambda t: None if t is None else t.to(DEV).contiguous()
+    out = head.tick(rids, noise=d(batch.noise), act_hidden=d(batch.cond),
+                    ext_hidden=d(batch.prev_hidden), ext_latent=d(batch.prev_latent),
+                    g_cond=d(batch.g_cond), n_extend=batch.n_extend)
+    head.check_errors()
+    return out.float().cpu(), refs
+
+
+def test_cfg2_full_tick_against_oracle(head, weights):
+    """BASELINE config 2 at full size: 64 requests with prefixes of 17*U{0..120}
+    rows in one tick; every request is checked against the oracle."""
     b = syn.config_batch("cfg2")
-    out = _run(head, b, [f"c2_{i}" for i in range(b.n)])
-    longest = max(range(b.n), key=lambda i: b.prefix_rows[i])
-    pick = sorted({0, 17, longest, min(range(b.n), key=lambda i: b.prefix_rows[i])})
-    ref = O.tick_batch(weights, b, indices=pick)
-    _assert_close(out[pick], ref, "cfg2 sample")
+    out, refs = _run_checked(head, weights, b, [f"c2_{i}" for i in range(b.n)], set(range(b.n)))
+    ref = torch.stack([refs[i] for i in range(b.n)])
+    _assert_close(out, ref, "cfg2 (64 requests)")
+
+
+def test_cfg4_mix_against_oracle(weights):
+    """BASELINE config 4's per-GPU batch: 64 requests, 75% short prefixes
+    (U{0..60} patches) and 25% long ones (U{200..320} patches, 3400-5440
+    rows, each split over two attention work units).  Every long request and
+    eight short ones are checked against the oracle."""
+    cfg = syn.BASE
+    b = syn.config_batch("cfg4")
+    pages = sum(-(-(p + 2 * cfg.stride) // cfg.page_rows) for p in b.prefix_rows) + 8
+    width = max(-(-(p + 2 * cfg.stride) // cfg.page_rows) for p in b.prefix_rows)
+    h = B200FMHead(weights, cfg, num_pages=pages, max_pages_per_req=width, max_requests=64,
+                   device=DEV)
+    long_ = [i for i in range(b.n) if b.prefix_rows[i] >= 200 * cfg.stride]
+    short = [i for i in range(b.n) if b.prefix_rows[i] < 200 * cfg.stride][:8]
+    assert len(long_) >= 8 and max(b.prefix_rows) > 4096
+    try:
+        out, refs = _run_checked(h, weights, b, [f"c4_{i}" for i in range(b.n)], set(long_ + short))
+    finally:
+        h.close()
+    pick = sorted(refs)
+    _assert_close(out[pick], torch.stack([refs[i] for i in pick]), "cfg4 mix")
 
 
 def test_graduating_rows_persist_in_cache(head, weights):

@@ -28,9 +28,19 @@ def test_noalloc_refuses_calls_beyond_its_scratch():
     L = _lib.lib()
     one = ctypes.c_void_p(1)   # never dereferenced: the size check comes first
     rc = L.dfm_paged_attention_noalloc(one, one, one, 10, 2, 16, 0, 1, one, one, one, 4000, 64,
-                                       None, None)
+                                       one, None)
     assert rc == 6
     assert b"scratch" in L.dfm_error_string(rc)
+
+
+def test_noalloc_requires_an_error_word():
+    """Device errors are reported only through the caller's error word, so a
+    call without one is refused (nothing launches)."""
+    L = _lib.lib()
+    one = ctypes.c_void_p(1)   # never dereferenced: the argument check comes first
+    rc = L.dfm_paged_attention_noalloc(one, one, one, 10, 2, 16, 0, 1, one, one, one, 4, 2,
+                                       None, None)
+    assert rc == 1
 
 
 @pytest.mark.gpu
@@ -76,3 +86,49 @@ def test_noalloc_matches_workspace_entry_point():
         assert torch.isfinite(out.float()).all(), f"call {call}"
         assert (out.float() - ref.float()).abs().max().item() < 2e-2, f"call {call}"
         assert cos_min(out, ref, 64) > 0.9999, f"call {call}"
+
+
+@pytest.mark.gpu
+def test_noalloc_reports_a_bad_block_id_through_the_error_word():
+    """A block-table entry outside the pool is reported in the caller's error
+    word (the kernel skips the page and reads zeros), and the next good call
+    on the shared scratch is unaffected."""
+    heads, num_pages, max_pages, planes = 16, 64, 8, 2
+    g = torch.Generator(device=DEV).manual_seed(3)
+    pool = torch.randn(planes, num_pages, heads, 16, 64, device=DEV, generator=g).to(torch.bfloat16)
+    n = 2
+    bt = torch.tensor([[0, 1, 2, 3, -1, -1, -1, -1], [4, 5, 10 ** 6, 7, -1, -1, -1, -1]],
+                      dtype=torch.int32, device=DEV)
+    cl = torch.tensor([30, 30], dtype=torch.int32, device=DEV)
+    ne = torch.tensor([17, 17], dtype=torch.int32, device=DEV)
+    q = torch.randn(n * 34, heads * 64, device=DEV, generator=g).to(torch.bfloat16)
+    L = _lib.lib()
+    stream = _lib.c_void_p(torch.cuda.current_stream().cuda_stream)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.empty_like(q)
+    _lib.check(L.dfm_paged_attention_noalloc(q.data_ptr(), out.data_ptr(), pool.data_ptr(),
+                                             num_pages, planes, heads, 0, 1, cl.data_ptr(),
+                                             ne.data_ptr(), bt.data_ptr(), max_pages, n,
+                                             err.data_ptr(), stream),
+               "dfm_paged_attention_noalloc")
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.DEVERR_PAGE
+    # the same call with a valid table: no error, and the result equals the
+    # workspace entry point's
+    bt[1, 2] = 6
+    err.zero_()
+    _lib.check(L.dfm_paged_attention_noalloc(q.data_ptr(), out.data_ptr(), pool.data_ptr(),
+                                             num_pages, planes, heads, 0, 1, cl.data_ptr(),
+                                             ne.data_ptr(), bt.data_ptr(), max_pages, n,
+                                             err.data_ptr(), stream),
+               "dfm_paged_attention_noalloc")
+    wsb = L.dfm_attention_workspace_size(n, max_pages, heads)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=DEV)
+    ref = torch.empty_like(q)
+    _lib.check(L.dfm_paged_attention(q.data_ptr(), ref.data_ptr(), pool.data_ptr(), num_pages,
+                                     planes, heads, 0, 1, cl.data_ptr(), ne.data_ptr(),
+                                     bt.data_ptr(), max_pages, n, ws.data_ptr(), wsb, stream),
+               "dfm_paged_attention")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(out, ref)
