@@ -23,8 +23,11 @@
 //   warp 1     TMEM owner and the single MMA-issuing thread:
 //                S^T[128 keys x 48 queries] = K . Q^T   (M=128, N=48, K=64)
 //                O[128 x 64]               += P . V     (M=128, N=64, K=128, P and V MN-major)
-//              each issued as soon as its own inputs are ready (polling); O
+//              in a fixed order (QK^T of tile g + 1, then PV of tile g); O
 //              has one TMEM buffer per unit parity
+// The producer and the MMA thread wait in mbarrier.try_wait, which suspends
+// the warp: a busy-polling warp would take issue slots from the softmax warp
+// that shares its SM sub-partition.
 //   warps 2-5  softmax: thread = one key row of S^T (TMEM lane); exponentials
 //              against a running max per query, re-reduced across the 128 rows
 //              only on a unit's first tile or when a score exceeds it by 2^16;
@@ -304,16 +307,18 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    AttnCursor ck, cv;   // next K tile, next V tile
-    attn_start(ck, p, order_s, U);
-    attn_start(cv, p, order_s, U);
+    // Tiles in order: per tile g its K then its V, each as soon as its ring
+    // slot is free.  Every wait suspends the warp in mbarrier.try_wait (no
+    // busy polling: this warp shares an SM sub-partition with a softmax warp).
+    AttnCursor cu;
+    attn_start(cu, p, order_s, U);
     // a request with invalid lengths is reported once (by its first unit)
     if (lane == 0)
       for (int u = blockIdx.x; u < U; u += gridDim.x)
         if ((u % p.heads) == 0 && ((u / p.heads) % p.MC) == 0 && attn_unit(p, order_s, u).bad)
           atomicOr(p.err, DFM_DEV_ERR_LEN);
     // one tile = 8 page boxes, issued by lanes 0..7 after lane 0 armed the barrier
-    auto load_tile = [&](uint8_t* dst, uint64_t* bar, const AttnCursor& cu, int plane) {
+    auto load_tile = [&](uint8_t* dst, uint64_t* bar, int plane) {
       if (lane == 0) mbar_arrive_expect_tx(bar, TA_KV_BYTES);
       __syncwarp();
       if (lane < TA_KT / 16) {
@@ -322,73 +327,57 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
         tma_load_5d(dst + lane * 2048, &tm_pool, bar, 0, 0, cu.f.h, page, plane);
       }
     };
-    int gk = 0, gv = 0;   // K and V tiles issued so far (ring positions)
-    uint32_t spins = 0;
-    uint64_t t_idle = 0;
-    while (!ck.done || !cv.done) {
-      int doK = 0, doV = 0, stop = 0;
-      if (lane == 0) {
-        doK = !ck.done && (gk < TA_KSLOTS ||
-                           mbar_test(&k_empty[gk % TA_KSLOTS], ((gk / TA_KSLOTS) & 1) ^ 1));
-        if (doK && ck.t == 0)   // a new unit: its page ids and query buffer must be free
-          doK = ck.seq <= cv.seq + 1 &&
-                (ck.seq < 2 || mbar_test(&q_empty[ck.seq & 1], ((ck.seq >> 1) & 1) ^ 1));
-        doV = !cv.done && gv < gk &&
-              (gv < TA_VSLOTS ||
-               mbar_test(&v_empty[gv % TA_VSLOTS], ((gv / TA_VSLOTS) & 1) ^ 1));
-        if (doK || doV) {
-          spins = 0;
-          t_idle = 0;
-        } else if ((++spins & 255) == 0) {
-          if (t_idle == 0) t_idle = globaltimer();
-          else if (globaltimer() - t_idle > DFM_WAIT_LIMIT_NS) {
-            *abort_flag = 1;
-            atomicOr(p.err, DFM_DEV_ERR_TIMEOUT);
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
+    };
+    int g = 0;   // tiles issued so far (ring positions)
+#pragma unroll 1
+    while (!cu.done) {
+      if (cu.t == 0) {
+        // A new unit: its query buffer is free once the last QK^T of the unit
+        // two before has read it.  Its page-id buffer was last used by that
+        // unit too, whose loads were all issued before this one's.
+        if (cu.seq >= 2 && !wait_all(&q_empty[cu.seq & 1], ((cu.seq >> 1) & 1) ^ 1)) break;
+        // The unit's page ids: pages past the request's keys, or invalid
+        // table entries, become an out-of-range page index so TMA fills
+        // those boxes with zeros.
+        const int pg0 = cu.f.k0 >> 4;
+        const int npg = cu.f.ntiles * (TA_KT / 16);
+        const int* bt = p.block_table + static_cast<size_t>(cu.f.i) * p.max_pages;
+        int* ps = page_s + (cu.seq & 1) * TA_MAX_PAGES;
+        for (int x = lane; x < npg && x < TA_MAX_PAGES; x += 32) {
+          const int pidx = pg0 + x;
+          int page = p.num_pages;
+          if (pidx * 16 < cu.f.total) {
+            const int e = pidx < p.max_pages ? bt[pidx] : -1;
+            if (e >= 0 && e < p.num_pages) page = e;
+            else atomicOr(p.err, DFM_DEV_ERR_PAGE);
           }
+          ps[x] = page;
         }
-        stop = *abort_flag;
-      }
-      doK = __shfl_sync(0xffffffffu, doK, 0);
-      doV = __shfl_sync(0xffffffffu, doV, 0);
-      if (__shfl_sync(0xffffffffu, stop, 0)) break;
-      if (doK) {
-        if (ck.t == 0) {
-          // The unit's page ids: pages past the request's keys, or invalid
-          // table entries, become an out-of-range page index so TMA fills
-          // those boxes with zeros.
-          const int pg0 = ck.f.k0 >> 4;
-          const int npg = ck.f.ntiles * (TA_KT / 16);
-          const int* bt = p.block_table + static_cast<size_t>(ck.f.i) * p.max_pages;
-          int* ps = page_s + (ck.seq & 1) * TA_MAX_PAGES;
-          for (int x = lane; x < npg && x < TA_MAX_PAGES; x += 32) {
-            const int pidx = pg0 + x;
-            int page = p.num_pages;
-            if (pidx * 16 < ck.f.total) {
-              const int e = pidx < p.max_pages ? bt[pidx] : -1;
-              if (e >= 0 && e < p.num_pages) page = e;
-              else atomicOr(p.err, DFM_DEV_ERR_PAGE);
-            }
-            ps[x] = page;
-          }
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&q_full[ck.seq & 1], TA_Q_BYTES);
-            tma_load_2d(sQ + (ck.seq & 1) * TA_Q_BYTES, &tm_q, &q_full[ck.seq & 1], ck.f.h * 64,
-                        ck.f.i * p.q_rows);
-          }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&q_full[cu.seq & 1], TA_Q_BYTES);
+          tma_load_2d(sQ + (cu.seq & 1) * TA_Q_BYTES, &tm_q, &q_full[cu.seq & 1], cu.f.h * 64,
+                      cu.f.i * p.q_rows);
         }
-        load_tile(sK + (gk % TA_KSLOTS) * TA_KV_BYTES, &k_full[gk % TA_KSLOTS], ck, p.plane_k);
-        ++gk;
-        attn_step(ck, p, order_s, U);
       }
-      if (doV) {
-        load_tile(sV + (gv % TA_VSLOTS) * TA_KV_BYTES, &v_full[gv % TA_VSLOTS], cv, p.plane_v);
-        ++gv;
-        attn_step(cv, p, order_s, U);
-      }
+      if (g >= TA_KSLOTS &&
+          !wait_all(&k_empty[g % TA_KSLOTS], ((g / TA_KSLOTS) & 1) ^ 1))
+        break;
+      load_tile(sK + (g % TA_KSLOTS) * TA_KV_BYTES, &k_full[g % TA_KSLOTS], p.plane_k);
+      if (g >= TA_VSLOTS &&
+          !wait_all(&v_empty[g % TA_VSLOTS], ((g / TA_VSLOTS) & 1) ^ 1))
+        break;
+      load_tile(sV + (g % TA_VSLOTS) * TA_KV_BYTES, &v_full[g % TA_VSLOTS], p.plane_v);
+      ++g;
+      attn_step(cu, p, order_s, U);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // One thread issues in a fixed order: QK^T of tile g + 1 before the PV
+    // product of tile g (the softmax of tile g + 1 needs its scores when it is
+    // done with tile g), every wait a suspending try_wait.
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, TA_QN);
       constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(128, 64) | (1u << 15);  // A MN-major too
@@ -397,13 +386,20 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
       attn_start(c1, p, order_s, U);
       attn_start(c2, p, order_s, U);
       int g1 = 0, g2 = 0;
-      uint32_t spins = 0;
-      uint64_t t_idle = 0;
-      while (!c2.done && !*abort_flag) {
-        bool prog = false;
-        if (!c1.done && mbar_test(&k_full[g1 % TA_KSLOTS], (g1 / TA_KSLOTS) & 1) &&
-            (g1 < 2 || mbar_test(&s_empty[g1 & 1], ((g1 >> 1) & 1) ^ 1)) &&
-            (c1.t > 0 || mbar_test(&q_full[c1.seq & 1], (c1.seq >> 1) & 1))) {
+      bool ok = true;
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return mbar_wait(bar, parity, abort_flag, p.err);
+      };
+#pragma unroll 1
+      while (ok && !c2.done) {
+#pragma unroll 1
+        while (!c1.done && g1 < g2 + 2) {
+          if (!wait(&k_full[g1 % TA_KSLOTS], (g1 / TA_KSLOTS) & 1) ||
+              (g1 >= 2 && !wait(&s_empty[g1 & 1], ((g1 >> 1) & 1) ^ 1)) ||
+              (c1.t == 0 && !wait(&q_full[c1.seq & 1], (c1.seq >> 1) & 1))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sK + (g1 % TA_KSLOTS) * TA_KV_BYTES);
           const uint32_t q_addr = smem_u32(sQ + (c1.seq & 1) * TA_Q_BYTES);
@@ -416,36 +412,26 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
           if (c1.t == c1.f.ntiles - 1) umma_commit(&q_empty[c1.seq & 1]);
           ++g1;
           attn_step(c1, p, order_s, U);
-          prog = true;
         }
-        if (g2 < g1 && mbar_test(&p_full[g2 % TA_PSLOTS], (g2 / TA_PSLOTS) & 1) &&
-            mbar_test(&v_full[g2 % TA_VSLOTS], (g2 / TA_VSLOTS) & 1) &&
-            (c2.t > 0 || c2.seq < 2 || mbar_test(&o_empty[c2.seq & 1], ((c2.seq >> 1) & 1) ^ 1))) {
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + (g2 % TA_VSLOTS) * TA_KV_BYTES);
-          const uint32_t o_col = tmem + TA_O_COL + (c2.seq & 1) * 64;
+        if (!ok) break;
+        if (!wait(&p_full[g2 % TA_PSLOTS], (g2 / TA_PSLOTS) & 1) ||
+            !wait(&v_full[g2 % TA_VSLOTS], (g2 / TA_VSLOTS) & 1) ||
+            (c2.t == 0 && c2.seq >= 2 &&
+             !wait(&o_empty[c2.seq & 1], ((c2.seq >> 1) & 1) ^ 1)))
+          break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (g2 % TA_VSLOTS) * TA_KV_BYTES);
+        const uint32_t o_col = tmem + TA_O_COL + (c2.seq & 1) * 64;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(o_col,
-                      umma_desc_sw128_mn(p_addr + (g2 % TA_PSLOTS) * TA_P_BYTES + kk * 2048,
-                                         TA_P_BYTES),
-                      umma_desc_sw128(v_addr + kk * 2048), idesc_o, (c2.t > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&v_empty[g2 % TA_VSLOTS]);
-          umma_commit(&p_empty[g2 % TA_PSLOTS]);
-          ++g2;
-          attn_step(c2, p, order_s, U);
-          prog = true;
-        }
-        if (prog) {
-          spins = 0;
-          t_idle = 0;
-        } else if ((++spins & 255) == 0) {
-          if (t_idle == 0) t_idle = globaltimer();
-          else if (globaltimer() - t_idle > DFM_WAIT_LIMIT_NS) {
-            *abort_flag = 1;
-            atomicOr(p.err, DFM_DEV_ERR_TIMEOUT);
-          }
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(o_col,
+                    umma_desc_sw128_mn(p_addr + (g2 % TA_PSLOTS) * TA_P_BYTES + kk * 2048,
+                                       TA_P_BYTES),
+                    umma_desc_sw128(v_addr + kk * 2048), idesc_o, (c2.t > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[g2 % TA_VSLOTS]);
+        umma_commit(&p_empty[g2 % TA_PSLOTS]);
+        ++g2;
+        attn_step(c2, p, order_s, U);
       }
     }
   } else {
