@@ -23,11 +23,8 @@
 //   warp 1     TMEM owner and the single MMA-issuing thread:
 //                S^T[128 keys x 48 queries] = K . Q^T   (M=128, N=48, K=64)
 //                O[128 x 64]               += P . V     (M=128, N=64, K=128, P and V MN-major)
-//              in a fixed order (QK^T of tile g + 1, then PV of tile g); O
+//              each issued as soon as its own inputs are ready (polling); O
 //              has one TMEM buffer per unit parity
-// The producer and the MMA thread wait in mbarrier.try_wait, which suspends
-// the warp: a busy-polling warp would take issue slots from the softmax warp
-// that shares its SM sub-partition.
 //   warps 2-5  softmax: thread = one key row of S^T (TMEM lane); exponentials
 //              against a running max per query, re-reduced across the 128 rows
 //              only on a unit's first tile or when a score exceeds it by 2^16;
@@ -97,8 +94,6 @@ struct AttnParams {
                              // encoder's 8); the 40-row query box then also carries
                              // the next requests' rows, whose outputs are not written
   uint32_t* err;
-  int meta_early;            // 1: cache_len / n_ext / block_table may be read before the
-                             // wait for the previous kernel (no kernel of the tick writes them)
 };
 
 // Reduce-scatter of 32 per-lane values across a warp: afterwards lane l holds
@@ -149,35 +144,19 @@ struct AttnUnit {
   bool bad;                // the request's lengths are invalid
 };
 
-// Request lengths packed for shared memory: (cache_len << 6) | n_ext, or -1
-// for lengths no unit may use.
-DFM_DEV int attn_pack_len(int P, int ne, int ext_slots) {
-  return (P < 0 || P >= (1 << 24) || ne < 0 || ne > ext_slots || ne > 63) ? -1 : (P << 6) | ne;
-}
-
-// order_s: [TA_MAX_ORDER] requests longest first, then [TA_MAX_ORDER] packed
-// lengths (when n <= TA_MAX_ORDER; otherwise requests in index order, lengths
-// read from global memory).
 DFM_DEV AttnUnit attn_unit(const AttnParams& p, const int* order_s, int u) {
   AttnUnit f;
   f.h = u % p.heads;
   f.c = (u / p.heads) % p.MC;
   const int r = u / (p.heads * p.MC);
-  int packed;
-  if (p.n <= TA_MAX_ORDER) {
-    f.i = order_s[r];
-    packed = order_s[TA_MAX_ORDER + f.i];
-  } else {
-    f.i = r;
-    packed = attn_pack_len(p.cache_len[f.i], p.n_ext[f.i], p.ext_slots);
-  }
-  f.P = packed >> 6;
-  f.ne = packed & 63;
+  f.i = p.n <= TA_MAX_ORDER ? order_s[r] : r;
+  f.P = p.cache_len[f.i];
+  f.ne = p.n_ext[f.i];
   f.total = f.P + f.ne + (TA_ROWS - p.ext_slots);
   f.k0 = 0;
   f.ntiles = 0;
   f.nchunks = 0;
-  f.bad = packed < 0 || f.total > p.max_pages * 16;
+  f.bad = f.P < 0 || f.ne < 0 || f.ne > p.ext_slots || f.total > p.max_pages * 16;
   if (f.bad) return f;
   f.nchunks = (f.total + TA_CH - 1) / TA_CH;
   if (f.c >= f.nchunks || f.nchunks > p.MC) return f;
@@ -239,11 +218,7 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
     tma_prefetch(&tm_pool);
     tma_prefetch(&tm_q);
   }
-  // Lengths and block tables are inputs of the whole tick (no kernel of the
-  // tick writes them), so inside a tick they are read before the wait for the
-  // previous kernel; a standalone call waits first (its caller may have just
-  // written them).
-  if (!p.meta_early) pdl_wait();
+  pdl_wait();
   const int U = p.n * p.MC * p.heads;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -275,38 +250,22 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
   float* vals = red + 3 * 4 * TA_ROWS;                               // [34]
   float* mfin = vals + TA_ROWS;                                      // [34]
   float* m_s = mfin + TA_ROWS;                                       // [2][34]
-  int* page_s = reinterpret_cast<int*>(m_s + 2 * TA_ROWS);           // [TA_MAX_PAGES]
-  int* order_s = page_s + TA_MAX_PAGES;                              // [2][TA_MAX_ORDER]
-  static_assert(TA_MISC_RED + (3 * 4 + 5) * TA_ROWS * 4 + (TA_MAX_PAGES + 2 * TA_MAX_ORDER) * 4 <=
+  int* page_s = reinterpret_cast<int*>(m_s + 2 * TA_ROWS);           // [2][TA_MAX_PAGES]
+  int* order_s = page_s + 2 * TA_MAX_PAGES;                          // [TA_MAX_ORDER]
+  static_assert(TA_MISC_RED + (3 * 4 + 5) * TA_ROWS * 4 + (2 * TA_MAX_PAGES + TA_MAX_ORDER) * 4 <=
                     TA_MISC_BYTES, "misc area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // every request's lengths (packed) and the requests in longest-first order
-  // (ties by index), once per CTA; CTA 0 reports invalid lengths
+  // requests in longest-first order (ties by index), once per CTA; the
+  // lengths sit in the page-id buffer until the producer first uses it
   if (p.n <= TA_MAX_ORDER) {
-    int* len_s = order_s + TA_MAX_ORDER;
-    for (int x = threadIdx.x; x < p.n; x += blockDim.x) {
-      const int v = attn_pack_len(p.cache_len[x], p.n_ext[x], p.ext_slots);
-      len_s[x] = v;
-      if (blockIdx.x == 0 &&
-          (v < 0 || (v >> 6) + (v & 63) + (TA_ROWS - p.ext_slots) > p.max_pages * 16))
-        atomicOr(p.err, DFM_DEV_ERR_LEN);
-    }
+    int* len_s = page_s;
+    for (int x = threadIdx.x; x < p.n; x += blockDim.x) len_s[x] = p.cache_len[x] + p.n_ext[x];
     __syncthreads();
     for (int x = threadIdx.x; x < p.n; x += blockDim.x) {
-      const int lx = len_s[x] < 0 ? -1 : (len_s[x] >> 6) + (len_s[x] & 63);
       int rank = 0;
-      for (int y = 0; y < p.n; ++y) {
-        const int ly = len_s[y] < 0 ? -1 : (len_s[y] >> 6) + (len_s[y] & 63);
-        rank += (ly > lx) || (ly == lx && y < x);
-      }
+      for (int y = 0; y < p.n; ++y) rank += (len_s[y] > len_s[x]) || (len_s[y] == len_s[x] && y < x);
       order_s[rank] = x;
-    }
-  } else if (blockIdx.x == 0) {
-    for (int x = threadIdx.x; x < p.n; x += blockDim.x) {
-      const int v = attn_pack_len(p.cache_len[x], p.n_ext[x], p.ext_slots);
-      if (v < 0 || (v >> 6) + (v & 63) + (TA_ROWS - p.ext_slots) > p.max_pages * 16)
-        atomicOr(p.err, DFM_DEV_ERR_LEN);
     }
   }
   if (threadIdx.x == 0) {
@@ -345,96 +304,91 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // Tiles in order: per tile g its K then its V, each as soon as its ring
-    // slot is free.  Every wait suspends the warp in mbarrier.try_wait (no
-    // busy polling: this warp shares an SM sub-partition with a softmax warp).
-    AttnCursor cu;
-    attn_start(cu, p, order_s, U);
+    AttnCursor ck, cv;   // next K tile, next V tile
+    attn_start(ck, p, order_s, U);
+    attn_start(cv, p, order_s, U);
+    // a request with invalid lengths is reported once (by its first unit)
+    if (lane == 0)
+      for (int u = blockIdx.x; u < U; u += gridDim.x)
+        if ((u % p.heads) == 0 && ((u / p.heads) % p.MC) == 0 && attn_unit(p, order_s, u).bad)
+          atomicOr(p.err, DFM_DEV_ERR_LEN);
     // one tile = 8 page boxes, issued by lanes 0..7 after lane 0 armed the barrier
-    auto load_tile = [&](uint8_t* dst, uint64_t* bar, int plane) {
+    auto load_tile = [&](uint8_t* dst, uint64_t* bar, const AttnCursor& cu, int plane) {
       if (lane == 0) mbar_arrive_expect_tx(bar, TA_KV_BYTES);
       __syncwarp();
       if (lane < TA_KT / 16) {
         const int x = cu.t * (TA_KT / 16) + lane;
-        const int page = x < TA_MAX_PAGES ? page_s[x] : p.num_pages;
+        const int page = x < TA_MAX_PAGES ? page_s[(cu.seq & 1) * TA_MAX_PAGES + x] : p.num_pages;
         tma_load_5d(dst + lane * 2048, &tm_pool, bar, 0, 0, cu.f.h, page, plane);
       }
     };
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.err));
-    };
-    // A unit's block-table entries, lane-strided, loaded into registers one
-    // unit ahead (the loads complete while the previous unit streams).
-    // kBeyond marks pages past the request's keys (read as zeros, no error).
-    constexpr int kPf = (TA_MAX_PAGES + 31) / 32;
-    constexpr int kBeyond = -0x7fffffff;
-    int pf[kPf];
-    auto fetch_pages = [&](const AttnUnit& f) {
-      const int pg0 = f.k0 >> 4;
-      const int npg = f.ntiles * (TA_KT / 16);
-      const int* bt = p.block_table + static_cast<size_t>(f.i) * p.max_pages;
-#pragma unroll
-      for (int j = 0; j < kPf; ++j) {
-        const int x = lane + 32 * j;
-        const int pidx = pg0 + x;
-        pf[j] = kBeyond;
-        if (x < npg && x < TA_MAX_PAGES && pidx * 16 < f.total)
-          pf[j] = pidx < p.max_pages ? __ldg(bt + pidx) : -1;
-      }
-    };
-    if (!cu.done) fetch_pages(cu.f);
-    if (p.meta_early) pdl_wait();   // K/V and q are written by the previous kernel
-    int g = 0;   // tiles issued so far (ring positions)
-#pragma unroll 1
-    while (!cu.done) {
-      if (cu.t == 0) {
-        // A new unit: its query buffer is free once the last QK^T of the unit
-        // two before has read it.  The page-id buffer's previous unit has
-        // issued all its loads (they go in order).
-        if (cu.seq >= 2 && !wait_all(&q_empty[cu.seq & 1], ((cu.seq >> 1) & 1) ^ 1)) break;
-        // Out-of-range entries and pages past the request's keys become an
-        // out-of-range page index, so TMA fills those boxes with zeros.
-#pragma unroll
-        for (int j = 0; j < kPf; ++j) {
-          const int x = lane + 32 * j;
-          if (x < TA_MAX_PAGES) {
-            int page = p.num_pages;
-            if (pf[j] != kBeyond) {
-              if (pf[j] >= 0 && pf[j] < p.num_pages) page = pf[j];
-              else atomicOr(p.err, DFM_DEV_ERR_PAGE);
-            }
-            page_s[x] = page;
+    int gk = 0, gv = 0;   // K and V tiles issued so far (ring positions)
+    uint32_t spins = 0;
+    uint64_t t_idle = 0;
+    while (!ck.done || !cv.done) {
+      int doK = 0, doV = 0, stop = 0;
+      if (lane == 0) {
+        doK = !ck.done && (gk < TA_KSLOTS ||
+                           mbar_test(&k_empty[gk % TA_KSLOTS], ((gk / TA_KSLOTS) & 1) ^ 1));
+        if (doK && ck.t == 0)   // a new unit: its page ids and query buffer must be free
+          doK = ck.seq <= cv.seq + 1 &&
+                (ck.seq < 2 || mbar_test(&q_empty[ck.seq & 1], ((ck.seq >> 1) & 1) ^ 1));
+        doV = !cv.done && gv < gk &&
+              (gv < TA_VSLOTS ||
+               mbar_test(&v_empty[gv % TA_VSLOTS], ((gv / TA_VSLOTS) & 1) ^ 1));
+        if (doK || doV) {
+          spins = 0;
+          t_idle = 0;
+        } else if ((++spins & 255) == 0) {
+          if (t_idle == 0) t_idle = globaltimer();
+          else if (globaltimer() - t_idle > DFM_WAIT_LIMIT_NS) {
+            *abort_flag = 1;
+            atomicOr(p.err, DFM_DEV_ERR_TIMEOUT);
           }
         }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&q_full[cu.seq & 1], TA_Q_BYTES);
-          tma_load_2d(sQ + (cu.seq & 1) * TA_Q_BYTES, &tm_q, &q_full[cu.seq & 1], cu.f.h * 64,
-                      cu.f.i * p.q_rows);
-        }
-        // the next unit's entries, while this one streams
-        AttnCursor nx = cu;
-        nx.t = cu.f.ntiles - 1;
-        attn_step(nx, p, order_s, U);
-        if (!nx.done) fetch_pages(nx.f);
+        stop = *abort_flag;
       }
-      if (g >= TA_KSLOTS &&
-          !wait_all(&k_empty[g % TA_KSLOTS], ((g / TA_KSLOTS) & 1) ^ 1))
-        break;
-      load_tile(sK + (g % TA_KSLOTS) * TA_KV_BYTES, &k_full[g % TA_KSLOTS], p.plane_k);
-      if (g >= TA_VSLOTS &&
-          !wait_all(&v_empty[g % TA_VSLOTS], ((g / TA_VSLOTS) & 1) ^ 1))
-        break;
-      load_tile(sV + (g % TA_VSLOTS) * TA_KV_BYTES, &v_full[g % TA_VSLOTS], p.plane_v);
-      ++g;
-      attn_step(cu, p, order_s, U);
+      doK = __shfl_sync(0xffffffffu, doK, 0);
+      doV = __shfl_sync(0xffffffffu, doV, 0);
+      if (__shfl_sync(0xffffffffu, stop, 0)) break;
+      if (doK) {
+        if (ck.t == 0) {
+          // The unit's page ids: pages past the request's keys, or invalid
+          // table entries, become an out-of-range page index so TMA fills
+          // those boxes with zeros.
+          const int pg0 = ck.f.k0 >> 4;
+          const int npg = ck.f.ntiles * (TA_KT / 16);
+          const int* bt = p.block_table + static_cast<size_t>(ck.f.i) * p.max_pages;
+          int* ps = page_s + (ck.seq & 1) * TA_MAX_PAGES;
+          for (int x = lane; x < npg && x < TA_MAX_PAGES; x += 32) {
+            const int pidx = pg0 + x;
+            int page = p.num_pages;
+            if (pidx * 16 < ck.f.total) {
+              const int e = pidx < p.max_pages ? bt[pidx] : -1;
+              if (e >= 0 && e < p.num_pages) page = e;
+              else atomicOr(p.err, DFM_DEV_ERR_PAGE);
+            }
+            ps[x] = page;
+          }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&q_full[ck.seq & 1], TA_Q_BYTES);
+            tma_load_2d(sQ + (ck.seq & 1) * TA_Q_BYTES, &tm_q, &q_full[ck.seq & 1], ck.f.h * 64,
+                        ck.f.i * p.q_rows);
+          }
+        }
+        load_tile(sK + (gk % TA_KSLOTS) * TA_KV_BYTES, &k_full[gk % TA_KSLOTS], ck, p.plane_k);
+        ++gk;
+        attn_step(ck, p, order_s, U);
+      }
+      if (doV) {
+        load_tile(sV + (gv % TA_VSLOTS) * TA_KV_BYTES, &v_full[gv % TA_VSLOTS], cv, p.plane_v);
+        ++gv;
+        attn_step(cv, p, order_s, U);
+      }
     }
   } else if (warp == 1) {
-    if (p.meta_early) pdl_wait();
     // ------------------------------------------------------------ MMA issuer
-    // One thread issues in a fixed order: QK^T of tile g + 1 before the PV
-    // product of tile g (the softmax of tile g + 1 needs its scores when it is
-    // done with tile g), every wait a suspending try_wait.
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, TA_QN);
       constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(128, 64) | (1u << 15);  // A MN-major too
@@ -443,20 +397,13 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
       attn_start(c1, p, order_s, U);
       attn_start(c2, p, order_s, U);
       int g1 = 0, g2 = 0;
-      bool ok = true;
-      auto wait = [&](uint64_t* bar, uint32_t parity) {
-        return mbar_wait(bar, parity, abort_flag, p.err);
-      };
-#pragma unroll 1
-      while (ok && !c2.done) {
-#pragma unroll 1
-        while (!c1.done && g1 < g2 + 2) {
-          if (!wait(&k_full[g1 % TA_KSLOTS], (g1 / TA_KSLOTS) & 1) ||
-              (g1 >= 2 && !wait(&s_empty[g1 & 1], ((g1 >> 1) & 1) ^ 1)) ||
-              (c1.t == 0 && !wait(&q_full[c1.seq & 1], (c1.seq >> 1) & 1))) {
-            ok = false;
-            break;
-          }
+      uint32_t spins = 0;
+      uint64_t t_idle = 0;
+      while (!c2.done && !*abort_flag) {
+        bool prog = false;
+        if (!c1.done && mbar_test(&k_full[g1 % TA_KSLOTS], (g1 / TA_KSLOTS) & 1) &&
+            (g1 < 2 || mbar_test(&s_empty[g1 & 1], ((g1 >> 1) & 1) ^ 1)) &&
+            (c1.t > 0 || mbar_test(&q_full[c1.seq & 1], (c1.seq >> 1) & 1))) {
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sK + (g1 % TA_KSLOTS) * TA_KV_BYTES);
           const uint32_t q_addr = smem_u32(sQ + (c1.seq & 1) * TA_Q_BYTES);
@@ -469,30 +416,39 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
           if (c1.t == c1.f.ntiles - 1) umma_commit(&q_empty[c1.seq & 1]);
           ++g1;
           attn_step(c1, p, order_s, U);
+          prog = true;
         }
-        if (!ok) break;
-        if (!wait(&p_full[g2 % TA_PSLOTS], (g2 / TA_PSLOTS) & 1) ||
-            !wait(&v_full[g2 % TA_VSLOTS], (g2 / TA_VSLOTS) & 1) ||
-            (c2.t == 0 && c2.seq >= 2 &&
-             !wait(&o_empty[c2.seq & 1], ((c2.seq >> 1) & 1) ^ 1)))
-          break;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + (g2 % TA_VSLOTS) * TA_KV_BYTES);
-        const uint32_t o_col = tmem + TA_O_COL + (c2.seq & 1) * 64;
+        if (g2 < g1 && mbar_test(&p_full[g2 % TA_PSLOTS], (g2 / TA_PSLOTS) & 1) &&
+            mbar_test(&v_full[g2 % TA_VSLOTS], (g2 / TA_VSLOTS) & 1) &&
+            (c2.t > 0 || c2.seq < 2 || mbar_test(&o_empty[c2.seq & 1], ((c2.seq >> 1) & 1) ^ 1))) {
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sV + (g2 % TA_VSLOTS) * TA_KV_BYTES);
+          const uint32_t o_col = tmem + TA_O_COL + (c2.seq & 1) * 64;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(o_col,
-                    umma_desc_sw128_mn(p_addr + (g2 % TA_PSLOTS) * TA_P_BYTES + kk * 2048,
-                                       TA_P_BYTES),
-                    umma_desc_sw128(v_addr + kk * 2048), idesc_o, (c2.t > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&v_empty[g2 % TA_VSLOTS]);
-        umma_commit(&p_empty[g2 % TA_PSLOTS]);
-        ++g2;
-        attn_step(c2, p, order_s, U);
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(o_col,
+                      umma_desc_sw128_mn(p_addr + (g2 % TA_PSLOTS) * TA_P_BYTES + kk * 2048,
+                                         TA_P_BYTES),
+                      umma_desc_sw128(v_addr + kk * 2048), idesc_o, (c2.t > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&v_empty[g2 % TA_VSLOTS]);
+          umma_commit(&p_empty[g2 % TA_PSLOTS]);
+          ++g2;
+          attn_step(c2, p, order_s, U);
+          prog = true;
+        }
+        if (prog) {
+          spins = 0;
+          t_idle = 0;
+        } else if ((++spins & 255) == 0) {
+          if (t_idle == 0) t_idle = globaltimer();
+          else if (globaltimer() - t_idle > DFM_WAIT_LIMIT_NS) {
+            *abort_flag = 1;
+            atomicOr(p.err, DFM_DEV_ERR_TIMEOUT);
+          }
+        }
       }
     }
   } else {
-    if (p.meta_early) pdl_wait();
     // ------------------------------------------------------------ softmax warps
     const int q4 = warp & 3;            // TMEM lane quadrant of this warp
     const int sw = warp - 2;            // 0..3

@@ -222,19 +222,16 @@ EpiStore store(void* out, int ldo, bool f32, const float* bias, bool gelu, RowMa
   return e;
 }
 
-int sm_count();
-
-// Residual + LayerNorm launch: a couple of blocks per SM walking row pairs
-// (ln_mod_kernel).
+// Residual + LayerNorm launch (ln_mod_kernel: two rows per block; every block
+// resident at once, so all rows' loads are in flight together).
 template <int NSUB, int MODE>
 cudaError_t launch_ln(cudaStream_t s, int M, float* h, const float* sub, size_t sub_plane,
                       const float* gate, RowMap map, const float* shift, const float* scale,
                       int mod_ld, int rows_per_req, __nv_bfloat16* out, float eps, uint8_t* out8,
                       float* out_scale) {
-  const int pairs = (M + LN_ROWS_PER_BLOCK - 1) / LN_ROWS_PER_BLOCK;
-  const int cap = LN_BLOCKS_PER_SM * sm_count();
-  return launch_pdl(ln_mod_kernel<NSUB, MODE>, dim3(pairs < cap ? pairs : cap), dim3(LN_THREADS), 0,
-                    s, h, sub, sub_plane, gate, M, map, shift, scale, mod_ld, rows_per_req, out, eps,
+  return launch_pdl(ln_mod_kernel<NSUB, MODE>,
+                    dim3((M + LN_ROWS_PER_BLOCK - 1) / LN_ROWS_PER_BLOCK), dim3(LN_THREADS), 0, s,
+                    h, sub, sub_plane, gate, M, map, shift, scale, mod_ld, rows_per_req, out, eps,
                     out8, out_scale);
 }
 
@@ -556,7 +553,6 @@ struct Tick {
     ap.ext_slots = kStride;
     ap.q_rows = kSlot;
     ap.err = err;
-    ap.meta_early = 1;   // the tick's lengths and block table are written before dfm_step
   }
   __nv_bfloat16* bf(size_t off) const { return reinterpret_cast<__nv_bfloat16*>(ws + off); }
   float* f32(size_t off) const { return reinterpret_cast<float*>(ws + off); }

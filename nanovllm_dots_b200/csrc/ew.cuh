@@ -9,47 +9,6 @@ namespace dfm {
 enum LnMode : int { LN_ADALN = 0, LN_AFFINE = 1, LN_NONE = 2 };
 constexpr int LN_ROWS_PER_BLOCK = 2;
 constexpr int LN_THREADS = 128 * LN_ROWS_PER_BLOCK;
-constexpr int LN_BLOCKS_PER_SM = 2;
-
-// One row's inputs as a thread of its 128-thread group holds them: the 16-byte
-// column groups t and t + 128 of h, of the summed split-K partials, and of
-// gate / shift / scale.
-struct LnRow {
-  float4 x[2], a[2], g[2], sh[2], sc[2];
-};
-
-template <int NSUB, int MODE>
-DFM_DEV void ln_load(LnRow& v, bool valid, const float* __restrict__ h, const float* __restrict__ sub,
-                     size_t sub_plane, const float* __restrict__ gate, size_t hrow, size_t req,
-                     const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
-                     int t) {
-  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    v.x[j] = v.a[j] = v.sh[j] = v.sc[j] = z;
-    v.g[j] = make_float4(1.f, 1.f, 1.f, 1.f);
-  }
-  if (!valid) return;
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int col = j * 512 + t * 4;
-    v.x[j] = *reinterpret_cast<const float4*>(h + hrow + col);
-    if constexpr (MODE != LN_NONE) {
-      v.sh[j] = *reinterpret_cast<const float4*>(shift + req * mod_ld + col);
-      v.sc[j] = *reinterpret_cast<const float4*>(scale + req * mod_ld + col);
-    }
-    if (sub) {
-      float4 a = *reinterpret_cast<const float4*>(sub + hrow + col);
-#pragma unroll
-      for (int q = 1; q < NSUB; ++q) {  // split-K: the other partial sums
-        const float4 a2 = *reinterpret_cast<const float4*>(sub + q * sub_plane + hrow + col);
-        a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
-      }
-      v.a[j] = a;
-      if constexpr (MODE == LN_ADALN) v.g[j] = *reinterpret_cast<const float4*>(gate + req * mod_ld + col);
-    }
-  }
-}
 
 // Residual update + adaLN LayerNorm + modulate, one row per 128 threads:
 //   x = h[in_map(r)] (+ gate[req] * sub[in_map(r)], written back to h; sub is
@@ -67,12 +26,6 @@ DFM_DEV void ln_load(LnRow& v, bool valid, const float* __restrict__ h, const fl
 //   LN_NONE    x                            (the residual stream itself)
 // Only LN_ADALN reads a gate; the others add sub with a gate of ones (the
 // encoder's plain residual, ``patch_encoder.py:82-86``).
-//
-// The grid is a couple of blocks per SM; each block walks row pairs with a
-// grid stride and loads the next pair's inputs before reducing the current
-// one, so the load latency of one pair hides behind the work of the previous
-// (a block per row pair spent most of its time being dispatched and waiting
-// on its single round of loads).
 template <int NSUB, int MODE>
 __global__ void __launch_bounds__(LN_THREADS)
     ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub, size_t sub_plane,
@@ -80,119 +33,119 @@ __global__ void __launch_bounds__(LN_THREADS)
                   const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
                   int rows_per_req, __nv_bfloat16* __restrict__ out, float eps,
                   uint8_t* __restrict__ out8, float* __restrict__ out_scale) {
-  // 128 threads (4 warps) per row, two rows per block iteration: thread t of
-  // a row owns the 16-byte column groups t and t + 128 (each warp's accesses
-  // are 512 contiguous bytes).
+  // 128 threads (4 warps) per row, two rows per block: thread t of a row owns
+  // the 16-byte column groups t and t + 128 (each warp's accesses are 512
+  // contiguous bytes), and the shift / scale vectors are loaded with the row.
+  // One warp per row left the kernel latency-bound (few warps per SM, each
+  // waiting on its own chain of loads).
   constexpr int H = 1024;
-  __shared__ float red[2][LN_ROWS_PER_BLOCK][3][4];   // [parity][row][sum | centred squares | absmax][warp]
+  __shared__ float red[LN_ROWS_PER_BLOCK][3][4];   // [row][sum | centred squares | absmax][warp]
   const int rb = threadIdx.x >> 7;
   const int t = threadIdx.x & 127;
   const int w = t >> 5, lane = threadIdx.x & 31;
-  constexpr bool norm = MODE != LN_NONE;
+  const int r = blockIdx.x * LN_ROWS_PER_BLOCK + rb;
   pdl_trigger();
   pdl_wait();
-  const int step = gridDim.x * LN_ROWS_PER_BLOCK;
-  int r = blockIdx.x * LN_ROWS_PER_BLOCK + rb;
-  LnRow cur;
-  {
-    const bool valid = r < M;
-    ln_load<NSUB, MODE>(cur, valid, h, sub, sub_plane, gate,
-                        valid ? static_cast<size_t>(in_map(r)) * H : 0,
-                        valid ? static_cast<size_t>(r / rows_per_req) : 0, shift, scale, mod_ld, t);
-  }
-  int par = 0;
-#pragma unroll 1
-  for (int r0 = blockIdx.x * LN_ROWS_PER_BLOCK; r0 < M; r0 += step, r += step, par ^= 1) {
-    const bool valid = r < M;
-    const size_t hrow = valid ? static_cast<size_t>(in_map(r)) * H : 0;
-    // the next row pair's loads go out before this pair's reductions
-    LnRow nxt;
-    {
-      const int rn = r + step;
-      const bool vn = rn < M;
-      ln_load<NSUB, MODE>(nxt, vn, h, sub, sub_plane, gate,
-                          vn ? static_cast<size_t>(in_map(rn)) * H : 0,
-                          vn ? static_cast<size_t>(rn / rows_per_req) : 0, shift, scale, mod_ld, t);
-    }
-    float4 x[2];
+  const bool valid = r < M;
+  const size_t hrow = valid ? static_cast<size_t>(in_map(r)) * H : 0;
+  const size_t req = valid ? static_cast<size_t>(r / rows_per_req) : 0;
+  float* hr = h + hrow;
+  float4 x[2], a_sh[2], b_sc[2];
+  constexpr bool norm = MODE != LN_NONE;
+  if (valid) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      x[j] = cur.x[j];
-      if (sub) {
-        x[j].x += cur.g[j].x * cur.a[j].x;
-        x[j].y += cur.g[j].y * cur.a[j].y;
-        x[j].z += cur.g[j].z * cur.a[j].z;
-        x[j].w += cur.g[j].w * cur.a[j].w;
-        if (valid) *reinterpret_cast<float4*>(h + hrow + j * 512 + t * 4) = x[j];
+      const int col = j * 512 + t * 4;
+      x[j] = *reinterpret_cast<const float4*>(hr + col);
+      if constexpr (norm) {   // the modulation / affine vectors, loaded before they are needed
+        a_sh[j] = *reinterpret_cast<const float4*>(shift + req * mod_ld + col);
+        b_sc[j] = *reinterpret_cast<const float4*>(scale + req * mod_ld + col);
       }
     }
-    if constexpr (!norm) {
-      if (valid) {
-        __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          *reinterpret_cast<uint2*>(o + j * 512 + t * 4) =
-              make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
-      }
-    } else {
-      float s = (x[0].x + x[0].y) + (x[0].z + x[0].w) + (x[1].x + x[1].y) + (x[1].z + x[1].w);
-      s = warp_sum(s);
-      // the reduction buffers alternate between iterations, so one barrier per
-      // reduction suffices (no thread can still read the previous iteration's)
-      if (lane == 0) red[par][rb][0][w] = s;
-      __syncthreads();
-      const float mean =
-          ((red[par][rb][0][0] + red[par][rb][0][1]) + (red[par][rb][0][2] + red[par][rb][0][3])) * (1.0f / H);
-      float v = 0.f;
+    if (sub) {
+      const float* sr = sub + hrow;
+      const float* gr = gate + req * mod_ld;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const float a = x[j].x - mean, b = x[j].y - mean, c = x[j].z - mean, d = x[j].w - mean;
-        v += a * a + b * b + c * c + d * d;
-      }
-      v = warp_sum(v);
-      if (lane == 0) red[par][rb][1][w] = v;
-      __syncthreads();
-      const float var =
-          ((red[par][rb][1][0] + red[par][rb][1][1]) + (red[par][rb][1][2] + red[par][rb][1][3])) * (1.0f / H);
-      const float rstd = rsqrtf(var + eps);
-      constexpr float one = MODE == LN_ADALN ? 1.f : 0.f;
+        const int col = j * 512 + t * 4;
+        float4 a = *reinterpret_cast<const float4*>(sr + col);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        x[j].x = (x[j].x - mean) * rstd * (one + cur.sc[j].x) + cur.sh[j].x;
-        x[j].y = (x[j].y - mean) * rstd * (one + cur.sc[j].y) + cur.sh[j].y;
-        x[j].z = (x[j].z - mean) * rstd * (one + cur.sc[j].z) + cur.sh[j].z;
-        x[j].w = (x[j].w - mean) * rstd * (one + cur.sc[j].w) + cur.sh[j].w;
-      }
-      if (out8) {
-        // e4m3 row with one fp32 scale per row (row absmax / 448)
-        float m = 0.f;
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          m = fmaxf(m, fmaxf(fmaxf(fabsf(x[j].x), fabsf(x[j].y)), fmaxf(fabsf(x[j].z), fabsf(x[j].w))));
-        m = warp_max(m);
-        if (lane == 0) red[par][rb][2][w] = m;
-        __syncthreads();
-        m = fmaxf(fmaxf(red[par][rb][2][0], red[par][rb][2][1]),
-                  fmaxf(red[par][rb][2][2], red[par][rb][2][3]));
-        if (valid) {
-          const float sc = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
-          const float inv = 1.0f / sc;
-          uint8_t* o8 = out8 + static_cast<size_t>(r) * H;
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-            *reinterpret_cast<uint32_t*>(o8 + j * 512 + t * 4) =
-                pack_e4m3x4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
-          if (t == 0) out_scale[r] = sc;
+        for (int p = 1; p < NSUB; ++p) {  // split-K: the other partial sums
+          const float4 a2 = *reinterpret_cast<const float4*>(sr + p * sub_plane + col);
+          a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
         }
-      } else if (valid) {
-        __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          *reinterpret_cast<uint2*>(o + j * 512 + t * 4) =
-              make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
+        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
+        if constexpr (MODE == LN_ADALN) g = *reinterpret_cast<const float4*>(gr + col);
+        x[j].x += g.x * a.x;
+        x[j].y += g.y * a.y;
+        x[j].z += g.z * a.z;
+        x[j].w += g.w * a.w;
+        *reinterpret_cast<float4*>(hr + col) = x[j];
       }
     }
-    cur = nxt;
+  } else {
+    x[0] = x[1] = a_sh[0] = a_sh[1] = b_sc[0] = b_sc[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if constexpr (!norm) {
+    if (valid) {
+      __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        *reinterpret_cast<uint2*>(o + j * 512 + t * 4) =
+            make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
+    }
+  } else {
+    float s = (x[0].x + x[0].y) + (x[0].z + x[0].w) + (x[1].x + x[1].y) + (x[1].z + x[1].w);
+    s = warp_sum(s);
+    if (lane == 0) red[rb][0][w] = s;
+    __syncthreads();
+    const float mean = ((red[rb][0][0] + red[rb][0][1]) + (red[rb][0][2] + red[rb][0][3])) * (1.0f / H);
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float a = x[j].x - mean, b = x[j].y - mean, c = x[j].z - mean, d = x[j].w - mean;
+      v += a * a + b * b + c * c + d * d;
+    }
+    v = warp_sum(v);
+    if (lane == 0) red[rb][1][w] = v;
+    __syncthreads();
+    const float var = ((red[rb][1][0] + red[rb][1][1]) + (red[rb][1][2] + red[rb][1][3])) * (1.0f / H);
+    const float rstd = rsqrtf(var + eps);
+    constexpr float one = MODE == LN_ADALN ? 1.f : 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      x[j].x = (x[j].x - mean) * rstd * (one + b_sc[j].x) + a_sh[j].x;
+      x[j].y = (x[j].y - mean) * rstd * (one + b_sc[j].y) + a_sh[j].y;
+      x[j].z = (x[j].z - mean) * rstd * (one + b_sc[j].z) + a_sh[j].z;
+      x[j].w = (x[j].w - mean) * rstd * (one + b_sc[j].w) + a_sh[j].w;
+    }
+    if (out8) {
+      // e4m3 row with one fp32 scale per row (row absmax / 448)
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(x[j].x), fabsf(x[j].y)), fmaxf(fabsf(x[j].z), fabsf(x[j].w))));
+      m = warp_max(m);
+      if (lane == 0) red[rb][2][w] = m;
+      __syncthreads();
+      m = fmaxf(fmaxf(red[rb][2][0], red[rb][2][1]), fmaxf(red[rb][2][2], red[rb][2][3]));
+      if (!valid) return;
+      const float sc = m > 0.f ? m * (1.0f / 448.0f) : 1.0f;
+      const float inv = 1.0f / sc;
+      uint8_t* o8 = out8 + static_cast<size_t>(r) * H;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        *reinterpret_cast<uint32_t*>(o8 + j * 512 + t * 4) =
+            pack_e4m3x4(x[j].x * inv, x[j].y * inv, x[j].z * inv, x[j].w * inv);
+      if (t == 0) out_scale[r] = sc;
+      return;
+    }
+    if (!valid) return;
+    __nv_bfloat16* o = out + static_cast<size_t>(r) * H;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      *reinterpret_cast<uint2*>(o + j * 512 + t * 4) =
+          make_uint2(pack_bf16(x[j].x, x[j].y), pack_bf16(x[j].z, x[j].w));
   }
 }
 
