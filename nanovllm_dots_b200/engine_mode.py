@@ -28,7 +28,7 @@ import weakref
 import torch
 
 from . import _lib
-from .fm_head import B200FMHead, FMRequest
+from .fm_head import B200FMHead, FMRequest, TickGraph
 
 
 class B200FMDispatch:
@@ -36,14 +36,19 @@ class B200FMDispatch:
 
     ``noise_fn(n)``, when set, supplies the tick's solver noise (bf16 [n, lp,
     ld] on the head's device) instead of the reference's own draw; tests use it
-    to feed the noise a golden run used."""
+    to feed the noise a golden run used.  With ``use_graphs`` each batch size's
+    tick is captured once as a CUDA graph and replayed (its first tick pays the
+    capture); otherwise every tick launches its kernels eagerly."""
 
-    def __init__(self, head: B200FMHead, noise_fn=None):
+    def __init__(self, head: B200FMHead, noise_fn=None, use_graphs: bool = True):
         self.head = head
         self.cfg = head.cfg
         self.noise_fn = noise_fn
+        self.use_graphs = use_graphs
         self._cached: dict[int, int] = {}     # rid -> history rows already in the cache
         self._g_dev: dict[int, tuple[int, torch.Tensor]] = {}   # rid -> (source id, device g_cond)
+        self._graphs: dict[int, TickGraph] = {}   # batch size -> captured tick
+        self._seq_ok: dict[int, tuple] = {}   # rid -> (checked history buffer, row 0 address, rows)
 
     def _rid(self, payload) -> int:
         rid = id(payload)
@@ -55,6 +60,7 @@ class B200FMDispatch:
     def _forget(self, rid: int) -> None:
         self._cached.pop(rid, None)
         self._g_dev.pop(rid, None)
+        self._seq_ok.pop(rid, None)
         self.head.release(rid)
 
     def plan(self, payloads):
@@ -123,25 +129,36 @@ class B200FMDispatch:
             self._g_dev[rid] = have
         return have[1].data_ptr()
 
-    def pack(self, payloads, plans):
+    def pack(self, payloads, plans, out=None):
         """This tick's device inputs: the active hidden rows act [n, H], the
         graduating rows ext [n, stride, H] (zero past each request's count) and
         g_cond [n, H], gathered from every request's ``fm_sequence`` by one
-        kernel from a table of row addresses (one host-to-device copy)."""
+        kernel from a table of row addresses (one host-to-device copy), into
+        ``out`` = (act, ext, g) when given."""
         c, head = self.cfg, self.head
         dev, H, n = head.device, c.hidden, len(payloads)
         table = []
         for p, (rid, s, e) in zip(payloads, plans):
             seq = p.gen_state.fm_sequence
-            if (seq.device != dev or seq.dtype != torch.bfloat16 or seq.stride(-1) != 1
-                    or seq.stride(-2) != H or seq.shape[-1] != H or seq.shape[-2] <= e):
-                raise RuntimeError("fm_sequence: expected bf16 rows of width "
-                                   f"{H} on {dev} covering the active row")
-            table.append((seq[0].data_ptr(), s, e - s, self._g_row(rid, p)))
+            # a request's history buffer is checked once (the engine allocates it
+            # at admission and appends in place); its row count every tick
+            ok = self._seq_ok.get(rid)
+            if ok is None or ok[0] is not seq:
+                if (seq.device != dev or seq.dtype != torch.bfloat16 or seq.stride(-1) != 1
+                        or seq.stride(-2) != H or seq.shape[-1] != H):
+                    raise RuntimeError("fm_sequence: expected bf16 rows of width "
+                                       f"{H} on {dev}")
+                ok = self._seq_ok[rid] = (seq, seq[0].data_ptr(), seq.shape[-2])
+            if ok[2] <= e:
+                raise RuntimeError("fm_sequence does not hold the active row")
+            table.append((ok[1], s, e - s, self._g_row(rid, p)))
         tab = torch.tensor(table, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
-        act = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
-        ext = torch.empty(n, c.stride, H, dtype=torch.bfloat16, device=dev)
-        g = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        if out is None:
+            act = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+            ext = torch.empty(n, c.stride, H, dtype=torch.bfloat16, device=dev)
+            g = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        else:
+            act, ext, g = out
         s = torch.cuda.current_stream(dev)
         _lib.check(head.L.dfm_gather_rows(tab.data_ptr(), n, H, c.stride, act.data_ptr(),
                                           ext.data_ptr(), g.data_ptr(),
@@ -157,31 +174,134 @@ class B200FMDispatch:
         # the head's device is current for the gather and the tick (a head on
         # cuda:1 works while cuda:0 is the caller's current device)
         with torch.cuda.device(dev) if dev.type == "cuda" else contextlib.nullcontext():
-            act, ext, g = self.pack(payloads, plans)
+            rids = [r for r, _, _ in plans]
+            for rid, s, _ in plans:
+                req = head.requests.get(rid)
+                if req is not None and req.cache_len != s:
+                    raise RuntimeError("FM cache out of step with the request history")
+            n_ext = [e - s for _, s, e in plans]
             # same draw as batched_meanflow (batched_fm.py:110-111) so seeded runs line up
             if self.noise_fn is not None:
                 noise = self.noise_fn(n)
             else:
                 noise = torch.randn((n, c.latent_patch, c.latent_dim), device=dev,
                                     dtype=torch.bfloat16)
-            rids = [r for r, _, _ in plans]
-            for rid, s, _ in plans:
-                req = head.requests.get(rid)
-                if req is not None and req.cache_len != s:
-                    raise RuntimeError("FM cache out of step with the request history")
-            out = head.tick(rids, noise=noise, act_row=act, ext_rows=ext,
-                            n_extend=[e - s for _, s, e in plans], g_cond=g)
+            if self.use_graphs and dev.type == "cuda":
+                # one captured tick per batch size (the reference captures its
+                # decode per batch size too, batched_llm.py:177-296): the rows,
+                # the noise and the page table go into the graph's buffers
+                tg = self._graphs.get(n)
+                if tg is None:
+                    tg = self._graphs[n] = head.graph(n, raw_inputs=False, with_g=True)
+                t = tg.inputs
+                self.pack(payloads, plans, out=(t["act_row"], t["ext_rows"], t["g_cond"]))
+                t["noise"].copy_(noise)
+                out = head.replay_tick(tg, rids, n_ext).clone()
+            else:
+                act, ext, g = self.pack(payloads, plans)
+                out = head.tick(rids, noise=noise, act_row=act, ext_rows=ext, n_extend=n_ext,
+                                g_cond=g)
         for rid, _, e in plans:
             self._cached[rid] = e
         return out
 
 
-def install(engine, head: B200FMHead) -> B200FMDispatch:
-    """Route ``engine._batched_fm`` through the B200 head (``fm_accel="b200"``)."""
+def install(engine, head: B200FMHead, batch_host_syncs: bool = True) -> B200FMDispatch:
+    """Route ``engine._batched_fm`` through the B200 head (``fm_accel="b200"``).
+
+    With ``batch_host_syncs`` (and the engine's batched patch encoder,
+    ``flash_pe``) the two per-request host synchronisations of every tick go
+    too: the end-of-speech check becomes a device flag instead of an
+    ``.item()`` per request (``native/model.py:197-201``), and the emitted
+    patches and those flags come to the host in one read per tick instead of
+    a ``.cpu()`` per request (``engine.py:761-774``); see ``BatchedFinish``."""
     dispatch = B200FMDispatch(head)
     engine.fm_accel = "b200"
     engine._batched_fm = dispatch
+    if batch_host_syncs and getattr(engine, "flash_pe", False):
+        fin = BatchedFinish(engine)
+        engine.dots._should_stop_after_current_audio = fin.deferred_stop
+        engine._finish_patches_flash = fin
     return dispatch
+
+
+class BatchedFinish:
+    """The engine's post-FM step for the batched patch encoder
+    (``DotsBatchEngine._finish_patches_flash`` + ``_emit_patch``,
+    ``engine.py:743-778``) with one host synchronisation per tick.
+
+    The reference reads each request's end-of-speech probability with
+    ``.item()`` before the FM call (``model.py:197-201``) and copies each
+    emitted patch to the host with ``.cpu()`` after it (``engine.py:761``):
+    2N waits per tick for the GPU, each stalling the launch of the next
+    work.  Here the end-of-speech check returns the device flag
+    (``deferred_stop``); after the FM head and the patch encoder have been
+    queued, the patches and every flag come to the host in one pinned copy,
+    and each request's record is then updated exactly as ``_emit_patch``
+    does: the patch encoder's embedding as the next LLM input, the
+    denormalised patch appended to the results and to the sequence, the
+    counters advanced, and the stop rule (end of speech, schedule exhausted
+    or patch cap)."""
+
+    def __init__(self, engine):
+        self.engine = engine
+
+    def deferred_stop(self, state, *, eos_threshold):
+        """``_should_stop_after_current_audio`` without the host read: False
+        before the first hidden, True after an explicit end, else the device
+        flag ``eos_prob > eos_threshold`` (``model.py:197-201``)."""
+        if state.llm_hiddens is None:
+            return False
+        if state.end_flag:
+            return True
+        eos = self.engine.core.eos_proj(state.llm_hiddens).softmax(dim=-1)[:, -1, 1]
+        return (eos > eos_threshold).reshape(())
+
+    def __call__(self, seqs, latents, stops) -> None:
+        eng = self.engine
+        core, dots, dev = eng.core, eng.dots, latents.device
+        rows, claim = [], []
+        for seq, latent in zip(seqs, latents):
+            st = seq.custom_payload
+            dots._append_history_chunk(st.gen_state, latent.unsqueeze(0))  # normalized
+            if st.pe_row is None:                       # lazily claim a cache row
+                if not eng._pe_free:
+                    raise RuntimeError(
+                        f"flash_pe: row pool exhausted ({eng._pe_max_batch} rows); "
+                        f"more sequences are generating concurrently. Increase "
+                        f"pe_max_batch or cap concurrency (max_num_seqs).")
+                st.pe_row = eng._pe_free.pop()
+                claim.append(st.pe_row)
+            rows.append(st.pe_row)
+        cuda = dev.type == "cuda"
+        pinned = (lambda t: t.pin_memory()) if cuda else (lambda t: t)
+        to_dev = lambda v: pinned(torch.tensor(v, dtype=torch.int32)).to(dev, non_blocking=True)
+        if claim:
+            eng._flash_pe.reset_rows(to_dev(claim))
+        patches = core.io_helper.denormalize(latents)              # [N, ps, ld]
+        embeds = eng._flash_pe.decode_patch(patches, to_dev(rows))  # [N, 1, H]
+        n = len(seqs)
+        flags = torch.stack([s.to(dev, torch.float32).reshape(()) if torch.is_tensor(s)
+                             else torch.tensor(float(bool(s)), device=dev) for s in stops])
+        # the one host synchronisation of the tick: every patch and stop flag
+        host = pinned(torch.empty(patches.numel() + n, dtype=torch.float32))
+        host.copy_(torch.cat([patches.detach().float().reshape(-1), flags]), non_blocking=cuda)
+        if cuda:
+            torch.cuda.current_stream(dev).synchronize()
+        lat = host[:patches.numel()].view(patches.shape)
+        stop_h = host[patches.numel():]
+        for i, (seq, emb) in enumerate(zip(seqs, embeds)):
+            st = seq.custom_payload
+            st.next_embed = emb
+            latent_cpu = lat[i:i + 1].clone()
+            st.latents.append(latent_cpu)
+            st.patches_emitted += 1
+            st.position += 1
+            seq.append_token(latent_cpu.reshape(-1).numpy().tobytes())
+            schedule_exhausted = st.position >= st.schedule.size(1)
+            cap = st.span_count if st.max_patches is None else min(st.span_count, st.max_patches)
+            if bool(stop_h[i] > 0.5) or schedule_exhausted or st.patches_emitted >= cap:
+                seq.stoped = True
 
 
 def install_patch_encoder(engine, pe) -> None:

@@ -112,6 +112,8 @@ class PageAllocator:
     every (layer, step, K|V) plane.  This is the FM counterpart of the LLM
     engine's block manager (``nanovllm_dots/engine/block_manager.py:90``)
     without prefix sharing (FM cache contents depend on the request's g_cond).
+    Each request's pages are also kept as a block-table row (int32, -1 past
+    its pages), so a tick's block table is one row copy per request.
     """
 
     def __init__(self, num_pages: int, page_rows: int, max_pages_per_req: int):
@@ -120,22 +122,35 @@ class PageAllocator:
         self.max_pages_per_req = max_pages_per_req
         self.free = list(range(num_pages - 1, -1, -1))
         self.pages: dict[object, list[int]] = {}
+        self.rows: dict[object, np.ndarray] = {}
 
     def ensure(self, rid, rows: int) -> list[int]:
         """Grow request rid's page list to cover ``rows`` positions."""
-        need = math.ceil(rows / self.page_rows)
+        need = -(-rows // self.page_rows)
+        have = self.pages.get(rid)
+        if have is not None and len(have) >= need:
+            return have
         if need > self.max_pages_per_req:
             raise RuntimeError(f"request {rid!r}: {rows} FM cache rows exceed the block-table "
                                f"capacity ({self.max_pages_per_req} pages of {self.page_rows})")
-        have = self.pages.setdefault(rid, [])
+        if have is None:
+            have = self.pages[rid] = []
+            self.rows[rid] = np.full(self.max_pages_per_req, -1, dtype=np.int32)
+        row = self.rows[rid]
         while len(have) < need:
             if not self.free:
                 raise RuntimeError("FM K/V pool exhausted: no free pages "
                                    f"({self.num_pages} pages total)")
+            row[len(have)] = self.free[-1]
             have.append(self.free.pop())
         return have
 
+    def row(self, rid) -> np.ndarray:
+        """Request rid's block-table row (after ``ensure``)."""
+        return self.rows[rid]
+
     def release(self, rid) -> None:
+        self.rows.pop(rid, None)
         for p in self.pages.pop(rid, []):
             self.free.append(p)
 
@@ -230,10 +245,12 @@ class B200FMHead:
         self.requests.pop(rid, None)
 
     # ------------------------------------------------------------- ticks
-    def prepare(self, rids, n_extend) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    def prepare(self, rids, n_extend, dst: torch.Tensor | None = None
+                ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """Host bookkeeping for one tick: allocate pages for the graduating and
         active rows, build (cache_len, n_extend, block_table) device tensors
-        (packed in one buffer: one host-to-device copy)."""
+        (packed in one buffer: one host-to-device copy, into ``dst`` when
+        given: an int32 device buffer of 2n + n * max_pages_per_req)."""
         c = self.cfg
         n = len(rids)
         if not 1 <= n <= self.max_requests:
@@ -241,16 +258,21 @@ class B200FMHead:
         W = self.max_pages_per_req
         buf = np.empty(2 * n + n * W, dtype=np.int32)
         cl, ne, bt = buf[:n], buf[n:2 * n], buf[2 * n:].reshape(n, W)
-        bt.fill(-1)
         for i, (rid, e) in enumerate(zip(rids, n_extend)):
             if not 0 <= e <= c.stride:
                 raise RuntimeError(f"request {rid!r}: n_extend={e} outside [0, {c.stride}]")
-            req = self.requests.setdefault(rid, FMRequest(rid))
-            pages = self.pages.ensure(rid, req.cache_len + e + c.stride)
-            bt[i, :len(pages)] = pages
+            req = self.requests.get(rid)
+            if req is None:
+                req = self.requests[rid] = FMRequest(rid)
+            self.pages.ensure(rid, req.cache_len + e + c.stride)
+            bt[i] = self.pages.row(rid)
             cl[i] = req.cache_len
             ne[i] = e
-        d = torch.from_numpy(buf).pin_memory().to(self.device, non_blocking=True)
+        if dst is None:
+            d = torch.from_numpy(buf).pin_memory().to(self.device, non_blocking=True)
+        else:
+            d = dst
+            d.copy_(torch.from_numpy(buf).pin_memory(), non_blocking=True)
         return d[:n], d[n:2 * n], d[2 * n:].view(n, W)
 
     def _batch(self, *, noise, cache_len, n_extend, block_table, out, act_hidden=None,
@@ -310,6 +332,19 @@ class B200FMHead:
         self.launch(noise=noise, cache_len=cl, n_extend=ne, block_table=bt, out=out,
                     act_hidden=act_hidden, act_row=act_row, ext_hidden=ext_hidden,
                     ext_latent=ext_latent, ext_rows=ext_rows, g_cond=g_cond)
+        for rid, e in zip(rids, n_extend):
+            self.requests[rid].cache_len += int(e)
+        return out
+
+    def replay_tick(self, tg: "TickGraph", rids, n_extend) -> torch.Tensor:
+        """``tick`` through a captured graph: the caller has written this
+        tick's row inputs and noise into ``tg.inputs``; this does the page
+        bookkeeping (straight into the graph's block-table buffer) and replays.
+        Returns ``tg.out`` (overwritten by the next replay)."""
+        if len(rids) != tg.n:
+            raise RuntimeError(f"graph for {tg.n} requests replayed with {len(rids)}")
+        self.prepare(rids, n_extend, dst=tg.ints)
+        out = tg.replay()
         for rid, e in zip(rids, n_extend):
             self.requests[rid].cache_len += int(e)
         return out
@@ -393,10 +428,12 @@ class TickGraph:
         c, dev = head.cfg, head.device
         self.head, self.n = head, n
         bf = dict(dtype=torch.bfloat16, device=dev)
-        i32 = dict(dtype=torch.int32, device=dev)
+        W = head.max_pages_per_req
+        # cache_len, n_extend and block_table in one buffer (prepare's layout)
+        self.ints = torch.zeros(2 * n + n * W, dtype=torch.int32, device=dev)
         t = {"noise": torch.zeros(n, c.latent_patch, c.latent_dim, **bf),
-             "cache_len": torch.zeros(n, **i32), "n_extend": torch.zeros(n, **i32),
-             "block_table": torch.zeros(n, head.max_pages_per_req, **i32)}
+             "cache_len": self.ints[:n], "n_extend": self.ints[n:2 * n],
+             "block_table": self.ints[2 * n:].view(n, W)}
         if raw_inputs:
             t["act_hidden"] = torch.zeros(n, c.cond_dim, **bf)
             t["ext_hidden"] = torch.zeros(n, c.cond_dim, **bf)

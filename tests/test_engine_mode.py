@@ -174,3 +174,76 @@ def test_install_decode_attention_routes_only_decode_steps():
     assert seen == [((3, 4, 8), (3, 2, 8), "s", "c", "b")]
     m.is_causal = False
     assert m.forward(q, k, k) == "flash"
+
+
+# --------------------------------------------------------------------------- #
+# Post-FM with one host synchronisation per tick                               #
+# --------------------------------------------------------------------------- #
+class _Seq:
+    def __init__(self, payload):
+        self.custom_payload = payload
+        self.tokens = []
+        self.stoped = False
+
+    def append_token(self, tok):
+        self.tokens.append(tok)
+
+
+def _engine_and_seqs(n, seed):
+    """A stand-in engine with the attributes the reference's post-FM step reads
+    (``engine.py:743-778``): core.eos_proj / io_helper, dots._append_history_chunk,
+    the batched patch encoder and its free rows."""
+    g = torch.Generator().manual_seed(seed)
+    lin = torch.nn.Linear(8, 2)
+    core = SimpleNamespace(eos_proj=lin,
+                           io_helper=SimpleNamespace(denormalize=lambda x: x * 2.0 + 1.0))
+    hist = []
+    dots = SimpleNamespace(_append_history_chunk=lambda st, chunk: hist.append((id(st), chunk)))
+
+    class _PE:
+        def __init__(self):
+            self.reset = []
+
+        def reset_rows(self, rows):
+            self.reset.extend(rows.tolist())
+
+        def decode_patch(self, patches, rows):
+            return patches.reshape(patches.shape[0], 1, -1)[:, :, :4] + rows.view(-1, 1, 1).float()
+
+    eng = SimpleNamespace(core=core, dots=dots, flash_pe=True, _flash_pe=_PE(), _pe_free=[5, 6, 7],
+                          _pe_max_batch=3)
+    seqs = []
+    for i in range(n):
+        st = SimpleNamespace(llm_hiddens=torch.randn(1, 1, 8, generator=g), end_flag=(i == 2))
+        p = SimpleNamespace(gen_state=st, pe_row=(1 if i == 0 else None), next_embed=None, latents=[],
+                            patches_emitted=0, position=3, schedule=torch.zeros(1, 5 if i != 1 else 4),
+                            span_count=10, max_patches=None, eos_threshold=0.5)
+        seqs.append(_Seq(p))
+    latents = torch.randn(n, syn.BASE.latent_patch, syn.BASE.latent_dim, generator=g)
+    return eng, seqs, latents, hist
+
+
+def test_batched_finish_matches_the_per_request_post_fm_step():
+    from nanovllm_dots_b200.engine_mode import BatchedFinish
+    eng, seqs, latents, hist = _engine_and_seqs(4, 3)
+    fin = BatchedFinish(eng)
+    stops = [fin.deferred_stop(s.custom_payload.gen_state, eos_threshold=0.5) for s in seqs]
+    # the per-request reference rule (model.py:197-201): end flag, else eos prob > threshold
+    want_eos = []
+    for s in seqs:
+        st = s.custom_payload.gen_state
+        prob = eng.core.eos_proj(st.llm_hiddens).softmax(dim=-1)[:, -1, 1]
+        want_eos.append(st.end_flag or bool((prob > 0.5).item()))
+    assert [bool(x) for x in stops] == want_eos
+    fin(seqs, latents, stops)
+    assert len(hist) == 4                                   # every patch appended to its history
+    assert eng._flash_pe.reset == [7, 6, 5]                # rows claimed in order, one call
+    for i, s in enumerate(seqs):
+        p = s.custom_payload
+        want = latents[i:i + 1] * 2.0 + 1.0                 # denormalised patch (engine.py:761)
+        assert torch.equal(p.latents[0], want)
+        assert s.tokens == [want.reshape(-1).numpy().tobytes()]
+        assert p.patches_emitted == 1 and p.position == 4
+        assert p.next_embed is not None
+        # stop rule (engine.py:772-774): eos/end flag, schedule exhausted (seq 1), or cap
+        assert s.stoped == (want_eos[i] or i == 1)

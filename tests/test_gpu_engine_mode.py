@@ -8,7 +8,8 @@ Three requests over three ticks, shaped like the reference's payloads
 ``g_cond``): one without prompt, one whose history starts with a voice-clone
 prompt (the dispatch bulk-prefills it), one with a speaker condition that joins
 at the second tick; the request order changes between ticks and one request
-finishes early.  Each tick's noise is the golden run's.  Tolerance (bf16 path,
+finishes early.  Each tick's noise is the golden run's.  Both dispatch modes:
+a captured tick per batch size, and eager launches.  Tolerance (bf16 path,
 after 4 NFE): per-frame cosine >= 0.9999 and max-abs <= 2e-2 against the fp32
 reference."""
 from __future__ import annotations
@@ -46,13 +47,15 @@ class _Payload:
         self.num_steps = syn.BASE.nfe
 
 
-def test_dispatch_matches_reference_engine(weights):
+@pytest.mark.parametrize("use_graphs", [True, False], ids=["graph", "eager"])
+def test_dispatch_matches_reference_engine(weights, use_graphs):
     man, arr = load_engine_golden()
     head = B200FMHead(weights, syn.BASE, num_pages=64, max_pages_per_req=16, max_requests=4,
                       device=DEV)
     engine = SimpleNamespace(fm_accel="none")
     noise = {}
     dispatch = install(engine, head)
+    dispatch.use_graphs = use_graphs
     dispatch.noise_fn = lambda n: noise["t"]
     payloads = {}
     for name in "ABC":
