@@ -268,6 +268,14 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
       order_s[rank] = x;
     }
   }
+  // CTA 0 reports requests whose lengths no unit can serve (one thread per
+  // request; the producer no longer walks its units' lengths before its first load)
+  if (blockIdx.x == 0)
+    for (int x = threadIdx.x; x < p.n; x += blockDim.x) {
+      const int P = p.cache_len[x], ne = p.n_ext[x];
+      if (P < 0 || ne < 0 || ne > p.ext_slots || P + ne + (TA_ROWS - p.ext_slots) > p.max_pages * 16)
+        atomicOr(p.err, DFM_DEV_ERR_LEN);
+    }
   if (threadIdx.x == 0) {
     for (int b = 0; b < TA_VSLOTS; ++b) {
       mbar_init(&v_full[b], 1);
@@ -307,11 +315,6 @@ __global__ void __launch_bounds__(TA_THREADS, TA_CTAS_PER_SM)
     AttnCursor ck, cv;   // next K tile, next V tile
     attn_start(ck, p, order_s, U);
     attn_start(cv, p, order_s, U);
-    // a request with invalid lengths is reported once (by its first unit)
-    if (lane == 0)
-      for (int u = blockIdx.x; u < U; u += gridDim.x)
-        if ((u % p.heads) == 0 && ((u / p.heads) % p.MC) == 0 && attn_unit(p, order_s, u).bad)
-          atomicOr(p.err, DFM_DEV_ERR_LEN);
     // one tile = 8 page boxes, issued by lanes 0..7 after lane 0 armed the barrier
     auto load_tile = [&](uint8_t* dst, uint64_t* bar, const AttnCursor& cu, int plane) {
       if (lane == 0) mbar_arrive_expect_tx(bar, TA_KV_BYTES);
