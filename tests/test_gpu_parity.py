@@ -243,6 +243,24 @@ def test_device_error_on_bad_block_table(head):
     head.check_errors()   # cleared
 
 
+def test_device_error_on_cache_longer_than_the_block_table(head):
+    """A cache length the block table cannot hold is reported as a length
+    error (no K/V write, no attention over it), and the next good tick runs."""
+    cfg = syn.BASE
+    noise = torch.zeros(1, cfg.latent_patch, cfg.latent_dim, dtype=torch.bfloat16, device=DEV)
+    act = torch.zeros(1, cfg.cond_dim, dtype=torch.bfloat16, device=DEV)
+    cl = torch.full((1,), head.max_pages_per_req * cfg.page_rows, dtype=torch.int32, device=DEV)
+    ne = torch.zeros(1, dtype=torch.int32, device=DEV)
+    bt = torch.zeros((1, head.max_pages_per_req), dtype=torch.int32, device=DEV)
+    out = torch.empty_like(noise)
+    head.launch(noise=noise, act_hidden=act, cache_len=cl, n_extend=ne, block_table=bt, out=out)
+    with pytest.raises(RuntimeError, match="len"):
+        head.check_errors()
+    b = syn.make_batch(1, [1], seed=8)
+    good = _run(head, b, ["after_len_error"])
+    assert torch.isfinite(good).all()
+
+
 def test_prime_equals_tick_by_tick(head):
     """Bulk prefill (``prime``) of three patches of history rows leaves the
     same cache as graduating them over three ticks: the next tick's latents
