@@ -27,6 +27,7 @@ constexpr int kQkvBN = 256, kQkvST = 6;
 constexpr int kFc1BN = 256, kFc1ST = 5;
 constexpr int kOutBN = 256, kOutST = 5;  // O-projection and fc2 (N = hidden) ...
 constexpr int kOutSplit = 2;             // ... as two split-K partial sums (72 units at n = 64)
+constexpr int kAdaBN = 256, kAdaST = 5;  // the all-layer adaLN GEMM (one 256-row tile of steps x requests)
 
 // ---------------------------------------------------------------- TMA encoding
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -283,6 +284,7 @@ struct Handle {
   const void* plan_pool = nullptr;
   CUtensorMap a_csilu, a_xrows, a_xm, a_ob, a_u, a_zb, a_xmf, a_act, a_exth, a_extl, pool, q_att;
   CUtensorMap o_sub, o_u;  // staged-epilogue outputs: fp32 sub planes, bf16 MLP hidden
+  CUtensorMap o_mod;       // ... and the fp32 modulation rows of every step
 };
 
 WsLayout layout_for(const DfmConfig& c, int mc) {
@@ -355,6 +357,8 @@ bool ensure_plan(Handle* h, void* ws, void* pool, cudaStream_t s) {
             map_out(&h->o_sub, b + h->ws.sub, true, R, H, 2, R * H * 4) &&
             map_2d_u8(&h->a_xm8, b + h->ws.xm8, R, H, H, 128) &&
             map_out(&h->o_u, b + h->ws.u, false, R, c.ffn, 1, R * c.ffn * 2) &&
+            map_out(&h->o_mod, b + h->ws.mod, true, c.nfe * NR, h->mod_w, 1,
+                    c.nfe * NR * static_cast<uint64_t>(h->mod_w) * 4) &&
             map_pool(&h->pool, pool, c.num_pages, c.heads, c.layers * c.nfe * 2);
   if (!ok) {
     h->plan_ws = h->plan_pool = nullptr;
@@ -442,7 +446,7 @@ int dfm_create(const DfmConfig* cfg, const DfmWeights* w, void** out) {
   h->m_fc18 = new CUtensorMap[L];
   auto bw = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
   auto b8 = [](const void* p) { return static_cast<const uint8_t*>(p); };
-  bool ok = map_2d(&h->m_ada, w->ada_w, h->mod_w, H, H, 256) &&
+  bool ok = map_2d(&h->m_ada, w->ada_w, h->mod_w, H, H, kAdaBN / 2) &&
             map_2d(&h->m_in, w->input_w, H, H, H, 128) &&
             map_2d(&h->m_final, w->final_w, c.latent_dim, H, H, 64) &&
             map_2d(&h->m_coord, w->coord_w, H, c.latent_dim, c.latent_dim, 128) &&
@@ -717,11 +721,13 @@ int dfm_step(void* handle, const DfmBatch* b, void* workspace, size_t workspace_
   }
   CK(launch_pdl(embed1_kernel, dim3((2 * H * 32 + 255) / 256), dim3(256), 0, s, W(w.temb_w1),
                 w.temb_b1, W(w.demb_w1), w.demb_b1, grid, NFE, H, f32(hd->ws.emb1)));
-  CK(launch_pdl(embed2_kernel, dim3((H * 32 + 255) / 256), dim3(256), 0, s, W(w.temb_w2), w.temb_b2,
+  CK(launch_pdl(embed2_kernel, dim3((H + 7) / 8), dim3(256), 0, s, W(w.temb_w2), w.temb_b2,
                 W(w.demb_w2), w.demb_b2, static_cast<const float*>(f32(hd->ws.emb1)),
                 static_cast<const __nv_bfloat16*>(b->g_cond), n, NFE, H, bf(hd->ws.csilu)));
-  CK(gemm<256, 4>(hd->a_csilu, hd->m_ada, NFE * n, static_cast<int>(modw), H,
-                  store(f32(hd->ws.mod), static_cast<int>(modw), true, w.ada_b, false), err, s));
+  // every step's modulation for every block and the final layer: one CTA-pair
+  // GEMM (each pair reads its weight tile once; the GEMM streams ~155 MB of weights)
+  CK(gemm2<kAdaBN, kAdaST>(hd->a_csilu, hd->m_ada, hd->o_mod, NFE * n, static_cast<int>(modw), H, 1,
+                           store_t<true>(w.ada_b, kActNone), err, s));
 
   // ---- DiT-input rows: [graduating 17 | active hidden | active latents 16] per request
   __nv_bfloat16* xrows = bf(hd->ws.xrows);

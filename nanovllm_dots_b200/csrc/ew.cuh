@@ -166,15 +166,23 @@ DFM_DEV float sinusoid(float t, int idx) {
 
 // First embedder layer for both embedders and every step:
 // out1[e][k][j] = silu(W1_e[j, :] . emb(x_{e,k}) + b1_e[j]); e = 0 time, 1 duration.
-// One warp per (e, j); the 256-wide dot product is 8 bf16 per lane.
+// The 256-d embeddings of the (at most 2 x 8) scalars are built once per block
+// in shared memory; then one warp per (e, j) does the 256-wide dot product,
+// 8 bf16 per lane.
 __global__ void __launch_bounds__(256)
     embed1_kernel(const __nv_bfloat16* __restrict__ w_t, const float* __restrict__ b_t,
                   const __nv_bfloat16* __restrict__ w_d, const float* __restrict__ b_d,
                   TimeGrid grid, int nfe, int H, float* __restrict__ out1) {
+  __shared__ float emb_s[2][EMB_MAX_STEPS][256];
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_trigger();
   pdl_wait();
+  for (int idx = threadIdx.x; idx < 2 * nfe * 256; idx += blockDim.x) {
+    const int e = idx / (nfe * 256), k = (idx >> 8) % nfe, d = idx & 255;
+    emb_s[e][k][d] = sinusoid(e == 0 ? grid.t[k] : grid.dt[k], d);
+  }
+  __syncthreads();
   if (wid >= 2 * H) return;
   const int e = wid / H, j = wid - e * H;
   const __nv_bfloat16* w = (e == 0 ? w_t : w_d) + static_cast<size_t>(j) * 256 + lane * 8;
@@ -186,10 +194,10 @@ __global__ void __launch_bounds__(256)
   const float bias = (e == 0 ? b_t : b_d)[j];
 #pragma unroll 1
   for (int k = 0; k < nfe; ++k) {
-    const float x = e == 0 ? grid.t[k] : grid.dt[k];
+    const float* x = &emb_s[e][k][lane * 8];
     float acc = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) acc += wf[q] * sinusoid(x, lane * 8 + q);
+    for (int q = 0; q < 8; ++q) acc += wf[q] * x[q];
     acc = warp_sum(acc);
     if (lane == 0) out1[(static_cast<size_t>(e) * nfe + k) * H + j] = silu(acc + bias);
   }
@@ -198,54 +206,75 @@ __global__ void __launch_bounds__(256)
 // Second embedder layer, the condition sum and the adaLN input:
 // c_k[j] = (W2_t[j].out1[0][k] + b2_t[j]) + (W2_d[j].out1[1][k] + b2_d[j])
 // csilu[(k*n + i), j] = bf16(silu(c_k[j] + g_cond[i][j]))    (``native/dit.py:137-143``;
-// adaLN_modulation = SiLU -> Linear, ``dit.py:75-79``).  One warp per j.
+// adaLN_modulation = SiLU -> Linear, ``dit.py:75-79``).  One warp per j; a
+// block's 8 warps cover 8 consecutive j, whose c_k go through shared memory so
+// the block writes each csilu row's 8 columns as one 16-byte store.
 __global__ void __launch_bounds__(256)
     embed2_kernel(const __nv_bfloat16* __restrict__ w_t, const float* __restrict__ b_t,
                   const __nv_bfloat16* __restrict__ w_d, const float* __restrict__ b_d,
                   const float* __restrict__ out1, const __nv_bfloat16* __restrict__ g_cond, int n,
                   int nfe, int H, __nv_bfloat16* __restrict__ csilu) {
-  const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  __shared__ float ck_s[EMB_MAX_STEPS][8];
+  const int warp = threadIdx.x >> 5;
+  const int j = blockIdx.x * 8 + warp;
   const int lane = threadIdx.x & 31;
   pdl_trigger();
   pdl_wait();
-  if (j >= H) return;
-  float ck[EMB_MAX_STEPS];
+  if (j < H) {
+    float ck[EMB_MAX_STEPS];
 #pragma unroll
-  for (int k = 0; k < EMB_MAX_STEPS; ++k) ck[k] = 0.f;
+    for (int k = 0; k < EMB_MAX_STEPS; ++k) ck[k] = 0.f;
 #pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const __nv_bfloat16* w = (e == 0 ? w_t : w_d) + static_cast<size_t>(j) * H;
-    float acc[EMB_MAX_STEPS];
+    for (int e = 0; e < 2; ++e) {
+      const __nv_bfloat16* w = (e == 0 ? w_t : w_d) + static_cast<size_t>(j) * H;
+      float acc[EMB_MAX_STEPS];
 #pragma unroll
-    for (int k = 0; k < EMB_MAX_STEPS; ++k) acc[k] = 0.f;
+      for (int k = 0; k < EMB_MAX_STEPS; ++k) acc[k] = 0.f;
 #pragma unroll 1
-    for (int c = lane * 8; c < H; c += 256) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
-      const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      for (int c = lane * 8; c < H; c += 256) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+        const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+        for (int k = 0; k < EMB_MAX_STEPS; ++k) {
+          if (k >= nfe) break;
+          const float4* x4 =
+              reinterpret_cast<const float4*>(out1 + (static_cast<size_t>(e) * nfe + k) * H + c);
+          const float4 xa = x4[0], xb = x4[1];
+          acc[k] += __bfloat162float(wp[0]) * xa.x + __bfloat162float(wp[1]) * xa.y +
+                    __bfloat162float(wp[2]) * xa.z + __bfloat162float(wp[3]) * xa.w +
+                    __bfloat162float(wp[4]) * xb.x + __bfloat162float(wp[5]) * xb.y +
+                    __bfloat162float(wp[6]) * xb.z + __bfloat162float(wp[7]) * xb.w;
+        }
+      }
+      const float bias = (e == 0 ? b_t : b_d)[j];
 #pragma unroll
       for (int k = 0; k < EMB_MAX_STEPS; ++k) {
         if (k >= nfe) break;
-        const float* x = out1 + (static_cast<size_t>(e) * nfe + k) * H + c;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[k] += __bfloat162float(wp[q]) * x[q];
+        ck[k] += warp_sum(acc[k]) + bias;
       }
     }
-    const float bias = (e == 0 ? b_t : b_d)[j];
-#pragma unroll
-    for (int k = 0; k < EMB_MAX_STEPS; ++k) {
-      if (k >= nfe) break;
-      ck[k] += warp_sum(acc[k]) + bias;
-    }
+    if (lane == 0)
+      for (int k = 0; k < nfe; ++k) ck_s[k][warp] = ck[k];
   }
-  // lanes stride over the (k, i) pairs
-  for (int idx = lane; idx < nfe * n; idx += 32) {
+  __syncthreads();
+  // rows (k, i): 8 columns j0 .. j0 + 7 per thread
+  const int j0 = blockIdx.x * 8;
+  if (j0 + 8 > H) return;
+  for (int idx = threadIdx.x; idx < nfe * n; idx += blockDim.x) {
     const int k = idx / n, i = idx - k * n;
-    float c = 0.f;
+    float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (g_cond) {
+      const uint4 gv = *reinterpret_cast<const uint4*>(g_cond + static_cast<size_t>(i) * H + j0);
+      const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(&gv);
 #pragma unroll
-    for (int kk = 0; kk < EMB_MAX_STEPS; ++kk)
-      if (kk == k) c = ck[kk];
-    if (g_cond) c += __bfloat162float(g_cond[static_cast<size_t>(i) * H + j]);
-    csilu[static_cast<size_t>(idx) * H + j] = __float2bfloat16(silu(c));
+      for (int q = 0; q < 8; ++q) g[q] = __bfloat162float(gp[q]);
+    }
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = silu(ck_s[k][q] + g[q]);
+    *reinterpret_cast<uint4*>(csilu + static_cast<size_t>(idx) * H + j0) =
+        make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]),
+                   pack_bf16(v[6], v[7]));
   }
 }
 
