@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import dataclasses
 import hashlib
+import math
 
 import numpy as np
 import torch
@@ -354,3 +355,182 @@ def make_llm_weights(cfg: LLMConfig = LLM_BASE, seed: int = 0, device="cpu",
         sd[f"{p}.mlp.down_proj.weight"] = rn(H, I)
     sd["norm.weight"] = rn(H, s=0.1, base=1.0)
     return sd
+
+
+# --------------------------------------------------------------------------- #
+# Vocoder (BigVGAN AudioVAE decoder, the step after the patch encoder)         #
+# --------------------------------------------------------------------------- #
+@dataclasses.dataclass(frozen=True)
+class VocConfig:
+    """Shape of the vocoder's decode path (``AudioVAE``,
+    ``nanovllm_dots/models/dots/native/vocoder/bigvgan.py:751-788`` and
+    ``Decoder``, ``bigvgan.py:542-640``; keys of ``vocoder/config.py``).
+
+    The checkpoint's config.json is not published.  The defaults are synthetic
+    choices consistent with the rest of this package: 64-channel latents (the
+    FM head's ``latent_dim``, so FM patches feed it directly), 25 latent frames
+    per second and 48 kHz audio (the reference's golden manifests: 1920 samples
+    per frame), the config default of 1536 initial channels, six causal
+    transposed-conv upsamplers whose rates multiply to 1920, three AMPBlock1
+    resblocks per stage with kernels 3/7/11 and dilations 1/3/5, SnakeBeta on a
+    log scale, a 4-layer LSTM front (``mi_num_layers``) and 2 lookahead frames.
+    """
+    latent_dim: int = 64
+    initial_channels: int = 1536
+    upsample_rates: tuple = (8, 5, 4, 3, 2, 2)
+    resblock_kernel_sizes: tuple = (3, 7, 11)
+    resblock_dilations: tuple = ((1, 3, 5), (1, 3, 5), (1, 3, 5))
+    resblock: str = "1"
+    activation: str = "snakebeta"
+    mi_layers: int = 4
+    lookahead: int = 2
+    use_tanh: bool = True
+    use_bias_at_final: bool = True
+    sample_rate: int = 48000
+
+    @property
+    def hop(self) -> int:
+        """Audio samples per latent frame (the product of the upsample rates)."""
+        return int(np.prod(self.upsample_rates))
+
+    @property
+    def upsample_kernel_sizes(self) -> tuple:
+        """Causal transposed convs need kernel = 2 * stride (``layers.py:61-64``)."""
+        return tuple(2 * u for u in self.upsample_rates)
+
+    def stage_channels(self, i: int) -> int:
+        """Output channels of stage i (``bigvgan.py:572-583``); -1 is conv_pre's."""
+        return self.initial_channels // (2 ** (i + 1))
+
+    def reference_dict(self) -> dict:
+        """The ``vocoder`` section of config.json that builds this shape with the
+        reference's ``AudioVAEConfig``."""
+        return {
+            "sample_rate": self.sample_rate, "upsample_rates": list(self.upsample_rates),
+            "upsample_kernel_sizes": list(self.upsample_kernel_sizes),
+            "upsample_initial_channel": self.initial_channels, "resblock": self.resblock,
+            "resblock_kernel_sizes": list(self.resblock_kernel_sizes),
+            "resblock_dilation_sizes": [list(d) for d in self.resblock_dilations],
+            "downsample_rates": list(self.upsample_rates),
+            "downsample_channels": [8] * (len(self.upsample_rates) + 1),
+            "activation": self.activation, "snake_logscale": True,
+            "latent_dim": self.latent_dim, "causal": True, "mi_num_layers": self.mi_layers,
+            "causal_encoder": True, "use_bias_at_final": self.use_bias_at_final,
+            "use_tanh_at_final": self.use_tanh, "num_decoder_lookahead": self.lookahead,
+        }
+
+
+VOC_BASE = VocConfig()
+# A small shape for golden fixtures and fast parity tests: three stages, the
+# last one narrower than 32 channels (exercises the channel padding).
+VOC_SMALL = VocConfig(latent_dim=32, initial_channels=128, upsample_rates=(4, 3, 2), mi_layers=2)
+
+
+def kaiser_sinc(cutoff: float, half_width: float, kernel_size: int) -> np.ndarray:
+    """Kaiser-windowed sinc low-pass filter normalised to unit sum (Kaiser's
+    window with his published beta rule; the filter the reference builds in
+    ``alias_free_filter.py:28-60``).  float64 [kernel_size]."""
+    half = kernel_size // 2
+    delta_f = 4.0 * half_width
+    att = 2.285 * (half - 1) * math.pi * delta_f + 7.95
+    if att > 50.0:
+        beta = 0.1102 * (att - 8.7)
+    elif att >= 21.0:
+        beta = 0.5842 * (att - 21.0) ** 0.4 + 0.07886 * (att - 21.0)
+    else:
+        beta = 0.0
+    window = np.kaiser(kernel_size, beta)
+    time = np.arange(-half, half) + 0.5 if kernel_size % 2 == 0 else np.arange(kernel_size) - half
+    filt = 2.0 * cutoff * window * np.sinc(2.0 * cutoff * time)
+    return filt / filt.sum()
+
+
+def voc_filter(kernel_size: int = 12) -> torch.Tensor:
+    """The fixed filter of the ratio-2 up- and down-samplers (cutoff 0.25, half
+    width 0.3), fp32.  Computed here in float64 and rounded once; a real
+    checkpoint carries the reference's own fp32 buffers, which are used then."""
+    return torch.tensor(kaiser_sinc(0.25, 0.3, kernel_size), dtype=torch.float32)
+
+
+def voc_act_names(cfg: VocConfig) -> list[str]:
+    """State-dict prefixes of every alias-free activation of the decoder in
+    execution order: per resblock its 6 (AMPBlock1) or 2 (AMPBlock2)
+    activations, then ``activation_post``."""
+    per = 6 if cfg.resblock == "1" else 2
+    names = []
+    for r in range(len(cfg.upsample_rates) * len(cfg.resblock_kernel_sizes)):
+        names += [f"decoder.resblocks.{r}.activations.{a}" for a in range(per)]
+    return names + ["decoder.activation_post"]
+
+
+def make_voc_weights(cfg: VocConfig = VOC_SMALL, seed: int = 0) -> dict[str, torch.Tensor]:
+    """Seeded fp32 weights of the vocoder's decode path under the reference's
+    state-dict names (after ``remove_weight_norm``, ``loader.py:94-110``).
+
+    Convolutions are N(0, (g / sqrt(fan_in))^2) with gains that keep the
+    residual stream O(1) through every stage (the reference's N(0, 0.01^2)
+    init would leave the audio near zero), biases N(0, 0.05^2), log-alpha and
+    log-beta N(0, 0.3^2), the LSTM uniform(+-1/sqrt(hidden)) as torch
+    initialises it.  The resblock activations carry the fixed filter (a
+    buffer); ``activation_post``'s learnable per-channel filters are that
+    filter jittered per channel, as a trained checkpoint's would differ.
+    """
+    g = torch.Generator().manual_seed(seed)
+    L, Hm = cfg.latent_dim, 4 * cfg.latent_dim
+    sd: dict[str, torch.Tensor] = {}
+
+    def rn(*shape, s=1.0):
+        return torch.randn(*shape, generator=g) * s
+
+    def conv(name, cout, cin, k, gain=1.0, bias=True):
+        sd[f"{name}.weight"] = rn(cout, cin, k, s=gain / math.sqrt(cin * k))
+        if bias:
+            sd[f"{name}.bias"] = rn(cout, s=0.05)
+
+    conv("post_proj", L, L, 1)
+    sd["dec_mi_layer.0.weight"] = rn(Hm, L, s=1.0 / math.sqrt(L))
+    sd["dec_mi_layer.0.bias"] = rn(Hm, s=0.05)
+    bound = 1.0 / math.sqrt(Hm)
+    for l in range(cfg.mi_layers):
+        for kind in ("ih", "hh"):
+            sd[f"dec_mi_layer.1.lstm.weight_{kind}_l{l}"] = (torch.rand(4 * Hm, Hm, generator=g) * 2 - 1) * bound
+            sd[f"dec_mi_layer.1.lstm.bias_{kind}_l{l}"] = (torch.rand(4 * Hm, generator=g) * 2 - 1) * bound
+    sd["dec_mi_layer.2.weight"] = rn(L, Hm, s=1.0 / math.sqrt(Hm))
+    sd["dec_mi_layer.2.bias"] = rn(L, s=0.05)
+    conv("decoder.conv_pre", cfg.initial_channels, L, 2 * cfg.lookahead + 1)
+    filt = voc_filter()
+    nk = len(cfg.resblock_kernel_sizes)
+    for i, (u, k) in enumerate(zip(cfg.upsample_rates, cfg.upsample_kernel_sizes)):
+        cin, cout = cfg.stage_channels(i - 1), cfg.stage_channels(i)
+        sd[f"decoder.ups.{i}.0.weight"] = rn(cin, cout, k, s=1.0 / math.sqrt(cin * 2))
+        sd[f"decoder.ups.{i}.0.bias"] = rn(cout, s=0.05)
+        for j, (ks, dil) in enumerate(zip(cfg.resblock_kernel_sizes, cfg.resblock_dilations)):
+            r = i * nk + j
+            if cfg.resblock == "1":
+                for cname in ("convs1", "convs2"):
+                    for l in range(len(dil)):
+                        conv(f"decoder.resblocks.{r}.{cname}.{l}", cout, cout, ks, gain=0.4)
+            else:
+                for l in range(2):
+                    conv(f"decoder.resblocks.{r}.convs.{l}", cout, cout, ks, gain=0.4)
+    C = cfg.stage_channels(len(cfg.upsample_rates) - 1)
+    for name in voc_act_names(cfg):
+        post = name.endswith("post")
+        ch = C if post else cfg.stage_channels(int(name.split(".")[2]) // nk)
+        sd[f"{name}.act.alpha"] = rn(ch, s=0.3)
+        if cfg.activation == "snakebeta":
+            sd[f"{name}.act.beta"] = rn(ch, s=0.3)
+        for part in ("upsample.filter", "downsample.lowpass.filter"):
+            if post:
+                sd[f"{name}.{part}"] = filt.view(1, 1, 12) * (1.0 + 0.05 * rn(ch, 1, 12))
+            else:
+                sd[f"{name}.{part}"] = filt.view(1, 1, 12).clone()
+    conv("decoder.conv_post", 1, C, 7, bias=cfg.use_bias_at_final)
+    return {k: v.float().contiguous() for k, v in sd.items()}
+
+
+def make_voc_latents(n: int, frames: int, seed: int, cfg: VocConfig = VOC_SMALL) -> torch.Tensor:
+    """Latent frames for n requests: fp32 [n, frames, latent_dim], N(0, 1),
+    frames-first (the layout the engine stores them in, ``engine.py:835-845``)."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(n, frames, cfg.latent_dim, generator=gen)
