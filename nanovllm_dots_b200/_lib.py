@@ -1,6 +1,6 @@
 """ctypes binding of ``libdfm.so`` (declarations in ``include/dfm.h`` for the FM
-head, ``include/dpe.h`` for the patch encoder and ``include/dllm.h`` for the LLM
-decode attention).
+head, ``include/dpe.h`` for the patch encoder, ``include/dllm.h`` for the LLM
+decode attention and ``include/dvoc.h`` for the vocoder).
 
 The library is built in-tree by ``nanovllm_dots_b200.build``.  There is no
 fallback: if the shared object is missing or fails to load, every entry point
@@ -25,7 +25,10 @@ EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "df
            "dfm_paged_attention", "dfm_paged_attention_noalloc", "dfm_gather_rows", "dfm_tick_launch",
            "dpe_create", "dpe_workspace_size", "dpe_pool_bytes", "dpe_decode", "dpe_read_error",
            "dpe_destroy", "dllm_decode_workspace_size", "dllm_decode_attention", "dllm_read_error",
-           "dllm_create", "dllm_step_workspace_size", "dllm_decode_step", "dllm_destroy")
+           "dllm_create", "dllm_step_workspace_size", "dllm_decode_step", "dllm_destroy",
+           "dvoc_create", "dvoc_destroy", "dvoc_conv_floats", "dvoc_bias_floats", "dvoc_act_floats",
+           "dvoc_hop", "dvoc_stream_left_context", "dvoc_workspace_size", "dvoc_decode",
+           "dvoc_read_error")
 
 
 class DfmConfig(ctypes.Structure):
@@ -96,6 +99,33 @@ class DllmStep(ctypes.Structure):
                 ("slot_mapping", c_void_p), ("context_lens", c_void_p), ("block_table", c_void_p),
                 ("k_caches", POINTER(c_void_p)), ("v_caches", POINTER(c_void_p)),
                 ("num_blocks", c_int32), ("out", c_void_p)]
+
+
+DVOC_MAX_STAGES, DVOC_MAX_KERNELS = 8, 4
+
+
+class DvocConfig(ctypes.Structure):
+    _fields_ = [("latent_dim", c_int32), ("initial_channels", c_int32), ("num_stages", c_int32),
+                ("upsample_rates", c_int32 * DVOC_MAX_STAGES), ("num_kernels", c_int32),
+                ("resblock_kernel_sizes", c_int32 * DVOC_MAX_KERNELS),
+                ("resblock_dilations", (c_int32 * 3) * DVOC_MAX_KERNELS),
+                ("resblock_type", c_int32), ("mi_layers", c_int32), ("lookahead", c_int32),
+                ("use_tanh", c_int32), ("max_batch", c_int32), ("max_frames", c_int32)]
+
+
+VOC_WEIGHT_FIELDS = ("post_w", "post_b", "mi_in_w", "mi_in_b", "lstm_w_ih", "lstm_w_hh",
+                     "lstm_b_ih", "lstm_b_hh", "mi_out_w", "mi_out_b", "conv_w", "conv_b", "act",
+                     "post_conv_w", "post_conv_b")
+
+
+class DvocWeights(ctypes.Structure):
+    _fields_ = [(f, c_void_p) for f in VOC_WEIGHT_FIELDS]
+
+
+class DvocBatch(ctypes.Structure):
+    _fields_ = [("n", c_int32), ("frames", c_int32), ("window", c_int32), ("latents", c_void_p),
+                ("lengths", c_void_p), ("lstm_h", c_void_p), ("lstm_c", c_void_p),
+                ("windows", c_void_p), ("valid", c_void_p), ("audio", c_void_p)]
 
 
 _lib = None
@@ -170,6 +200,23 @@ def lib() -> ctypes.CDLL:
     L.dllm_decode_step.restype = c_int32
     L.dllm_destroy.argtypes = [c_void_p]
     L.dllm_destroy.restype = c_int32
+    L.dvoc_create.argtypes = [POINTER(DvocConfig), POINTER(DvocWeights), POINTER(c_void_p)]
+    L.dvoc_create.restype = c_int32
+    L.dvoc_destroy.argtypes = [c_void_p]
+    L.dvoc_destroy.restype = c_int32
+    for name in ("dvoc_conv_floats", "dvoc_bias_floats", "dvoc_act_floats"):
+        getattr(L, name).argtypes = [POINTER(DvocConfig)]
+        getattr(L, name).restype = c_size_t
+    L.dvoc_hop.argtypes = [POINTER(DvocConfig)]
+    L.dvoc_hop.restype = c_int32
+    L.dvoc_stream_left_context.argtypes = [POINTER(DvocConfig)]
+    L.dvoc_stream_left_context.restype = c_int32
+    L.dvoc_workspace_size.argtypes = [c_void_p]
+    L.dvoc_workspace_size.restype = c_size_t
+    L.dvoc_decode.argtypes = [c_void_p, POINTER(DvocBatch), c_void_p, c_size_t, c_void_p]
+    L.dvoc_decode.restype = c_int32
+    L.dvoc_read_error.argtypes = [c_void_p, c_void_p, c_void_p, POINTER(c_uint32)]
+    L.dvoc_read_error.restype = c_int32
     _lib = L
     return L
 

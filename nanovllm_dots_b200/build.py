@@ -1,5 +1,5 @@
 """Build the shared library (``libdfm.so``: FM head, patch encoder, LLM decode
-attention) in-tree
+attention, vocoder) in-tree
 with nvcc for sm_100a.
 
     python -m nanovllm_dots_b200.build
@@ -19,8 +19,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdfm.so")
 SOURCES = ["dfm_api.cu"]
 DEPS = ["dfm_api.cu", "dpe_api.cu", "llm_api.cu", "common.cuh", "gemm.cuh", "attn_tc.cuh", "ew.cuh",
-        "pe.cuh", "llm_attn.cuh", "llm_step.cuh"]
-HEADERS = [os.path.join(os.path.dirname(PKG), "include", h) for h in ("dfm.h", "dpe.h", "dllm.h")]
+        "pe.cuh", "llm_attn.cuh", "llm_step.cuh", "voc_api.cu", "voc.cuh"]
+HEADERS = [os.path.join(os.path.dirname(PKG), "include", h) for h in ("dfm.h", "dpe.h", "dllm.h", "dvoc.h")]
 
 
 def nvcc() -> str:

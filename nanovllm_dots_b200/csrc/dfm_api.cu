@@ -1002,3 +1002,6 @@ extern "C" int dfm_paged_attention_noalloc(const void* q, void* out, const void*
 // ---------------------------------------------------------------- LLM decode attention
 // The LLM backbone's paged decode attention (include/dllm.h) shares them too.
 #include "llm_api.cu"
+
+// The vocoder (include/dvoc.h).
+#include "voc_api.cu"

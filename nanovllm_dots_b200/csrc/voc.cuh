@@ -1,0 +1,568 @@
+// Kernels of the vocoder's decode path (BigVGAN AudioVAE decoder,
+// ``nanovllm_dots/models/dots/native/vocoder/bigvgan.py``).
+//
+// Activations are fp32, frames-first: [request][frame][Cp] with Cp the
+// channel count padded to a multiple of 32 (one 128-byte swizzle row).
+//
+//   voc_conv_kernel   every convolution of the decoder as an implicit GEMM on
+//                     the tcgen05 tensor cores (kind::tf32, fp32 accumulate in
+//                     TMEM): out[t] = sum over taps j of x[t + off0 + j*dil] W_j;
+//                     tap j's A tile is a TMA box at the shifted frame
+//                     coordinate, frames outside the request read as zeros;
+//                     the epilogue adds bias, the residual, and the stage's
+//                     resblock sum
+//   voc_act_kernel    anti-aliased SnakeBeta (x2 upsample, activation, x2
+//                     downsample; ``alias_free_act.py:12-48``)
+//   voc_post_kernel   conv_post (7 causal taps to one channel) + tanh
+//   voc_linear_kernel fp32 linear layers of the front
+//   voc_lstm_step_kernel  one frame of one LSTM layer for every request
+//   voc_pack_kernel   the decoder input: a stream window after appending a
+//                     chunk, or one-shot latents masked to each length
+#pragma once
+
+#include "common.cuh"
+
+namespace dfm {
+
+// ---------------------------------------------------------------- tcgen05 tf32
+// Instruction descriptor of kind::tf32: tf32 A/B (format 2), fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+DFM_DEV void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                       uint32_t accumulate) {
+  const uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
+}
+
+DFM_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Round to the nearest tf32 value (ties away from zero), kept in an fp32 container.
+DFM_DEV float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// ---------------------------------------------------------------- conv
+constexpr int VC_BM = 128;
+constexpr int VC_BK = 32;  // fp32 elements per 128-byte swizzle row
+constexpr int VC_THREADS = 192;
+
+template <int BN, int STAGES>
+struct VcShape {
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "MMA N");
+  static constexpr int A_BYTES = VC_BM * VC_BK * 4;  // 16 KB: 128 frames x 32 channels
+  static constexpr int B_BYTES = BN * VC_BK * 4;
+  static_assert(B_BYTES % 1024 == 0, "swizzle atoms");
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128
+                                        : 2 * BN <= 256 ? 256 : 512;
+};
+
+struct VcArgs {
+  int tiles_m;        // M tiles over all requests: n * tiles_t
+  int tiles_t;        // 128-frame tiles per request
+  int N;              // output columns (a multiple of BN)
+  int nkb_c;          // 32-channel blocks of the input per tap
+  int taps, off0, dil;  // tap j reads frame t + off0 + j * dil
+  const float* bias;  // [N]
+  float* out;
+  long long out_b;    // floats between requests of out (and of res)
+  int out_ld;         // floats between frames t of out
+  int u, cp_out;      // column col of frame t is output frame t*u + col / cp_out ...
+  int out_rows;       // ... stored only below out_rows
+  const float* res;   // residual with out's layout, or null
+  int accum;          // 1: out += value (the stage's resblock sum)
+  float div;          // then out /= div (1: none)
+};
+
+// Persistent: CTA b takes tiles b, b + grid, ... with the M tiles fastest, so
+// CTAs working at once share W tiles in L2.  Warp 0 lane 0 loads (TMA), warp 1
+// owns TMEM and issues the MMAs, warps 2..5 run the epilogue from a
+// double-buffered TMEM accumulator.  Every wait is bounded.
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(VC_THREADS, 1)
+    voc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                    VcArgs p, uint32_t* err) {
+  using S = VcShape<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tm_full = empty + STAGES;  // [2]
+  uint64_t* tm_empty = tm_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.tiles_m * (p.N / BN);
+  const int nk = p.taps * p.nkb_c;
+
+  if (threadIdx.x == 0) {
+#pragma unroll 1
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tm_full[b], 1);
+      mbar_init(&tm_empty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // The first stages' weights do not depend on the previous kernel.
+      const int pre = (static_cast<int>(blockIdx.x) < total) ? (nk < STAGES ? nk : STAGES) : 0;
+      const int n00 = (blockIdx.x / p.tiles_m) * BN;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], S::STAGE_BYTES);
+        tma_load_2d(sB + kb * S::B_BYTES, &tmW, &full[kb], kb * VC_BK, n00);
+      }
+      pdl_wait();
+      int g = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        const int m = t % p.tiles_m, n0 = (t / p.tiles_m) * BN;
+        const int b = m / p.tiles_t, f0 = (m - b * p.tiles_t) * VC_BM;
+        int tap = 0, cb = 0;
+#pragma unroll 1
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (g >= pre) {
+            if (g >= STAGES && !mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+            tma_load_2d(sB + s * S::B_BYTES, &tmW, &full[s], kb * VC_BK, n0);
+          }
+          tma_load_3d(sA + s * S::A_BYTES, &tmA, &full[s], cb * VC_BK, f0 + p.off0 + tap * p.dil, b);
+          if (++cb == p.nkb_c) {
+            cb = 0;
+            ++tap;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_tf32(VC_BM, BN);
+      int g = 0, u = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++u) {
+        const int b = u & 1;
+        if (u >= 2 && !mbar_wait(&tm_empty[b], ((u >> 1) & 1) ^ 1, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * BN;
+#pragma unroll 1
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + s * S::A_BYTES);
+          const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < VC_BK / 8; ++kk)  // K = 8 tf32 (32 bytes) per MMA
+            umma_tf32(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+                      (kb | kk) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tm_full[b]);
+      }
+    }
+  } else {
+    pdl_wait();
+    const int q = warp & 3;
+    int u = 0;
+#pragma unroll 1
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++u) {
+      const int buf = u & 1;
+      const bool ready =
+          __all_sync(0xffffffffu, mbar_wait(&tm_full[buf], (u >> 1) & 1, abort_flag, err));
+      if (!ready) break;
+      tc_fence_after();
+      const int m = t % p.tiles_m, n0 = (t / p.tiles_m) * BN;
+      const int b = m / p.tiles_t;
+      const int f = (m - b * p.tiles_t) * VC_BM + q * 32 + lane;
+      const size_t rowoff = static_cast<size_t>(b) * p.out_b + static_cast<size_t>(f) * p.out_ld;
+      const uint32_t taddr = tmem + buf * BN + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
+        const int col = n0 + c;
+        if (f * p.u + col / p.cp_out >= p.out_rows) continue;
+        float v[32];
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 bb = __ldg(b4 + j);
+          v[4 * j] = __uint_as_float(r[4 * j]) + bb.x;
+          v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
+          v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
+          v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
+        }
+        float4* o4 = reinterpret_cast<float4*>(p.out + rowoff + col);
+        if (p.res) {
+          const float4* r4 = reinterpret_cast<const float4*>(p.res + rowoff + col);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = r4[j];
+            v[4 * j] += x.x; v[4 * j + 1] += x.y; v[4 * j + 2] += x.z; v[4 * j + 3] += x.w;
+          }
+        }
+        if (p.accum) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 x = o4[j];
+            v[4 * j] = x.x + v[4 * j]; v[4 * j + 1] = x.y + v[4 * j + 1];
+            v[4 * j + 2] = x.z + v[4 * j + 2]; v[4 * j + 3] = x.w + v[4 * j + 3];
+          }
+        }
+        if (p.div != 1.0f) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = v[j] / p.div;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- activation
+// Anti-aliased (Snake)Beta on [n][rows][cp] (``alias_free_act.py:43-48``,
+// ``alias_free_resample.py:44-81``, causal, ratio 2, 12-tap filters):
+//   u[2m+p] = 2 sum_{q<6} x[m-q] fu[2q+p]            (x[<0] = 0)
+//   y = u + ib * sin(a u)^2                             (a = exp(alpha), ib = 1/(exp(beta)+1e-9))
+//   out[m] = sum_{j<12} fd[j] y[max(2m+j-11, 0)]        (replicate padding on the left)
+// Thread: one channel (lanes = 32 consecutive channels, coalesced rows) and
+// VA_R consecutive output frames; it computes the 2 VA_R + 11 upsampled
+// values those frames need from VA_R + 11 input frames.
+constexpr int VA_R = 16;
+constexpr int VA_WARPS = 4;
+
+__global__ void __launch_bounds__(32 * VA_WARPS)
+    voc_act_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int cp,
+                   const float* __restrict__ prm, int round_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int m0 = (blockIdx.y * VA_WARPS + warp) * VA_R;
+  const size_t base = static_cast<size_t>(blockIdx.z) * rows * cp + c;
+  // parameters (constant) before the dependency wait
+  const float a = __ldg(prm + c), ib = __ldg(prm + cp + c);
+  float fu[12], fd[12];
+#pragma unroll
+  for (int j = 0; j < 12; ++j) {
+    fu[j] = __ldg(prm + 2 * cp + static_cast<size_t>(c) * 12 + j);
+    fd[j] = __ldg(prm + 14 * cp + static_cast<size_t>(c) * 12 + j);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (m0 >= rows) return;
+  float x[VA_R + 11];  // x[i] = in[m0 - 11 + i]
+#pragma unroll
+  for (int i = 0; i < VA_R + 11; ++i) {
+    const int m = m0 - 11 + i;
+    x[i] = (m >= 0 && m < rows) ? in[base + static_cast<size_t>(m) * cp] : 0.0f;
+  }
+  float y[2 * VA_R + 11];  // y[i] = act(u[2 m0 - 11 + i])
+#pragma unroll
+  for (int i = 0; i < 2 * VA_R + 11; ++i) {
+    // q = 2 m0 - 11 + i = 2 mm + ph with ph = (i + 1) & 1; x[mm] is window
+    // entry (i - 11 - ph) / 2 + 11 (an exact division)
+    const int ph = (i + 1) & 1;
+    const int xi = (i - 11 - ph) / 2 + 11;
+    float s = 0.0f;
+#pragma unroll
+    for (int qq = 0; qq < 6; ++qq) s += x[xi - qq] * fu[2 * qq + ph];
+    const float uu = 2.0f * s;
+    const float sn = sinf(uu * a);
+    y[i] = uu + ib * (sn * sn);
+  }
+  if (m0 == 0) {  // frames before the first: the first upsampled value (q = 0 is i = 11)
+#pragma unroll
+    for (int i = 0; i < 11; ++i) y[i] = y[11];
+  }
+#pragma unroll
+  for (int k = 0; k < VA_R; ++k) {
+    if (m0 + k >= rows) break;
+    float o = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 12; ++j) o += fd[j] * y[2 * k + j];
+    out[base + static_cast<size_t>(m0 + k) * cp] = round_out ? round_tf32(o) : o;
+  }
+}
+
+// ---------------------------------------------------------------- conv_post
+// audio[b][t] = act(bias + sum_{j<7} sum_c w[j][c] a[b][t-6+j][c]) for t < n_out
+// (a holds `rows` frames per request);
+// act = tanh or clamp to [-1, 1] (``bigvgan.py:632-638``).  A block computes
+// 256 frames from a shared-memory tile of 262 frames x 32 channels per pass.
+constexpr int VP_T = 256;
+
+__global__ void __launch_bounds__(VP_T)
+    voc_post_kernel(const float* __restrict__ a, float* __restrict__ audio, int rows, int cp,
+                    int n_out, long long audio_b, const float* __restrict__ w, const float* __restrict__ bias,
+                    int use_tanh) {
+  __shared__ float tile[VP_T + 6][33];
+  const int t0 = blockIdx.x * VP_T, t = t0 + threadIdx.x;
+  const size_t base = static_cast<size_t>(blockIdx.y) * rows * cp;
+  const float b0 = bias ? __ldg(bias) : 0.0f;
+  pdl_wait();
+  pdl_trigger();
+  float acc = 0.0f;
+#pragma unroll 1
+  for (int c0 = 0; c0 < cp; c0 += 32) {
+    __syncthreads();
+#pragma unroll 1
+    for (int i = threadIdx.x; i < (VP_T + 6) * 32; i += VP_T) {
+      const int r = i >> 5, cc = i & 31;
+      const int f = t0 - 6 + r;
+      tile[r][cc] = (f >= 0 && f < rows) ? a[base + static_cast<size_t>(f) * cp + c0 + cc] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+      const float* wj = w + static_cast<size_t>(j) * cp + c0;
+#pragma unroll 8
+      for (int cc = 0; cc < 32; ++cc) acc += __ldg(wj + cc) * tile[threadIdx.x + j][cc];
+    }
+  }
+  if (t < n_out) {
+    const float v = acc + b0;
+    audio[static_cast<size_t>(blockIdx.y) * audio_b + t] =
+        use_tanh ? tanhf(v) : fminf(fmaxf(v, -1.0f), 1.0f);
+  }
+}
+
+// ---------------------------------------------------------------- front
+// Y[orow(r)][j] = (b1[j] + sum_k X[r][k] W[j][k]) for r < M, j < N, with
+// orow(r) = (r / rpg) * ostride + r % rpg.  64 x 64 output tiles, 4 x 4 per
+// thread, fp32 FMA (the reference's fp32 nn.Linear).
+constexpr int VL_T = 64, VL_K = 16;
+
+__global__ void __launch_bounds__(256)
+    voc_linear_kernel(const float* __restrict__ X, int ldx, const float* __restrict__ W,
+                      const float* __restrict__ b1, float* __restrict__ Y, int ldy, int M, int N,
+                      int K, int rpg, int ostride) {
+  __shared__ float xs[VL_K][VL_T + 4];
+  __shared__ float ws[VL_K][VL_T + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int r0 = blockIdx.y * VL_T, j0 = blockIdx.x * VL_T;
+  pdl_wait();
+  pdl_trigger();
+  float acc[4][4] = {};
+#pragma unroll 1
+  for (int k0 = 0; k0 < K; k0 += VL_K) {
+#pragma unroll
+    for (int i = threadIdx.x; i < VL_K * VL_T; i += 256) {
+      const int rr = i / VL_K, kk = i % VL_K;
+      const int r = r0 + rr, j = j0 + rr, k = k0 + kk;
+      xs[kk][rr] = (r < M && k < K) ? X[static_cast<size_t>(r) * ldx + k] : 0.0f;
+      ws[kk][rr] = (j < N && k < K) ? __ldg(W + static_cast<size_t>(j) * K + k) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < VL_K; ++kk) {
+      float xv[4], wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        xv[i] = xs[kk][ty * 4 + i];
+        wv[i] = ws[kk][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj] += xv[i] * wv[jj];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + ty * 4 + i;
+    if (r >= M) continue;
+    const size_t orow = static_cast<size_t>(r / rpg) * ostride + r % rpg;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = j0 + tx * 4 + jj;
+      if (j < N) Y[orow * ldy + j] = acc[i][jj] + __ldg(b1 + j);
+    }
+  }
+}
+
+// One frame f of one LSTM layer for n requests (``SLSTM.stream_step``,
+// ``bigvgan.py:170-214``; gate order i, f, g, o):
+//   gates = (W_hh h_prev + b_hh) + gx[b][f]   (gx = W_ih x + b_ih)
+//   c = sig(f) c + sig(i) tanh(g);  h = sig(o) tanh(c)
+// h goes to h_next and to y[b][f] (plus skip[b][f] at the last layer).  A
+// block takes 8 hidden units (one per warp) for 32 requests (one per lane);
+// the 32 requests' h_prev sit transposed in shared memory.
+constexpr int VS_J = 8;
+
+__global__ void __launch_bounds__(32 * VS_J)
+    voc_lstm_step_kernel(const float* __restrict__ gx, int F, int f, const float* __restrict__ whh,
+                         const float* __restrict__ bhh, const float* __restrict__ h_prev,
+                         float* __restrict__ h_next, float* __restrict__ c, float* __restrict__ y,
+                         const float* __restrict__ skip, int n, int Hm) {
+  extern __shared__ float hs[];  // [Hm][33]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = blockIdx.x * VS_J + warp;
+  const int b0 = blockIdx.y * 32, b = b0 + lane;
+  pdl_wait();
+  pdl_trigger();
+#pragma unroll 1
+  for (int i = threadIdx.x; i < 32 * Hm; i += 32 * VS_J) {
+    const int bl = i / Hm, k = i - bl * Hm;
+    hs[k * 33 + bl] = (b0 + bl < n) ? h_prev[static_cast<size_t>(b0 + bl) * Hm + k] : 0.0f;
+  }
+  __syncthreads();
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* w0 = whh + static_cast<size_t>(j) * Hm;
+  const size_t gs = static_cast<size_t>(Hm) * Hm;
+#pragma unroll 1
+  for (int k = 0; k < Hm; k += 4) {
+    float hv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) hv[e] = hs[(k + e) * 33 + lane];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w0 + g * gs + k));
+      acc[g] += wv.x * hv[0];
+      acc[g] += wv.y * hv[1];
+      acc[g] += wv.z * hv[2];
+      acc[g] += wv.w * hv[3];
+    }
+  }
+  if (b >= n || j >= Hm) return;
+  const float* gxr = gx + (static_cast<size_t>(b) * F + f) * 4 * Hm;
+  float gate[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) gate[g] = (acc[g] + __ldg(bhh + g * Hm + j)) + gxr[g * Hm + j];
+  const float ig = 1.0f / (1.0f + expf(-gate[0]));
+  const float fg = 1.0f / (1.0f + expf(-gate[1]));
+  const float cg = tanhf(gate[2]);
+  const float og = 1.0f / (1.0f + expf(-gate[3]));
+  const size_t si = static_cast<size_t>(b) * Hm + j;
+  const float cn = fg * c[si] + ig * cg;
+  const float hn = og * tanhf(cn);
+  c[si] = cn;
+  h_next[si] = hn;
+  const size_t yi = (static_cast<size_t>(b) * F + f) * Hm + j;
+  y[yi] = skip ? hn + skip[yi] : hn;
+}
+
+// The decoder input [n][rows][lp] (``bigvgan.py:887-928`` for streams):
+//   window > 0: the window after appending z[b] (F frames) behind valid[b]
+//               frames (valid clamped to [0, W]); when the frames overflow W
+//               the window keeps the last W; zeros past the valid frames;
+//   window == 0: z[b][p] for p < len[b] (F when len is null), zeros elsewhere.
+// Rows past W (or the length) and channels past L are zero.
+__global__ void voc_pack_kernel(const float* __restrict__ z, const float* __restrict__ win,
+                                const int* __restrict__ valid, const int* __restrict__ len,
+                                float* __restrict__ dst, int n, int F, int W, int L, int lp,
+                                int rows) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t total = static_cast<size_t>(n) * rows * lp;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % lp);
+    const size_t bp = i / lp;
+    const int p = static_cast<int>(bp % rows), b = static_cast<int>(bp / rows);
+    float v = 0.0f;
+    if (c < L) {
+      if (W > 0) {
+        int vb = valid[b];
+        vb = vb < 0 ? 0 : (vb > W ? W : vb);
+        const int nv = vb + F < W ? vb + F : W;
+        const int s = vb + F - W > 0 ? vb + F - W : 0;
+        if (p < nv) {
+          const int q = p + s;
+          v = q < vb ? win[(static_cast<size_t>(b) * W + q) * L + c]
+                     : z[(static_cast<size_t>(b) * F + (q - vb)) * L + c];
+        }
+      } else {
+        const int lb = len ? len[b] : F;
+        if (p < lb && p < F) v = z[(static_cast<size_t>(b) * F + p) * L + c];
+      }
+    }
+    dst[i] = v;
+  }
+}
+
+// windows[b][p][c] = dinput[b][p][c] for p < W, c < L (the new stream windows).
+__global__ void voc_window_store_kernel(const float* __restrict__ din, float* __restrict__ win,
+                                        int n, int W, int L, int lp, int rows) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t total = static_cast<size_t>(n) * W * L;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % L);
+    const size_t bp = i / L;
+    const int p = static_cast<int>(bp % W), b = static_cast<int>(bp / W);
+    win[i] = din[(static_cast<size_t>(b) * rows + p) * lp + c];
+  }
+}
+
+// dst[i] = src[i] (the LSTM state hand-back).
+__global__ void voc_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t count) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
+}  // namespace dfm
