@@ -1,5 +1,6 @@
 """The C-ABI library builds, loads without a GPU and exports every entry point
-``include/dfm.h``, ``include/dpe.h`` and ``include/dllm.h`` declare; host-side
+``include/dfm.h``, ``include/dpe.h``, ``include/dllm.h`` and ``include/dvoc.h``
+declare; host-side
 bookkeeping that needs no GPU."""
 from __future__ import annotations
 
@@ -19,13 +20,15 @@ INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 HEADER = os.path.join(INCLUDE, "dfm.h")
 PE_HEADER = os.path.join(INCLUDE, "dpe.h")
 LLM_HEADER = os.path.join(INCLUDE, "dllm.h")
+VOC_HEADER = os.path.join(INCLUDE, "dvoc.h")
 
 
 def declared_functions():
     names = set()
-    for path, prefix in ((HEADER, "dfm_"), (PE_HEADER, "dpe_"), (LLM_HEADER, "dllm_")):
+    for path, prefix in ((HEADER, "dfm_"), (PE_HEADER, "dpe_"), (LLM_HEADER, "dllm_"),
+                         (VOC_HEADER, "dvoc_")):
         src = open(path).read()
-        found = re.findall(rf"^\s*(?:int|size_t|const char\*)\s+({prefix}\w+)\s*\(", src, re.M)
+        found = re.findall(rf"^\s*(?:int|int32_t|size_t|const char\*)\s+({prefix}\w+)\s*\(", src, re.M)
         assert found, f"no declarations parsed from {path}"
         names |= set(found)
     return sorted(names)
