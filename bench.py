@@ -21,8 +21,9 @@ no GPU MeanFlow cache head) on a bounded sample of the same workload.
 
 Other rows of the build, each with its own metric line (not the headline):
 ``--workload pe`` (the patch encoder: one batched decode_patch of 64 requests),
-``--workload llmattn`` (the LLM backbone's paged decode attention, one layer)
-and ``--workload llmdecode`` (the whole 28-layer backbone decode step).
+``--workload llmattn`` (the LLM backbone's paged decode attention, one layer),
+``--workload llmdecode`` (the whole 28-layer backbone decode step) and
+``--workload voc`` / ``voc1`` (the vocoder: strict streaming / one-shot).
 """
 from __future__ import annotations
 
@@ -52,7 +53,7 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2",
                     choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe", "llmattn",
-                             "llmdecode", "engine"],
+                             "llmdecode", "engine", "voc", "voc1"],
                     help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
                          "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool); "
@@ -62,7 +63,8 @@ def parse():
                          "sequences, Qwen2 GQA 12/2 x 128); llmdecode = the whole backbone "
                          "decode step (28 layers, 64 sequences); engine = the engine drop-in "
                          "(fm_accel='b200' dispatch over engine-style histories) against dfm_step "
-                         "alone")
+                         "alone; voc = the vocoder streaming 16-frame chunks for 64 requests; "
+                         "voc1 = the vocoder decoding 64 10-second utterances one-shot")
     ap.add_argument("--cpu-sample", type=int, default=64,
                     help="requests in the CPU baseline sample (64 = one whole tick)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1068,6 +1070,220 @@ def run_engine(args, rank, world):
     head.close()
 
 
+# --------------------------------------------------------------------------- #
+# Vocoder (``--workload voc`` streaming, ``--workload voc1`` one-shot)         #
+# --------------------------------------------------------------------------- #
+VOC_METRIC = "vocoder xRT (audio-s/s), strict streaming of 16-frame chunks, conc 64 per GPU"
+VOC1_METRIC = "vocoder xRT (audio-s/s), one-shot 10 s utterances, conc 64 per GPU"
+VOC_CHUNK, VOC_ONESHOT_FRAMES, VOC_FRAME_S = 16, 250, 0.04
+
+
+def voc_conv_flops(cfg, T: int, n: int) -> list[float]:
+    """Algorithmic FLOPs of each decoder convolution (execution order) for n
+    requests of T latent frames: 2 x output frames x Cout x Cin x taps, with the
+    unpadded channel counts and only the valid frames."""
+    out = [2.0 * n * T * cfg.initial_channels * cfg.latent_dim * (2 * cfg.lookahead + 1)]
+    t = T
+    for i, u in enumerate(cfg.upsample_rates):
+        cin, c = cfg.stage_channels(i - 1), cfg.stage_channels(i)
+        out.append(2.0 * n * t * u * c * 2 * cin)
+        t *= u
+        for k, dil in zip(cfg.resblock_kernel_sizes, cfg.resblock_dilations):
+            layers = 2 * len(dil) if cfg.resblock == "1" else 2
+            out += [2.0 * n * t * c * c * k] * layers
+    return out
+
+
+def run_voc(args, rank, world, oneshot: bool):
+    from nanovllm_dots_b200 import synthetic as syn
+    from nanovllm_dots_b200.vocoder import B200Vocoder
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = syn.VOC_BASE
+    n = 64
+    w = syn.make_voc_weights(cfg, seed=1)
+    W = VOC_CHUNK + cfg.lookahead + _voc_left(cfg)
+    F = VOC_ONESHOT_FRAMES if oneshot else VOC_CHUNK
+    T = F if oneshot else W
+    voc = B200Vocoder(w, cfg, max_batch=n, max_frames=T, device=dev)
+    assert oneshot or voc.stream_window_size(VOC_CHUNK) == W
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    Lm, Hm = cfg.latent_dim, 4 * cfg.latent_dim
+    lat = torch.randn(n, F, Lm, device=dev, generator=g)
+    h = torch.zeros(cfg.mi_layers, n, Hm, device=dev)
+    c = torch.zeros_like(h)
+    audio = torch.empty(n, T * cfg.hop, device=dev)
+    if oneshot:
+        b = voc.batch(n, F, 0, audio, latents=lat, h=h, c=c)
+    else:
+        win = torch.randn(n, W, Lm, device=dev, generator=g)        # steady state: windows full
+        valid = torch.full((n,), W, dtype=torch.int32, device=dev)
+        b = voc.batch(n, F, W, audio, latents=lat, h=h, c=c, windows=win, valid=valid)
+    stream = torch.cuda.current_stream(dev)
+
+    def call():
+        if oneshot:
+            h.zero_()
+            c.zero_()
+        voc.launch(b)
+
+    call()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        call()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    voc.check_errors()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    eager0, eager1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eager0.record(stream)
+    for _ in range(3):
+        call()
+    eager1.record(stream)
+    eager1.synchronize()
+    eager_ms = eager0.elapsed_time(eager1) / 3
+    voc.check_errors()
+
+    # each decoder convolution launched alone with the call's arguments
+    flops = voc_conv_flops(cfg, F if oneshot else W, n)
+    conv_us = []
+    reps = 3
+    for i in range(voc.num_convs):
+        voc.launch(b, conv=i)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(reps):
+            voc.launch(b, conv=i)
+        c1.record(stream)
+        c1.synchronize()
+        conv_us.append(c0.elapsed_time(c1) * 1000 / reps)
+    voc.check_errors()
+    hbm, bf16, peak_kind = load_peaks()
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if peak_kind == "measured" else {}
+    tf32 = 0.5 * peaks.get("bf16_tflops_sustained", 1400.0)
+    conv_total_us = sum(conv_us)
+    top = max(range(len(conv_us)), key=lambda i: conv_us[i] * 1.0)
+    heavy = max(range(len(flops)), key=lambda i: flops[i])
+    ach = lambda fl, us: fl / (us * 1e-6) / 1e12
+
+    # end to end through the public API: pinned host latents in, emitted audio out
+    audio_s = n * F * VOC_FRAME_S
+    h_lat = lat.cpu().pin_memory()
+    if oneshot:
+        def e2e_step():
+            outs = voc.decode_batch(h_lat)
+            return [o.to("cpu", non_blocking=True) for o in outs]
+        d2h = n * F * cfg.hop * 4
+    else:
+        states = [voc.init_stream_state(1, VOC_CHUNK) for _ in range(n)]
+        for st in states:
+            st.window.normal_(generator=g)
+            st.total, st.emitted = 10 ** 6, 10 ** 6 - cfg.lookahead
+
+        def e2e_step():
+            outs = voc.stream_step_many(states, h_lat)
+            return [o.to("cpu", non_blocking=True) for o in outs]
+        d2h = n * VOC_CHUNK * cfg.hop * 4
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(args.steps, 10))
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    f1.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / e2e_steps
+    voc.check_errors()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import voc_oracle as vo
+        orc = vo.VocOracle(w, cfg, dtype=torch.float32)
+        t0 = time.perf_counter()
+        if oneshot:
+            frames = 50
+            orc.inference(lat[:1, :frames].cpu())
+            sample = f"one {frames}-frame utterance (2 s) of the same workload"
+        else:
+            frames = 0
+            for i in range(2):
+                st = vo.stream_init(orc, VOC_CHUNK)
+                st.window.copy_(win[i].cpu())
+                st.total, st.emitted = 10 ** 6, 10 ** 6 - cfg.lookahead
+                vo.stream_step(orc, st, lat[i].cpu())
+                frames += VOC_CHUNK
+            sample = "2 request stream steps (16-frame chunks, 51-frame windows) of the same workload"
+        secs = time.perf_counter() - t0
+        cpu = {"value": round(frames * VOC_FRAME_S / secs, 4), "unit": "audio-s/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{sample}: this build's restatement of the reference AudioVAE "
+                         f"(oracle/voc_oracle.py), fp32 torch on the host, {secs:.2f} s"}
+    if rank == 0:
+        line = {"metric": VOC1_METRIC if oneshot else VOC_METRIC,
+                "value": round(audio_s / (ms / 1000), 2), "unit": "audio-s/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32/tf32",
+                "data": "synthetic (seeded random-init vocoder of the VOC_BASE shape, N(0,1) latents)",
+                "config": {"workload": "voc1" if oneshot else "voc", "requests_per_gpu": n,
+                           "frames_per_request": F, "decoded_frames": T, "hop": cfg.hop,
+                           "initial_channels": cfg.initial_channels,
+                           "upsample_rates": list(cfg.upsample_rates),
+                           "l2": "activations (GBs per call) larger than L2, no flush",
+                           "parallelism": f"request-sharded x{world}"},
+                "e2e": {"value": round(audio_s / (e2e_ms / 1000), 2), "unit": "audio-s/s",
+                        "h2d_bytes_per_step": h_lat.numel() * 4, "d2h_bytes_per_step": d2h,
+                        "ms_per_step": round(e2e_ms, 4), "api": "decode_batch" if oneshot else "stream_step_many"},
+                "eager_ms_per_step": round(eager_ms, 4),
+                "gpu_launches": voc_launches(cfg, F, oneshot, voc.num_convs) * args.steps,
+                "roofline": {"kernel": f"voc_conv_kernel #{heavy} (the call's largest convolution)",
+                             "bound": "tensor", "achieved": round(ach(flops[heavy], conv_us[heavy]), 1),
+                             "peak": round(tf32, 1), "unit": "TFLOP/s",
+                             "frac": round(ach(flops[heavy], conv_us[heavy]) / tf32, 4), "traffic": None,
+                             "algorithmic_per_launch": flops[heavy],
+                             "peak_source": f"tf32 = 0.5 x {peak_kind} sustained bf16 (the nominal tf32:bf16 ratio)",
+                             "timing": "dvoc_conv_launch, CUDA events, 3 launches"},
+                "kernels": {"convs": {"count": len(conv_us), "us": round(conv_total_us, 1),
+                                      "achieved": round(ach(sum(flops), conv_total_us), 1),
+                                      "unit": "TFLOP/s", "frac": round(ach(sum(flops), conv_total_us) / tf32, 4),
+                                      "share_of_call": round(conv_total_us / (ms * 1000), 4)},
+                            "slowest_conv": {"index": top, "us": round(conv_us[top], 1),
+                                             "achieved": round(ach(flops[top], conv_us[top]), 1)},
+                            "per_conv_us": [round(x, 1) for x in conv_us]},
+                "clocks": clk.summary(), "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    graph = None
+    voc.close()
+
+
+def voc_launches(cfg, F: int, oneshot: bool, convs: int) -> int:
+    """Kernels of one dvoc_decode call: the front (3 linears, per LSTM layer its
+    input linear, F steps and the state copy), the decoder input (and the
+    window store), every convolution and activation, conv_post."""
+    per = 6 if cfg.resblock == "1" else 2
+    acts = len(cfg.upsample_rates) * len(cfg.resblock_kernel_sizes) * per + 1
+    return 3 + cfg.mi_layers * (2 + F) + (1 if oneshot else 2) + convs + acts + 1
+
+
+def _voc_left(cfg) -> int:
+    import ctypes
+    from nanovllm_dots_b200 import _lib
+    from nanovllm_dots_b200.vocoder import dvoc_config
+    c = dvoc_config(cfg, 1, 1)
+    return _lib.lib().dvoc_stream_left_context(ctypes.byref(c))
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -1088,6 +1304,8 @@ def main():
             run_llmdecode(args, rank, world)
         elif args.workload == "engine":
             run_engine(args, rank, world)
+        elif args.workload in ("voc", "voc1"):
+            run_voc(args, rank, world, oneshot=args.workload == "voc1")
         else:
             run_b200(args, rank, world)
     finally:

@@ -153,6 +153,15 @@ size_t dvoc_workspace_size(void* handle);
 int dvoc_decode(void* handle, const DvocBatch* batch, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* Profiling: the number of decoder convolutions, and one of them (index in
+ * execution order: conv_pre, then per stage its transposed conv and its
+ * resblock convs) launched alone with the arguments a dvoc_decode of `batch`
+ * would give it, reading whatever the workspace holds.  bench.py times the
+ * decoder's own convolution launches with these; no reference counterpart. */
+int32_t dvoc_num_convs(void* handle);
+int dvoc_conv_launch(void* handle, const DvocBatch* batch, void* workspace, size_t workspace_bytes,
+                     int32_t index, void* stream);
+
 /* Synchronise `stream` and return the device error word of the workspace
  * (DFM_DEV_ERR_* bits: a bounded wait that gave up); the word is cleared. */
 int dvoc_read_error(void* handle, void* workspace, void* stream, uint32_t* err_word);

@@ -28,7 +28,7 @@ EXPORTS = ("dfm_create", "dfm_workspace_size", "dfm_pool_bytes", "dfm_step", "df
            "dllm_create", "dllm_step_workspace_size", "dllm_decode_step", "dllm_destroy",
            "dvoc_create", "dvoc_destroy", "dvoc_conv_floats", "dvoc_bias_floats", "dvoc_act_floats",
            "dvoc_hop", "dvoc_stream_left_context", "dvoc_workspace_size", "dvoc_decode",
-           "dvoc_read_error")
+           "dvoc_read_error", "dvoc_num_convs", "dvoc_conv_launch")
 
 
 class DfmConfig(ctypes.Structure):
@@ -217,6 +217,10 @@ def lib() -> ctypes.CDLL:
     L.dvoc_decode.restype = c_int32
     L.dvoc_read_error.argtypes = [c_void_p, c_void_p, c_void_p, POINTER(c_uint32)]
     L.dvoc_read_error.restype = c_int32
+    L.dvoc_num_convs.argtypes = [c_void_p]
+    L.dvoc_num_convs.restype = c_int32
+    L.dvoc_conv_launch.argtypes = [c_void_p, POINTER(DvocBatch), c_void_p, c_size_t, c_int32, c_void_p]
+    L.dvoc_conv_launch.restype = c_int32
     _lib = L
     return L
 

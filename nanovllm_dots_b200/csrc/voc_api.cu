@@ -400,9 +400,12 @@ int dvoc_read_error(void* handle, void* workspace, void* stream, uint32_t* err_w
   return DFM_OK;
 }
 
-int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t workspace_bytes,
-                void* stream) {
+// One call (dvoc_decode), or, with only >= 0, only the decoder convolution of
+// that index with the call's arguments (dvoc_conv_launch).
+static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t workspace_bytes,
+                   void* stream, int only) {
   VocHandle* h = static_cast<VocHandle*>(handle);
+  const bool all = only < 0;
   if (!h || !b || !workspace) return DFM_ERR_INVALID_ARG;
   const DvocConfig& c = h->c;
   const int n = b->n, F = b->frames, W = b->window;
@@ -449,7 +452,7 @@ int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t worksp
 
   const int L = h->L, Hm = h->Hm, M = n * F;
   // ---- front: post_proj, Linear(L, 4L), LSTM, Linear(4L, L)
-  if (F > 0) {
+  if (all && F > 0) {
     VCK(voc_linear(b->latents, L, h->w.post_w, h->w.post_b, P(h->o_p), L, M, L, L, s));
     VCK(voc_linear(P(h->o_p), L, h->w.mi_in_w, h->w.mi_in_b, P(h->o_s), Hm, M, Hm, L, s));
     const float* in = P(h->o_s);
@@ -481,16 +484,19 @@ int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t worksp
   }
   // ---- decoder input
   const size_t din = static_cast<size_t>(n) * r.cpre * h->Lp;
-  VCK(launch_pdl(voc_pack_kernel, dim3(grid_for(din)), dim3(256), 0, s,
+  if (all)
+    VCK(launch_pdl(voc_pack_kernel, dim3(grid_for(din)), dim3(256), 0, s,
                  static_cast<const float*>(P(h->o_z)), static_cast<const float*>(b->windows),
                  b->valid, b->lengths, P(h->o_din), n, F, W, L, h->Lp, r.cpre));
-  if (streaming && F > 0)
+  if (all && streaming && F > 0)
     VCK(launch_pdl(voc_window_store_kernel, dim3(grid_for(static_cast<size_t>(n) * W * L)), dim3(256),
                    0, s, static_cast<const float*>(P(h->o_din)), b->windows, n, W, L, h->Lp, r.cpre));
   // ---- decoder
   size_t li = 0, ai = 0;
-  const VocConv& pre = h->convs[li++];
-  VCK(voc_conv(*h, pre, h->m_din, n, r.cpre, P(h->o_x), static_cast<long long>(r.cpre) * c0p,
+  auto pick = [&](size_t i) { return all || static_cast<int>(i) == only; };
+  const VocConv& pre = h->convs[li];
+  if (pick(li++))
+    VCK(voc_conv(*h, pre, h->m_din, n, r.cpre, P(h->o_x), static_cast<long long>(r.cpre) * c0p,
                r.cpre, nullptr, 0, 1.0f, err, s));
   for (int i = 0; i < h->ns; ++i) {
     const int cp = vpad(h->ch[i]), rows = r.cap[i], rows_in = i ? r.cap[i - 1] : r.cpre;
@@ -500,7 +506,9 @@ int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t worksp
     float* H = P(h->o_h);
     float* A = P(h->o_a);
     float* C1 = P(h->o_c1);
-    VCK(voc_conv(*h, h->convs[li++], h->m_xin[i], n, rows_in, U, ob, rows, nullptr, 0, 1.0f, err, s));
+    if (pick(li))
+      VCK(voc_conv(*h, h->convs[li], h->m_xin[i], n, rows_in, U, ob, rows, nullptr, 0, 1.0f, err, s));
+    ++li;
     for (int j = 0; j < h->nk; ++j) {
       const int nl = c.resblock_type == 1 ? 3 : 2;
       for (int l = 0; l < nl; ++l) {
@@ -509,16 +517,23 @@ int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t worksp
         float* dst = last ? X : H;
         const int acc = last && j > 0;
         const float dv = last && j == h->nk - 1 ? static_cast<float>(h->nk) : 1.0f;
-        VCK(voc_act(src, A, n, rows, cp, h->w.act + h->act_off[ai++], 1, s));
+        if (all) VCK(voc_act(src, A, n, rows, cp, h->w.act + h->act_off[ai], 1, s));
+        ++ai;
         if (c.resblock_type == 1) {
-          VCK(voc_conv(*h, h->convs[li++], h->m_act[i], n, rows, C1, ob, rows, nullptr, 0, 1.0f, err, s));
-          VCK(voc_act(C1, A, n, rows, cp, h->w.act + h->act_off[ai++], 1, s));
+          if (pick(li))
+            VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, C1, ob, rows, nullptr, 0, 1.0f, err, s));
+          ++li;
+          if (all) VCK(voc_act(C1, A, n, rows, cp, h->w.act + h->act_off[ai], 1, s));
+          ++ai;
         }
-        VCK(voc_conv(*h, h->convs[li++], h->m_act[i], n, rows, dst, ob, rows, src, acc, dv, err, s));
+        if (pick(li))
+          VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, dst, ob, rows, src, acc, dv, err, s));
+        ++li;
       }
     }
   }
   // ---- activation_post, conv_post, tanh
+  if (!all) return DFM_OK;
   const int last = h->ns - 1, cpl = vpad(h->ch[last]), rows = r.cap[last];
   VCK(voc_act(P(h->o_x), P(h->o_a), n, rows, cpl, h->w.act + h->act_off[ai++], 0, s));
   const long long samples = r.t[last];
@@ -528,6 +543,22 @@ int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t worksp
                  c.use_tanh));
 #undef VCK
   return DFM_OK;
+}
+
+int dvoc_decode(void* handle, const DvocBatch* b, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  return voc_run(handle, b, workspace, workspace_bytes, stream, -1);
+}
+
+int32_t dvoc_num_convs(void* handle) {
+  return handle ? static_cast<int32_t>(static_cast<VocHandle*>(handle)->convs.size()) : 0;
+}
+
+int dvoc_conv_launch(void* handle, const DvocBatch* b, void* workspace, size_t workspace_bytes,
+                     int32_t index, void* stream) {
+  VocHandle* h = static_cast<VocHandle*>(handle);
+  if (!h || index < 0 || index >= static_cast<int32_t>(h->convs.size())) return DFM_ERR_INVALID_ARG;
+  return voc_run(handle, b, workspace, workspace_bytes, stream, index);
 }
 
 }  // extern "C"

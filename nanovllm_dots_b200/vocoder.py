@@ -210,19 +210,37 @@ class B200Vocoder:
         self._zero_len = None
 
     # ------------------------------------------------------------------ core call
-    def _call(self, n: int, frames: int, window: int, latents=None, lengths=None, h=None, c=None,
-              windows=None, valid=None) -> torch.Tensor:
-        T = window if window else frames
-        audio = torch.empty(n, T * self.hop_size, dtype=torch.float32, device=self.device)
+    def batch(self, n: int, frames: int, window: int, audio: torch.Tensor, latents=None,
+              lengths=None, h=None, c=None, windows=None, valid=None) -> _lib.DvocBatch:
+        """The ``DvocBatch`` of one call over caller-owned device tensors."""
         b = _lib.DvocBatch()
         b.n, b.frames, b.window = n, frames, window
         b.latents, b.lengths = _lib.ptr(latents), _lib.ptr(lengths)
         b.lstm_h, b.lstm_c = _lib.ptr(h), _lib.ptr(c)
         b.windows, b.valid = _lib.ptr(windows), _lib.ptr(valid)
         b.audio = audio.data_ptr()
+        return b
+
+    def launch(self, b: _lib.DvocBatch, conv: int | None = None) -> None:
+        """``dvoc_decode`` on the current stream (or, with ``conv``, only that
+        decoder convolution: ``dvoc_conv_launch``, for profiling)."""
         s = torch.cuda.current_stream(self.device).cuda_stream
-        _lib.check(_lib.lib().dvoc_decode(self._h, ctypes.byref(b), self.ws.data_ptr(),
-                                          self.ws.numel(), s), "dvoc_decode")
+        L = _lib.lib()
+        if conv is None:
+            _lib.check(L.dvoc_decode(self._h, ctypes.byref(b), self.ws.data_ptr(), self.ws.numel(), s),
+                       "dvoc_decode")
+        else:
+            _lib.check(L.dvoc_conv_launch(self._h, ctypes.byref(b), self.ws.data_ptr(), self.ws.numel(),
+                                          conv, s), "dvoc_conv_launch")
+
+    @property
+    def num_convs(self) -> int:
+        return _lib.lib().dvoc_num_convs(self._h)
+
+    def _call(self, n: int, frames: int, window: int, **tensors) -> torch.Tensor:
+        T = window if window else frames
+        audio = torch.empty(n, T * self.hop_size, dtype=torch.float32, device=self.device)
+        self.launch(self.batch(n, frames, window, audio, **tensors))
         return audio
 
     def check_errors(self) -> None:
