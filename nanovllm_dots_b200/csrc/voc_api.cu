@@ -45,6 +45,7 @@ struct VocHandle {
   CUtensorMap m_din;
   CUtensorMap m_xin[DVOC_MAX_STAGES];
   CUtensorMap m_act[DVOC_MAX_STAGES];
+  CUtensorMap m_act_h[DVOC_MAX_STAGES];  // 64-frame boxes (halo kernel)
 };
 
 int voc_validate(const DvocConfig& c) {
@@ -181,15 +182,15 @@ void voc_layout(VocHandle& h) {
   h.total = o;
 }
 
-// 3-D fp32 activation [n][rows][cp], box {32 channels, 128 frames, 1}.
-bool voc_map_act(CUtensorMap* m, const void* base, int n, int rows, int cp) {
+// 3-D fp32 activation [n][rows][cp], box {32 channels, box_rows frames, 1}.
+bool voc_map_act(CUtensorMap* m, const void* base, int n, int rows, int cp, int box_rows = VC_BM) {
   auto fn = encode_fn();
   if (!fn || !base) return false;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(cp), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(n)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(cp) * 4,
                            static_cast<cuuint64_t>(cp) * rows * 4};
-  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t es[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -217,6 +218,9 @@ int voc_bn(int N) {
   return 32;
 }
 
+// Conv CTAs that fit on one SM by shared memory (the kernels allow 2).
+int voc_ctas_per_sm(int smem) { return 2 * (smem + 1024) <= 233472 ? 2 : 1; }
+
 template <int BN, int ST>
 cudaError_t voc_conv_launch(const CUtensorMap& a, const CUtensorMap& w, const VcArgs& p,
                             uint32_t* err, cudaStream_t s) {
@@ -226,13 +230,37 @@ cudaError_t voc_conv_launch(const CUtensorMap& a, const CUtensorMap& w, const Vc
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
   const int tiles = p.tiles_m * (p.N / BN);
-  const int grid = tiles < sm_count() ? tiles : sm_count();
+  const int ctas = voc_ctas_per_sm(smem) * sm_count();
+  const int grid = tiles < ctas ? tiles : ctas;
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, p, err);
 }
 
+template <int BN, int SA, int SB>
+cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const VcArgs& p,
+                            uint32_t* err, cudaStream_t s) {
+  static std::atomic<uint64_t> attr_done{0};
+  auto fn = voc_conv_halo_kernel<BN, SA, SB>;
+  constexpr int smem = VhShape<BN, SA, SB>::SMEM;
+  cudaError_t r = smem_attr_once(attr_done, fn, smem);
+  if (r != cudaSuccess) return r;
+  const int tiles = p.tiles_m * (p.N / BN);
+  const int ctas = voc_ctas_per_sm(smem) * sm_count();
+  const int grid = tiles < ctas ? tiles : ctas;
+  return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, p, err);
+}
+
+// Narrow convolutions whose taps span at most VH_HALO frames run on the halo
+// kernel (one A tile per channel block for all taps).
+bool voc_halo(const VocConv& v) {
+  return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.N <= 192 && v.u == 1;
+}
+
+int voc_halo_bn(int N) { return N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : N % 64 == 0 ? 64 : 32; }
+
 cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& amap, int n,
                      int rows_in, float* out, long long out_b, int out_rows, const float* res,
-                     int accum, float div, uint32_t* err, cudaStream_t s) {
+                     int accum, float div, uint32_t* err, cudaStream_t s,
+                     const CUtensorMap* halo_map = nullptr) {
   VcArgs p;
   p.tiles_t = rows_in / VC_BM;
   p.tiles_m = n * p.tiles_t;
@@ -251,12 +279,20 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
   p.res = res;
   p.accum = accum;
   p.div = div;
+  if (halo_map && voc_halo(v)) {
+    switch (voc_halo_bn(v.N)) {
+      case 128: return voc_halo_launch<128, 2, 3>(*halo_map, v.wmap, p, err, s);
+      case 96: return voc_halo_launch<96, 2, 4>(*halo_map, v.wmap, p, err, s);
+      case 64: return voc_halo_launch<64, 2, 6>(*halo_map, v.wmap, p, err, s);
+      default: return voc_halo_launch<32, 2, 6>(*halo_map, v.wmap, p, err, s);
+    }
+  }
   switch (voc_bn(v.N)) {
     case 256: return voc_conv_launch<256, 4>(amap, v.wmap, p, err, s);
     case 128: return voc_conv_launch<128, 6>(amap, v.wmap, p, err, s);
     case 96: return voc_conv_launch<96, 7>(amap, v.wmap, p, err, s);
-    case 64: return voc_conv_launch<64, 8>(amap, v.wmap, p, err, s);
-    default: return voc_conv_launch<32, 8>(amap, v.wmap, p, err, s);
+    case 64: return voc_conv_launch<64, 4>(amap, v.wmap, p, err, s);
+    default: return voc_conv_launch<32, 4>(amap, v.wmap, p, err, s);
   }
 }
 
@@ -375,7 +411,8 @@ int dvoc_create(const DvocConfig* cfg, const DvocWeights* w, void** out) {
   voc_tables(*h);
   voc_layout(*h);
   for (VocConv& v : h->convs) {
-    if (!voc_map_w(&v.wmap, w->conv_w + v.w_off, v.N, v.taps * v.cin_p, voc_bn(v.N))) {
+    const int bn = voc_halo(v) ? voc_halo_bn(v.N) : voc_bn(v.N);
+    if (!voc_map_w(&v.wmap, w->conv_w + v.w_off, v.N, v.taps * v.cin_p, bn)) {
       delete h;
       return DFM_ERR_CUDA;
     }
@@ -434,7 +471,8 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
     for (int i = 0; ok && i < h->ns; ++i) {
       const int cin_p = i ? vpad(h->ch[i - 1]) : c0p, rows_in = i ? r.cap[i - 1] : r.cpre;
       ok = voc_map_act(&h->m_xin[i], P(h->o_x), n, rows_in, cin_p) &&
-           voc_map_act(&h->m_act[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i]));
+           voc_map_act(&h->m_act[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i])) &&
+           voc_map_act(&h->m_act_h[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i]), VH_BOX);
     }
     if (!ok) {
       h->plan_ws = nullptr;
@@ -521,13 +559,15 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
         ++ai;
         if (c.resblock_type == 1) {
           if (pick(li))
-            VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, C1, ob, rows, nullptr, 0, 1.0f, err, s));
+            VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, C1, ob, rows, nullptr, 0, 1.0f, err, s,
+                         &h->m_act_h[i]));
           ++li;
           if (all) VCK(voc_act(C1, A, n, rows, cp, h->w.act + h->act_off[ai], 1, s));
           ++ai;
         }
         if (pick(li))
-          VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, dst, ob, rows, src, acc, dv, err, s));
+          VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, dst, ob, rows, src, acc, dv, err, s,
+                       &h->m_act_h[i]));
         ++li;
       }
     }
