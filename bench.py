@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2",
                     choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe", "llmattn",
-                             "llmdecode", "engine", "voc", "voc1"],
+                             "llmdecode", "engine", "voc", "voc1", "vocprof"],
                     help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
                          "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool); "
@@ -64,7 +64,8 @@ def parse():
                          "decode step (28 layers, 64 sequences); engine = the engine drop-in "
                          "(fm_accel='b200' dispatch over engine-style histories) against dfm_step "
                          "alone; voc = the vocoder streaming 16-frame chunks for 64 requests; "
-                         "voc1 = the vocoder decoding 64 10-second utterances one-shot")
+                         "voc1 = the vocoder decoding 64 10-second utterances one-shot; vocprof = voc "
+                         "with 16 requests (a small case for ncu captures)")
     ap.add_argument("--cpu-sample", type=int, default=64,
                     help="requests in the CPU baseline sample (64 = one whole tick)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1073,8 +1074,8 @@ def run_engine(args, rank, world):
 # --------------------------------------------------------------------------- #
 # Vocoder (``--workload voc`` streaming, ``--workload voc1`` one-shot)         #
 # --------------------------------------------------------------------------- #
-VOC_METRIC = "vocoder xRT (audio-s/s), strict streaming of 16-frame chunks, conc 64 per GPU"
-VOC1_METRIC = "vocoder xRT (audio-s/s), one-shot 10 s utterances, conc 64 per GPU"
+VOC_METRIC = "vocoder xRT (audio-s/s), strict streaming of 16-frame chunks, conc {n} per GPU"
+VOC1_METRIC = "vocoder xRT (audio-s/s), one-shot 10 s utterances, conc {n} per GPU"
 VOC_CHUNK, VOC_ONESHOT_FRAMES, VOC_FRAME_S = 16, 250, 0.04
 
 
@@ -1094,14 +1095,13 @@ def voc_conv_flops(cfg, T: int, n: int) -> list[float]:
     return out
 
 
-def run_voc(args, rank, world, oneshot: bool):
+def run_voc(args, rank, world, oneshot: bool, n: int = 64):
     from nanovllm_dots_b200 import synthetic as syn
     from nanovllm_dots_b200.vocoder import B200Vocoder
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     cfg = syn.VOC_BASE
-    n = 64
     w = syn.make_voc_weights(cfg, seed=1)
     W = VOC_CHUNK + cfg.lookahead + _voc_left(cfg)
     F = VOC_ONESHOT_FRAMES if oneshot else VOC_CHUNK
@@ -1231,12 +1231,12 @@ def run_voc(args, rank, world, oneshot: bool):
                "sample": f"{sample}: this build's restatement of the reference AudioVAE "
                          f"(oracle/voc_oracle.py), fp32 torch on the host, {secs:.2f} s"}
     if rank == 0:
-        line = {"metric": VOC1_METRIC if oneshot else VOC_METRIC,
+        line = {"metric": (VOC1_METRIC if oneshot else VOC_METRIC).format(n=n),
                 "value": round(audio_s / (ms / 1000), 2), "unit": "audio-s/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32/tf32",
                 "data": "synthetic (seeded random-init vocoder of the VOC_BASE shape, N(0,1) latents)",
-                "config": {"workload": "voc1" if oneshot else "voc", "requests_per_gpu": n,
+                "config": {"workload": args.workload, "requests_per_gpu": n,
                            "frames_per_request": F, "decoded_frames": T, "hop": cfg.hop,
                            "initial_channels": cfg.initial_channels,
                            "upsample_rates": list(cfg.upsample_rates),
@@ -1306,6 +1306,8 @@ def main():
             run_engine(args, rank, world)
         elif args.workload in ("voc", "voc1"):
             run_voc(args, rank, world, oneshot=args.workload == "voc1")
+        elif args.workload == "vocprof":
+            run_voc(args, rank, world, oneshot=False, n=16)
         else:
             run_b200(args, rank, world)
     finally:
