@@ -505,29 +505,46 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
 constexpr int VA_R = 32;
 constexpr int VA_WARPS = 4;
 
+// rows must be a multiple of VA_R (every decoder tensor has a multiple of 128
+// frames), so each thread's 32 outputs are all in range.
+template <bool kRound>
 __global__ void __launch_bounds__(32 * VA_WARPS, 4)
     voc_act_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int cp,
-                   const float* __restrict__ prm, int round_out) {
+                   const float* __restrict__ prm) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
   const int m0 = (blockIdx.y * VA_WARPS + warp) * VA_R;
-  const size_t base = static_cast<size_t>(blockIdx.z) * rows * cp + c;
-  // parameters (constant) before the dependency wait
+  // parameters (constant) before the dependency wait; the filters as float4s
   const float a = __ldg(prm + c), ib = __ldg(prm + cp + c);
   float fu[12], fd[12];
+  {
+    const float4* u4 = reinterpret_cast<const float4*>(prm + 2 * cp + static_cast<size_t>(c) * 12);
+    const float4* d4 = reinterpret_cast<const float4*>(prm + 14 * cp + static_cast<size_t>(c) * 12);
 #pragma unroll
-  for (int j = 0; j < 12; ++j) {
-    fu[j] = __ldg(prm + 2 * cp + static_cast<size_t>(c) * 12 + j);
-    fd[j] = __ldg(prm + 14 * cp + static_cast<size_t>(c) * 12 + j);
+    for (int q = 0; q < 3; ++q) {
+      const float4 uu = __ldg(u4 + q), dd = __ldg(d4 + q);
+      fu[4 * q] = uu.x; fu[4 * q + 1] = uu.y; fu[4 * q + 2] = uu.z; fu[4 * q + 3] = uu.w;
+      fd[4 * q] = dd.x; fd[4 * q + 1] = dd.y; fd[4 * q + 2] = dd.z; fd[4 * q + 3] = dd.w;
+    }
   }
   pdl_wait();
   pdl_trigger();
   if (m0 >= rows) return;
+  const float* ip = in + static_cast<size_t>(blockIdx.z) * rows * cp + c;
   float x[VA_R + 11];  // x[i] = in[m0 - 11 + i]
+  if (m0 >= 11) {
+    const float* p0 = ip + static_cast<size_t>(m0 - 11) * cp;
 #pragma unroll
-  for (int i = 0; i < VA_R + 11; ++i) {
-    const int m = m0 - 11 + i;
-    x[i] = (m >= 0 && m < rows) ? in[base + static_cast<size_t>(m) * cp] : 0.0f;
+    for (int i = 0; i < VA_R + 11; ++i) {
+      x[i] = *p0;
+      p0 += cp;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VA_R + 11; ++i) {
+      const int m = m0 - 11 + i;
+      x[i] = m >= 0 ? ip[static_cast<size_t>(m) * cp] : 0.0f;
+    }
   }
   // y[i] = act(u[2 m0 - 11 + i]); q = 2 m0 - 11 + i = 2 mm + ph with
   // ph = (i + 1) & 1, and x[mm] is window entry (i - 11 - ph) / 2 + 11.  Each
@@ -552,18 +569,18 @@ __global__ void __launch_bounds__(32 * VA_WARPS, 4)
 #pragma unroll
     for (int i = 0; i < 11; ++i) y[i] = y[11];
   }
+  float* op = out + static_cast<size_t>(blockIdx.z) * rows * cp + c + static_cast<size_t>(m0) * cp;
 #pragma unroll
   for (int k = 0; k < VA_R; ++k) {
     if (k > 0) {
       y[2 * k + 10] = act(2 * k + 10);
       y[2 * k + 11] = act(2 * k + 11);
     }
-    if (m0 + k < rows) {
-      float o = 0.0f;
+    float o = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 12; ++j) o += fd[j] * y[2 * k + j];
-      out[base + static_cast<size_t>(m0 + k) * cp] = round_out ? round_tf32(o) : o;
-    }
+    for (int j = 0; j < 12; ++j) o += fd[j] * y[2 * k + j];
+    *op = kRound ? round_tf32(o) : o;
+    op += cp;
   }
 }
 

@@ -299,8 +299,10 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
 cudaError_t voc_act(const float* in, float* out, int n, int rows, int cp, const float* prm,
                     int round_out, cudaStream_t s) {
   const int per_block = VA_R * VA_WARPS;
-  return launch_pdl(voc_act_kernel, dim3(cp / 32, (rows + per_block - 1) / per_block, n),
-                    dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm, round_out);
+  const dim3 grid(cp / 32, (rows + per_block - 1) / per_block, n);
+  if (round_out)
+    return launch_pdl(voc_act_kernel<true>, grid, dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm);
+  return launch_pdl(voc_act_kernel<false>, grid, dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm);
 }
 
 cudaError_t voc_linear(const float* X, int ldx, const float* W, const float* b, float* Y, int ldy,
