@@ -8,7 +8,9 @@ shot), ``init_stream_state``, ``stream_step`` and ``stream_flush`` (strict
 streaming), plus ``hop_size`` and ``sample_rate``.  Assigning one to
 ``engine.dots.vocoder`` (``install_vocoder``) routes the engine's
 ``vocode``/``_vocode_stream_step``/``_vocode_flush`` (``engine.py:825-852``)
-through the CUDA path.  The batched forms, ``decode_batch`` and
+through the CUDA path, and replaces ``step_stream`` with
+``batched_step_stream``, which gives the step's vocoder work to the batched
+calls.  The batched forms, ``decode_batch`` and
 ``stream_step_many``/``stream_flush_many``, serve every request of a tick in
 one call: the reference runs one request at a time.
 
@@ -399,8 +401,91 @@ class B200Vocoder:
             pass
 
 
-def install_vocoder(engine, voc: B200Vocoder) -> None:
+@torch.no_grad()
+def batched_step_stream(engine, *, vocode: bool = True) -> list:
+    """``DotsBatchEngine.step_stream`` (``engine.py:855-893``) with the vocoder
+    work of the step batched: every streaming request's pending patches in one
+    ``stream_step_many`` call per round (usually one round: one patch per
+    request per step), every finished stream in one ``stream_flush_many``, every
+    finished one-shot request in one ``decode_batch``, and the audio read back
+    in one copy.  Events, their order and the per-request bookkeeping
+    (``vocoded``, lazy stream state, the silent chunks of ``vocode=False``) are
+    the reference's; each request's audio is what its own per-request calls
+    would give (requests are decoded independently)."""
+    hop = engine.dots.hop_size * engine.core.latent_patch_size
+    seqs = engine.step()
+    if not seqs and not engine.scheduler.is_finished():
+        raise RuntimeError("scheduler made no progress with pending requests "
+                           "(KV exhaustion / preemption livelock).")
+    voc = engine.dots.vocoder
+    pieces: dict[int, list] = {}
+    if vocode:
+        work = []
+        for i, seq in enumerate(seqs):
+            st = seq.custom_payload
+            if st.stream and st.vocoded < len(st.latents):
+                if st.vocoder_state is None:
+                    st.vocoder_state = engine.dots._init_vocoder_stream_state()
+                work.append((i, st))
+                pieces[i] = []
+        r = 0
+        while True:
+            batch = [(i, st) for i, st in work if st.vocoded + r < len(st.latents)]
+            if not batch:
+                break
+            lat = torch.cat([st.latents[st.vocoded + r] for _, st in batch], dim=0)
+            outs = voc.stream_step_many([st.vocoder_state for _, st in batch], lat)
+            for (i, _), o in zip(batch, outs):
+                pieces[i].append(o)
+            r += 1
+    flush = [(i, seq.custom_payload) for i, seq in enumerate(seqs)
+             if seq.custom_payload.stream and seq.stoped and seq.custom_payload.vocoder_state is not None]
+    finals = dict(zip((i for i, _ in flush),
+                      voc.stream_flush_many([st.vocoder_state for _, st in flush]))) if flush else {}
+    oneshot = [(i, seq.custom_payload) for i, seq in enumerate(seqs)
+               if vocode and not seq.custom_payload.stream and seq.stoped and seq.custom_payload.latents]
+    wavs = dict(zip((i for i, _ in oneshot),
+                    voc.decode_batch([torch.cat(st.latents, dim=1)[0] for _, st in oneshot]))) if oneshot else {}
+    # one device -> host copy of every piece of audio of the step
+    dev = [t.reshape(-1).float() for lst in pieces.values() for t in lst]
+    dev += [t.reshape(-1).float() for t in finals.values()] + [t.reshape(-1).float() for t in wavs.values()]
+    host = iter(torch.cat(dev).cpu().split([t.numel() for t in dev])) if dev else iter(())
+    host_pieces = {i: [next(host) for _ in lst] for i, lst in pieces.items()}
+    host_finals = {i: next(host) for i in finals}
+    host_wavs = {i: next(host) for i in wavs}
+    events: list = []
+    for i, seq in enumerate(seqs):
+        st = seq.custom_payload
+        if st.stream:
+            k = 0
+            while st.vocoded < len(st.latents):
+                chunk = host_pieces[i][k] if vocode else torch.zeros(hop)
+                k += 1
+                st.vocoded += 1
+                if chunk.numel():
+                    events.append((seq.seq_id, "audio", chunk))
+            if seq.stoped:
+                final = host_finals.get(i, torch.zeros(0))
+                if final.numel():
+                    events.append((seq.seq_id, "audio", final))
+                events.append((seq.seq_id, "done", None))
+        elif seq.stoped:
+            if vocode:
+                wav = host_wavs.get(i, torch.zeros(0))
+            else:
+                wav = torch.zeros(hop * len(st.latents))
+            if wav.numel():
+                events.append((seq.seq_id, "audio", wav))
+            events.append((seq.seq_id, "done", None))
+    return events
+
+
+def install_vocoder(engine, voc: B200Vocoder, batch_streams: bool = True) -> None:
     """Route the engine's vocoder calls (``engine.py:825-852`` through
-    ``DotsModel``, ``native/model.py:204-218``) to ``voc``."""
+    ``DotsModel``, ``native/model.py:204-218``) to ``voc``; with
+    ``batch_streams`` the engine's ``step_stream`` also batches the step's
+    vocoder work across requests (``batched_step_stream``)."""
     engine.dots.vocoder = voc
     engine.dots.hop_size = voc.hop_size
+    if batch_streams:
+        engine.step_stream = lambda *, vocode=True: batched_step_stream(engine, vocode=vocode)

@@ -152,3 +152,44 @@ def test_full_shape_against_oracle():
         voc.check_errors()
     finally:
         voc.close()
+
+
+def test_batched_step_stream_with_real_vocoder(small):
+    """The engine's batched ``step_stream`` (``vocoder.batched_step_stream``)
+    over the real vocoder: two streams and one one-shot request, audio equal to
+    the per-request AudioVAE-style calls (the same kernels, so equal to rounding
+    of the batch size: same tolerance as above)."""
+    from types import SimpleNamespace
+    from nanovllm_dots_b200.vocoder import batched_step_stream
+    cfg = syn.VOC_SMALL
+    ps = 8
+    lat = syn.make_voc_latents(3, 3 * ps, seed=21, cfg=cfg)
+    dots = SimpleNamespace(vocoder=small, hop_size=small.hop_size,
+                           _init_vocoder_stream_state=lambda: small.init_stream_state(1, ps))
+    mk = lambda sid, stream: SimpleNamespace(
+        seq_id=sid, stoped=False, custom_payload=SimpleNamespace(stream=stream, latents=[], vocoded=0,
+                                                                 vocoder_state=None))
+    seqs = [mk("s0", True), mk("s1", True), mk("o2", False)]
+    steps = iter(range(3))
+
+    def step():
+        k = next(steps)
+        for i, s in enumerate(seqs):
+            s.custom_payload.latents.append(lat[i:i + 1, k * ps:(k + 1) * ps])
+            s.stoped = k == 2
+        return seqs
+
+    engine = SimpleNamespace(dots=dots, core=SimpleNamespace(latent_patch_size=ps), step=step,
+                             scheduler=SimpleNamespace(is_finished=lambda: False))
+    audio = {s.seq_id: [] for s in seqs}
+    for _ in range(3):
+        for sid, kind, x in batched_step_stream(engine):
+            if kind == "audio":
+                audio[sid].append(x)
+    for i in range(2):
+        st = small.init_stream_state(1, ps)
+        ref = [small.stream_step(lat[i:i + 1, k * ps:(k + 1) * ps].transpose(1, 2), st)[0, 0] for k in range(3)]
+        ref.append(small.stream_flush(st)[0, 0])
+        ref = torch.cat([r for r in ref if r.numel()])
+        check(torch.cat(audio[f"s{i}"]), ref.cpu().numpy(), f"batched step_stream s{i}")
+    check(torch.cat(audio["o2"]), small.decode_batch([lat[2]])[0].cpu().numpy(), "batched step_stream one-shot")
