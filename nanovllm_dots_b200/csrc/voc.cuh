@@ -99,10 +99,11 @@ struct VcPre {
   float4 r[8], o[8];
 };
 
-DFM_DEV void voc_conv_prefetch(const VcArgs& p, int b, int f, int n0, VcPre& pre) {
+DFM_DEV void voc_conv_prefetch(const VcArgs& p, int b, int f, int n0, VcPre& pre,
+                               bool res = true) {
   const size_t at = static_cast<size_t>(b) * p.out_b + static_cast<size_t>(f) * p.out_ld + n0;
   if (f * p.u + n0 / p.cp_out >= p.out_rows) return;
-  if (p.res) {
+  if (res && p.res) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) pre.r[j] = reinterpret_cast<const float4*>(p.res + at)[j];
   }
@@ -115,9 +116,11 @@ DFM_DEV void voc_conv_prefetch(const VcArgs& p, int b, int f, int n0, VcPre& pre
 // The conv epilogue of one thread: frame f of request b, columns [n0, n0+BN)
 // of the accumulator at taddr (this warp's TMEM lanes):
 //   v = acc + bias (+ residual);  out = v, or (out + v) [/ div]
+// ebuf (optional): this tile's residual in shared memory, BN/32 boxes of 128
+// rows x 128 bytes with the 128-byte swizzle (row `row` of the tile).
 template <int BN>
 DFM_DEV void voc_conv_epilogue(const VcArgs& p, uint32_t taddr, int b, int f, int n0,
-                               const VcPre& pre) {
+                               const VcPre& pre, const uint8_t* ebuf = nullptr, int row = 0) {
   const size_t rowoff = static_cast<size_t>(b) * p.out_b + static_cast<size_t>(f) * p.out_ld;
 #pragma unroll 1
   for (int c = 0; c < BN; c += 32) {
@@ -137,7 +140,14 @@ DFM_DEV void voc_conv_epilogue(const VcArgs& p, uint32_t taddr, int b, int f, in
       v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
     }
     float4* o4 = reinterpret_cast<float4*>(p.out + rowoff + col);
-    if (p.res) {
+    if (ebuf) {
+      const uint8_t* er = ebuf + (c / 32) * (VC_BM * 128) + row * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 x = *reinterpret_cast<const float4*>(er + ((j ^ (row & 7)) << 4));
+        v[4 * j] += x.x; v[4 * j + 1] += x.y; v[4 * j + 2] += x.z; v[4 * j + 3] += x.w;
+      }
+    } else if (p.res) {
       const float4* r4 = reinterpret_cast<const float4*>(p.res + rowoff + col);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -322,13 +332,14 @@ constexpr int VH_HALO = 64;
 constexpr int VH_ROWS = VC_BM + VH_HALO;   // frames staged per A tile
 constexpr int VH_BOX = 64;                 // frames per TMA box
 
-template <int BN, int SA, int SB>
+template <int BN, int SA, int SB, int SE = 0>
 struct VhShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "MMA N");
   static constexpr int A_BYTES = VH_ROWS * VC_BK * 4;  // 24 KB
   static constexpr int B_BYTES = BN * VC_BK * 4;
+  static constexpr int E_BYTES = VC_BM * BN * 4;        // one tile's residual
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms");
-  static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + 1024 + 512;
+  static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + SE * E_BYTES + 1024 + 512;
   static_assert(SMEM <= 232448, "shared memory per CTA");
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 256;
 };
@@ -337,29 +348,40 @@ struct VhShape {
 // 1024-byte-aligned tile with the base-offset field left 0: the MMA applies
 // the swizzle to the address bits, as TMA wrote it (a start shifted by r
 // rows reads rows r, r+1, ... of the tile; checked by the parity tests).
-
-template <int BN, int SA, int SB>
+//
+// SE > 0: the producer also loads each tile's residual rows (tmR, boxes of
+// 32 channels x 128 frames) into SE shared-memory buffers while the mainloop
+// runs, and the epilogue reads them there instead of from global memory.
+// Tiles are ordered N fastest, so the N tiles of one M tile run on
+// neighbouring CTAs at the same time and share its A rows in L2.
+template <int BN, int SA, int SB, int SE>
 __global__ void __launch_bounds__(VC_THREADS, 2)
     voc_conv_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                         VcArgs p, uint32_t* err) {
-  using S = VhShape<BN, SA, SB>;
+                         const __grid_constant__ CUtensorMap tmR, VcArgs p, uint32_t* err) {
+  using S = VhShape<BN, SA, SB, SE>;
+  constexpr int SEN = SE > 0 ? SE : 1;  // residual buffers (1: none, never used)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + SA * S::A_BYTES;
-  uint64_t* a_full = reinterpret_cast<uint64_t*>(smem + SA * S::A_BYTES + SB * S::B_BYTES);
+  uint8_t* sE = sB + SB * S::B_BYTES;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(sE + SE * S::E_BYTES);
   uint64_t* a_empty = a_full + SA;
   uint64_t* b_full = a_empty + SA;
   uint64_t* b_empty = b_full + SB;
   uint64_t* tm_full = b_empty + SB;  // [2]
   uint64_t* tm_empty = tm_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 2);
+  uint64_t* e_full = tm_empty + 2;   // [SE]
+  uint64_t* e_empty = e_full + SEN;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(e_empty + SEN);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = p.tiles_m * (p.N / BN);
+  const int tiles_n = p.N / BN;
+  const int total = p.tiles_m * tiles_n;
   const int nbox = (VC_BM + (p.taps - 1) * p.dil + VH_BOX - 1) / VH_BOX;
+  const bool eres = SE > 0 && p.res != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
@@ -374,10 +396,15 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
       mbar_init(&tm_full[b], 1);
       mbar_init(&tm_empty[b], 4);
     }
+    for (int e = 0; e < SE; ++e) {
+      mbar_init(&e_full[e], 1);
+      mbar_init(&e_empty[e], 4);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch(&tmA);
     tma_prefetch(&tmW);
+    if (SE > 0) tma_prefetch(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
@@ -392,12 +419,19 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
   if (warp == 0) {
     if (lane == 0) {
       pdl_wait();
-      int ga = 0, gb = 0;
+      int ga = 0, gb = 0, u = 0;
       bool ok = true;
 #pragma unroll 1
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        const int m = t % p.tiles_m, n0 = (t / p.tiles_m) * BN;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++u) {
+        const int m = t / tiles_n, n0 = (t - m * tiles_n) * BN;
         const int b = m / p.tiles_t, f0 = (m - b * p.tiles_t) * VC_BM;
+        if (eres) {
+          const int eb = u % SEN;
+          if (u >= SEN && !mbar_wait(&e_empty[eb], ((u / SEN) & 1) ^ 1, abort_flag, err)) break;
+          mbar_arrive_expect_tx(&e_full[eb], S::E_BYTES);
+          for (int c = 0; c < BN / 32; ++c)
+            tma_load_3d(sE + eb * S::E_BYTES + c * VC_BM * 128, &tmR, &e_full[eb], n0 + 32 * c, f0, b);
+        }
 #pragma unroll 1
         for (int cb = 0; ok && cb < p.nkb_c; ++cb, ++ga) {
           const int sa = ga % SA;
@@ -469,19 +503,29 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
 #pragma unroll 1
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++u) {
       const int buf = u & 1;
-      const int m = t % p.tiles_m, n0 = (t / p.tiles_m) * BN;
+      const int m = t / tiles_n, n0 = (t - m * tiles_n) * BN;
       const int b = m / p.tiles_t;
-      const int f = (m - b * p.tiles_t) * VC_BM + q * 32 + lane;
+      const int row = q * 32 + lane;
+      const int f = (m - b * p.tiles_t) * VC_BM + row;
       VcPre pre;
-      voc_conv_prefetch(p, b, f, n0, pre);
-      const bool ready =
-          __all_sync(0xffffffffu, mbar_wait(&tm_full[buf], (u >> 1) & 1, abort_flag, err));
-      if (!ready) break;
+      voc_conv_prefetch(p, b, f, n0, pre, !eres);
+      bool ready = mbar_wait(&tm_full[buf], (u >> 1) & 1, abort_flag, err);
+      const uint8_t* ebuf = nullptr;
+      if (eres) {
+        const int eb = u % SEN;
+        ready = mbar_wait(&e_full[eb], (u / SEN) & 1, abort_flag, err) && ready;
+        ebuf = sE + eb * S::E_BYTES;
+      }
+      if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      voc_conv_epilogue<BN>(p, tmem + buf * BN + (static_cast<uint32_t>(q * 32) << 16), b, f, n0, pre);
+      voc_conv_epilogue<BN>(p, tmem + buf * BN + (static_cast<uint32_t>(q * 32) << 16), b, f, n0, pre,
+                            ebuf, row);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tm_empty[buf]);
+      if (lane == 0) {
+        mbar_arrive(&tm_empty[buf]);
+        if (eres) mbar_arrive(&e_empty[u % SEN]);
+      }
     }
   }
   tc_fence_before();

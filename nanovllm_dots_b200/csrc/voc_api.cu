@@ -46,6 +46,8 @@ struct VocHandle {
   CUtensorMap m_xin[DVOC_MAX_STAGES];
   CUtensorMap m_act[DVOC_MAX_STAGES];
   CUtensorMap m_act_h[DVOC_MAX_STAGES];  // 64-frame boxes (halo kernel)
+  CUtensorMap m_u[DVOC_MAX_STAGES];      // residual sources of the resblock convs
+  CUtensorMap m_h[DVOC_MAX_STAGES];
 };
 
 int voc_validate(const DvocConfig& c) {
@@ -235,18 +237,18 @@ cudaError_t voc_conv_launch(const CUtensorMap& a, const CUtensorMap& w, const Vc
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, p, err);
 }
 
-template <int BN, int SA, int SB>
-cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const VcArgs& p,
-                            uint32_t* err, cudaStream_t s) {
+template <int BN, int SA, int SB, int SE = 0>
+cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& res,
+                            const VcArgs& p, uint32_t* err, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
-  auto fn = voc_conv_halo_kernel<BN, SA, SB>;
-  constexpr int smem = VhShape<BN, SA, SB>::SMEM;
+  auto fn = voc_conv_halo_kernel<BN, SA, SB, SE>;
+  constexpr int smem = VhShape<BN, SA, SB, SE>::SMEM;
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
   const int tiles = p.tiles_m * (p.N / BN);
   const int ctas = voc_ctas_per_sm(smem) * sm_count();
   const int grid = tiles < ctas ? tiles : ctas;
-  return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, p, err);
+  return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, res, p, err);
 }
 
 // Narrow convolutions whose taps span at most VH_HALO frames run on the halo
@@ -255,12 +257,18 @@ bool voc_halo(const VocConv& v) {
   return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.N <= 192 && v.u == 1;
 }
 
-int voc_halo_bn(int N) { return N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : N % 64 == 0 ? 64 : 32; }
+// Tiles of the narrow convolutions: one tile of N = 32 or 64, else 96/128
+// columns.  At N = 32 the residual is staged by TMA in two buffers (two CTAs
+// per SM still fit); at 64 a single buffer measured slower than the direct
+// loads, which the wider tiles keep.
+int voc_halo_bn(int N) {
+  return N == 32 ? 32 : N == 64 ? 64 : N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : 32;
+}
 
 cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& amap, int n,
                      int rows_in, float* out, long long out_b, int out_rows, const float* res,
                      int accum, float div, uint32_t* err, cudaStream_t s,
-                     const CUtensorMap* halo_map = nullptr) {
+                     const CUtensorMap* halo_map = nullptr, const CUtensorMap* res_map = nullptr) {
   VcArgs p;
   p.tiles_t = rows_in / VC_BM;
   p.tiles_m = n * p.tiles_t;
@@ -281,10 +289,12 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
   p.div = div;
   if (halo_map && voc_halo(v)) {
     switch (voc_halo_bn(v.N)) {
-      case 128: return voc_halo_launch<128, 2, 3>(*halo_map, v.wmap, p, err, s);
-      case 96: return voc_halo_launch<96, 2, 4>(*halo_map, v.wmap, p, err, s);
-      case 64: return voc_halo_launch<64, 2, 6>(*halo_map, v.wmap, p, err, s);
-      default: return voc_halo_launch<32, 2, 6>(*halo_map, v.wmap, p, err, s);
+      case 128: return voc_halo_launch<128, 2, 3>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 96: return voc_halo_launch<96, 2, 4>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 64: return voc_halo_launch<64, 2, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
+      default:
+        if (res && res_map) return voc_halo_launch<32, 2, 6, 2>(*halo_map, v.wmap, *res_map, p, err, s);
+        return voc_halo_launch<32, 2, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
     }
   }
   switch (voc_bn(v.N)) {
@@ -474,7 +484,9 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
       const int cin_p = i ? vpad(h->ch[i - 1]) : c0p, rows_in = i ? r.cap[i - 1] : r.cpre;
       ok = voc_map_act(&h->m_xin[i], P(h->o_x), n, rows_in, cin_p) &&
            voc_map_act(&h->m_act[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i])) &&
-           voc_map_act(&h->m_act_h[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i]), VH_BOX);
+           voc_map_act(&h->m_act_h[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i]), VH_BOX) &&
+           voc_map_act(&h->m_u[i], P(h->o_u), n, r.cap[i], vpad(h->ch[i])) &&
+           voc_map_act(&h->m_h[i], P(h->o_h), n, r.cap[i], vpad(h->ch[i]));
     }
     if (!ok) {
       h->plan_ws = nullptr;
@@ -569,7 +581,7 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
         }
         if (pick(li))
           VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, dst, ob, rows, src, acc, dv, err, s,
-                       &h->m_act_h[i]));
+                       &h->m_act_h[i], l == 0 ? &h->m_u[i] : &h->m_h[i]));
         ++li;
       }
     }
