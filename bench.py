@@ -52,11 +52,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg2",
-                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "pe", "llmattn",
+                    choices=["cfg1", "cfg2", "cfg3", "cfg4", "prof", "gemm64", "gemm64fp8", "pe", "llmattn",
                              "llmdecode", "engine", "voc", "voc1", "vocprof"],
                     help="cfg3 = cfg2 on the FP8 path (QKV and fc1 on e4m3 operands); "
                          "prof = the first 16 requests of cfg2 (a few GB, for ncu captures); "
                          "gemm64 = 64 requests with empty prefixes (config-2 GEMM shapes, tiny pool); "
+                         "gemm64fp8 = gemm64 on the FP8 path; "
                          "pe = the patch encoder (the step after the FM head): one batched "
                          "decode_patch for 64 requests with cfg2's history lengths; "
                          "llmattn = the LLM backbone's paged decode attention (one layer, 64 "
@@ -128,7 +129,7 @@ def placement(pp: list[int], world: int):
 def workload_batch(name: str, rank: int, world: int = 1):
     """(this rank's RequestBatch, placement summary)."""
     from nanovllm_dots_b200 import synthetic as syn
-    if name == "gemm64":
+    if name in ("gemm64", "gemm64fp8"):
         return syn.make_batch(64, [0] * 64, seed=2), None
     if name == "prof":
         full = syn.config_batch("cfg2")
@@ -314,7 +315,7 @@ def run_b200(args, rank, world):
     max_pages = max(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows)
     num_pages = sum(math.ceil((p + 2 * cfg.stride) / cfg.page_rows) for p in b.prefix_rows) + 8
     weights = syn.make_weights(cfg)
-    precision = "fp8" if args.workload == "cfg3" else "bf16"
+    precision = "fp8" if args.workload in ("cfg3", "gemm64fp8") else "bf16"
     head = B200FMHead(weights, cfg, num_pages=num_pages, max_pages_per_req=max_pages,
                       max_requests=n, device=dev, precision=precision)
     # cached prefixes: N(0, 0.5^2) K/V drawn on the device straight into the pool
@@ -532,7 +533,7 @@ def run_b200(args, rank, world):
                            "nfe": cfg.nfe, "layers": cfg.layers, "page_rows": cfg.page_rows,
                            "l2": "inputs larger than L2 (K/V pool and weights), no flush",
                            "parallelism": f"request-sharded x{world}",
-                           "precision": "fp8" if args.workload == "cfg3" else "bf16",
+                           "precision": precision,
                            "per_rank_ms": per_rank_ms,
                            "rank_ms_max_over_mean": round(max(per_rank_ms)
                                                           / (sum(per_rank_ms) / world), 4),
