@@ -16,13 +16,16 @@
  * stage a causal transposed conv and the mean of its AMP resblocks of
  * anti-aliased SnakeBeta activations and causal dilated convs,
  * activation_post, conv_post, tanh) with every convolution on the tcgen05
- * tensor cores (tf32 operands, fp32 accumulation) and everything else in fp32.
+ * tensor cores (fp16 operands: the 10-bit mantissa of tf32, the precision of
+ * PyTorch's cuDNN convolutions on this GPU; fp32 accumulation) and everything
+ * else in fp32.
  *
  * The same shared library (libdfm.so) exports these symbols next to the FM
  * head's (dfm.h); status codes and device error bits are dfm.h's.
  *
  * Conventions: as in dfm.h.  Every pointer inside the structs is a DEVICE
- * pointer; all tensors are fp32; activations are frames-first ([request]
+ * pointer; tensors are fp32 except the packed conv weights (fp16);
+ * activations are frames-first ([request]
  * [frame][channel]); the caller owns every buffer.  The library owns only the
  * handle and its TMA descriptors; dvoc_decode allocates nothing and does not
  * synchronise.  Channel counts are padded to multiples of 32 inside the
@@ -71,7 +74,7 @@ typedef struct DvocConfig {
  *           resblock convs: W[co][ci][j] at [co][j][ci]) or u*Cp(Cout) (the
  *           transposed conv of a stage: tap 0 reads frame t-1 with
  *           W[ci][co][r+u], tap 1 frame t with W[ci][co][r], at row r*Cp(Cout)+co),
- *           values rounded to tf32; order: conv_pre, then per stage its
+ *           as fp16 (round to nearest); order: conv_pre, then per stage its
  *           transposed conv and per resblock per layer convs1.l, convs2.l
  *           (type 1) or convs.l (type 2);
  *   conv_b: per conv [N] (a transposed conv's bias repeated per phase r);
@@ -92,7 +95,7 @@ typedef struct DvocWeights {
   const float* lstm_b_hh;   /* [mi_layers][16L] */
   const float* mi_out_w;    /* dec_mi_layer.2 [L][4L] */
   const float* mi_out_b;    /* [L] */
-  const float* conv_w;      /* packed decoder convs (above) */
+  const void* conv_w;       /* packed decoder convs (above), fp16 */
   const float* conv_b;      /* packed decoder conv biases */
   const float* act;         /* packed alias-free activations */
   const float* post_conv_w; /* conv_post [7][Cp(C_last)]: weight[0][c][j] at [j][c] */

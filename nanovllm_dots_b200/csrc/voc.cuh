@@ -1,12 +1,16 @@
 // Kernels of the vocoder's decode path (BigVGAN AudioVAE decoder,
 // ``nanovllm_dots/models/dots/native/vocoder/bigvgan.py``).
 //
-// Activations are fp32, frames-first: [request][frame][Cp] with Cp the
-// channel count padded to a multiple of 32 (one 128-byte swizzle row).
+// Activations are frames-first: [request][frame][Cp] with Cp the channel
+// count padded to a multiple of 32.  Convolution operands (the activation
+// outputs, the decoder input, each stage's output copy, the weights) are fp16
+// (10-bit mantissa, as tf32) in 64-byte swizzle rows of 32 channels; the
+// residual stream, conv outputs and accumulators are fp32.
 //
 //   voc_conv_kernel   every convolution of the decoder as an implicit GEMM on
-//                     the tcgen05 tensor cores (kind::tf32, fp32 accumulate in
-//                     TMEM): out[t] = sum over taps j of x[t + off0 + j*dil] W_j;
+//                     the tcgen05 tensor cores (kind::f16 with fp16 operands,
+//                     fp32 accumulate in TMEM): out[t] = sum over taps j of
+//                     x[t + off0 + j*dil] W_j;
 //                     tap j's A tile is a TMA box at the shifted frame
 //                     coordinate, frames outside the request read as zeros;
 //                     the epilogue adds bias, the residual, and the stage's
@@ -20,26 +24,30 @@
 //                     chunk, or one-shot latents masked to each length
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace dfm {
 
-// ---------------------------------------------------------------- tcgen05 tf32
-// Instruction descriptor of kind::tf32: tf32 A/B (format 2), fp32 D, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
+// ---------------------------------------------------------------- tcgen05 f16
+// Instruction descriptor of kind::f16 with fp16 A/B (format 0), fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-DFM_DEV void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                       uint32_t accumulate) {
-  const uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
-          d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
+// Shared-memory descriptor of a K-major tile with the 64-byte swizzle: rows
+// of 32 fp16 (64 bytes), 8-row atoms of 512 bytes packed densely.  As with
+// the 128-byte swizzle, the start may sit at any row of a 512-byte-aligned
+// tile (the swizzle applies to the address bits, as TMA wrote them).
+DFM_DEV uint64_t umma_desc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                      // leading byte offset (unused)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;               // stride byte offset: 8 rows
+  d |= static_cast<uint64_t>(1) << 46;                      // descriptor version (sm100)
+  d |= static_cast<uint64_t>(4) << 61;                      // layout: 64-byte swizzle
+  return d;
 }
 
 DFM_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
@@ -50,23 +58,17 @@ DFM_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x
       : "memory");
 }
 
-// Round to the nearest tf32 value (ties away from zero), kept in an fp32 container.
-DFM_DEV float round_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
 // ---------------------------------------------------------------- conv
 constexpr int VC_BM = 128;
-constexpr int VC_BK = 32;  // fp32 elements per 128-byte swizzle row
+constexpr int VC_BK = 32;    // channels (fp16) per 64-byte swizzle row
+constexpr int VC_ROWB = 64;  // bytes per row of an operand tile
 constexpr int VC_THREADS = 192;
 
 template <int BN, int STAGES>
 struct VcShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "MMA N");
-  static constexpr int A_BYTES = VC_BM * VC_BK * 4;  // 16 KB: 128 frames x 32 channels
-  static constexpr int B_BYTES = BN * VC_BK * 4;
+  static constexpr int A_BYTES = VC_BM * VC_ROWB;  // 8 KB: 128 frames x 32 channels
+  static constexpr int B_BYTES = BN * VC_ROWB;
   static_assert(B_BYTES % 1024 == 0, "swizzle atoms");
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
@@ -90,7 +92,13 @@ struct VcArgs {
   const float* res;   // residual with out's layout, or null
   int accum;          // 1: out += value (the stage's resblock sum)
   float div;          // then out /= div (1: none)
+  __half* out16;      // optional fp16 copy of out (same layout), the next conv's operand
 };
+
+DFM_DEV uint32_t pack_half(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 // Inputs of the conv epilogue that do not depend on the accumulator: the
 // first 32 columns of the thread's residual row and running sum, loaded
@@ -169,6 +177,13 @@ DFM_DEV void voc_conv_epilogue(const VcArgs& p, uint32_t taddr, int b, int f, in
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    if (p.out16) {
+      uint4* h4 = reinterpret_cast<uint4*>(p.out16 + rowoff + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        h4[j] = make_uint4(pack_half(v[8 * j], v[8 * j + 1]), pack_half(v[8 * j + 2], v[8 * j + 3]),
+                           pack_half(v[8 * j + 4], v[8 * j + 5]), pack_half(v[8 * j + 6], v[8 * j + 7]));
+    }
   }
 }
 
@@ -261,7 +276,7 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_tf32(VC_BM, BN);
+      constexpr uint32_t idesc = umma_idesc_f16(VC_BM, BN);
       int g = 0, u = 0;
       bool ok = true;
 #pragma unroll 1
@@ -282,8 +297,8 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
           const uint32_t a = smem_u32(sA + s * S::A_BYTES);
           const uint32_t bb = smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < VC_BK / 8; ++kk)  // K = 8 tf32 (32 bytes) per MMA
-            umma_tf32(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+          for (int kk = 0; kk < VC_BK / 16; ++kk)  // K = 16 fp16 (32 bytes) per MMA
+            umma_bf16(acc, umma_desc_sw64(a + kk * 32), umma_desc_sw64(bb + kk * 32), idesc,
                       (kb | kk) != 0);
           umma_commit(&empty[s]);
         }
@@ -335,19 +350,20 @@ constexpr int VH_BOX = 64;                 // frames per TMA box
 template <int BN, int SA, int SB, int SE = 0>
 struct VhShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "MMA N");
-  static constexpr int A_BYTES = VH_ROWS * VC_BK * 4;  // 24 KB
-  static constexpr int B_BYTES = BN * VC_BK * 4;
-  static constexpr int E_BYTES = VC_BM * BN * 4;        // one tile's residual
+  static constexpr int A_BYTES = VH_ROWS * VC_ROWB;  // 12 KB
+  static constexpr int B_BYTES = BN * VC_ROWB;
+  static constexpr int E_BYTES = VC_BM * BN * 4;      // one tile's fp32 residual (128-byte swizzle)
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms");
   static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + SE * E_BYTES + 1024 + 512;
   static_assert(SMEM <= 232448, "shared memory per CTA");
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 256;
 };
 
-// A K-major 128-byte-swizzle descriptor may start at any 128-byte row of a
-// 1024-byte-aligned tile with the base-offset field left 0: the MMA applies
-// the swizzle to the address bits, as TMA wrote it (a start shifted by r
-// rows reads rows r, r+1, ... of the tile; checked by the parity tests).
+// A row-shifted operand descriptor keeps the base-offset field 0: the MMA
+// applies the swizzle to the address bits, as TMA wrote them (a start
+// shifted by r rows reads rows r, r+1, ... of the tile; measured with the
+// 128-byte swizzle, where setting the field to the row phase failed parity,
+// and checked by the parity tests).
 //
 // SE > 0: the producer also loads each tile's residual rows (tmR, boxes of
 // 32 channels x 128 frames) into SE shared-memory buffers while the mainloop
@@ -439,9 +455,9 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&a_full[sa], nbox * VH_BOX * VC_BK * 4);
+          mbar_arrive_expect_tx(&a_full[sa], nbox * VH_BOX * VC_ROWB);
           for (int q = 0; q < nbox; ++q)
-            tma_load_3d(sA + sa * S::A_BYTES + q * VH_BOX * 128, &tmA, &a_full[sa], cb * VC_BK,
+            tma_load_3d(sA + sa * S::A_BYTES + q * VH_BOX * VC_ROWB, &tmA, &a_full[sa], cb * VC_BK,
                         f0 + p.off0 + q * VH_BOX, b);
 #pragma unroll 1
           for (int j = 0; j < p.taps; ++j, ++gb) {
@@ -458,7 +474,7 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_tf32(VC_BM, BN);
+      constexpr uint32_t idesc = umma_idesc_f16(VC_BM, BN);
       int ga = 0, gb = 0, u = 0;
       bool ok = true;
 #pragma unroll 1
@@ -483,11 +499,11 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
               break;
             }
             tc_fence_after();
-            const uint32_t a = a0 + static_cast<uint32_t>(j * p.dil) * 128u;
+            const uint32_t a = a0 + static_cast<uint32_t>(j * p.dil) * VC_ROWB;
             const uint32_t bb = smem_u32(sB + sb * S::B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < VC_BK / 8; ++kk)
-              umma_tf32(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+            for (int kk = 0; kk < VC_BK / 16; ++kk)
+              umma_bf16(acc, umma_desc_sw64(a + kk * 32), umma_desc_sw64(bb + kk * 32), idesc,
                         (cb | j | kk) != 0);
             umma_commit(&b_empty[sb]);
           }
@@ -551,9 +567,10 @@ constexpr int VA_WARPS = 4;
 
 // rows must be a multiple of VA_R (every decoder tensor has a multiple of 128
 // frames), so each thread's 32 outputs are all in range.
-template <bool kRound>
+// kHalf: the output is a convolution operand (fp16); else fp32 (activation_post).
+template <bool kHalf>
 __global__ void __launch_bounds__(32 * VA_WARPS, 4)
-    voc_act_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int cp,
+    voc_act_kernel(const float* __restrict__ in, void* __restrict__ out, int rows, int cp,
                    const float* __restrict__ prm) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
@@ -603,7 +620,7 @@ __global__ void __launch_bounds__(32 * VA_WARPS, 4)
     for (int qq = 0; qq < 6; ++qq) s += x[xi - qq] * fu[2 * qq + ph];
     const float uu = 2.0f * s;
     // the MUFU sine: absolute error ~1e-6 for the arguments seen here, far
-    // below the tf32 rounding of the convolutions that consume the output
+    // below the fp16 rounding of the convolution operands
     const float sn = __sinf(uu * a);
     return uu + ib * (sn * sn);
   };
@@ -613,7 +630,9 @@ __global__ void __launch_bounds__(32 * VA_WARPS, 4)
 #pragma unroll
     for (int i = 0; i < 11; ++i) y[i] = y[11];
   }
-  float* op = out + static_cast<size_t>(blockIdx.z) * rows * cp + c + static_cast<size_t>(m0) * cp;
+  const size_t o0 = static_cast<size_t>(blockIdx.z) * rows * cp + c + static_cast<size_t>(m0) * cp;
+  __half* oh = static_cast<__half*>(out) + o0;
+  float* of = static_cast<float*>(out) + o0;
 #pragma unroll
   for (int k = 0; k < VA_R; ++k) {
     if (k > 0) {
@@ -623,8 +642,13 @@ __global__ void __launch_bounds__(32 * VA_WARPS, 4)
     float o = 0.0f;
 #pragma unroll
     for (int j = 0; j < 12; ++j) o += fd[j] * y[2 * k + j];
-    *op = kRound ? round_tf32(o) : o;
-    op += cp;
+    if constexpr (kHalf) {
+      *oh = __float2half_rn(o);
+      oh += cp;
+    } else {
+      *of = o;
+      of += cp;
+    }
   }
 }
 
@@ -791,11 +815,12 @@ __global__ void __launch_bounds__(32 * VS_J)
 //               frames (valid clamped to [0, W]); when the frames overflow W
 //               the window keeps the last W; zeros past the valid frames;
 //   window == 0: z[b][p] for p < len[b] (F when len is null), zeros elsewhere.
-// Rows past W (or the length) and channels past L are zero.
+// Rows past W (or the length) and channels past L are zero.  dst is the
+// fp16 operand of conv_pre; dst32 (optional) an fp32 copy for the window store.
 __global__ void voc_pack_kernel(const float* __restrict__ z, const float* __restrict__ win,
                                 const int* __restrict__ valid, const int* __restrict__ len,
-                                float* __restrict__ dst, int n, int F, int W, int L, int lp,
-                                int rows) {
+                                __half* __restrict__ dst, float* __restrict__ dst32, int n, int F,
+                                int W, int L, int lp, int rows) {
   pdl_wait();
   pdl_trigger();
   const size_t total = static_cast<size_t>(n) * rows * lp;
@@ -821,11 +846,13 @@ __global__ void voc_pack_kernel(const float* __restrict__ z, const float* __rest
         if (p < lb && p < F) v = z[(static_cast<size_t>(b) * F + p) * L + c];
       }
     }
-    dst[i] = v;
+    dst[i] = __float2half_rn(v);
+    if (dst32) dst32[i] = v;
   }
 }
 
-// windows[b][p][c] = dinput[b][p][c] for p < W, c < L (the new stream windows).
+// windows[b][p][c] = dinput[b][p][c] for p < W, c < L (the new stream windows,
+// from the fp32 copy of the decoder input).
 __global__ void voc_window_store_kernel(const float* __restrict__ din, float* __restrict__ win,
                                         int n, int W, int L, int lp, int rows) {
   pdl_wait();

@@ -38,7 +38,7 @@ struct VocHandle {
   size_t conv_floats = 0, bias_floats = 0, act_floats = 0;
   // workspace (maxima)
   size_t o_err = 0, o_p = 0, o_s = 0, o_gx = 0, o_y0 = 0, o_y1 = 0, o_z = 0, o_h0 = 0, o_h1 = 0,
-         o_din = 0, o_x = 0, o_u = 0, o_h = 0, o_a = 0, o_c1 = 0, total = 0;
+         o_din = 0, o_din32 = 0, o_x = 0, o_x16 = 0, o_u = 0, o_h = 0, o_a = 0, o_c1 = 0, total = 0;
   // tensor maps of the last call's shape
   const void* plan_ws = nullptr;
   int plan_n = -1, plan_t = -1;
@@ -175,8 +175,10 @@ void voc_layout(VocHandle& h) {
   h.o_z = take(nb * F * h.L);
   h.o_h0 = take(nb * h.Hm);
   h.o_h1 = take(nb * h.Hm);
-  h.o_din = take(nb * static_cast<size_t>(r.cpre) * h.Lp);
+  h.o_din = take(nb * static_cast<size_t>(r.cpre) * h.Lp / 2);  // fp16
+  h.o_din32 = take(nb * static_cast<size_t>(r.cpre) * h.Lp);
   h.o_x = take(big);
+  h.o_x16 = take(big / 2);                                        // fp16 copy of X
   h.o_u = take(big);
   h.o_h = take(big);
   h.o_a = take(big);
@@ -184,31 +186,48 @@ void voc_layout(VocHandle& h) {
   h.total = o;
 }
 
-// 3-D fp32 activation [n][rows][cp], box {32 channels, box_rows frames, 1}.
+// 3-D fp16 operand [n][rows][cp], box {32 channels, box_rows frames, 1},
+// 64-byte swizzle (one 64-byte row per frame).
 bool voc_map_act(CUtensorMap* m, const void* base, int n, int rows, int cp, int box_rows = VC_BM) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cp), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(n)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cp) * 2,
+                           static_cast<cuuint64_t>(cp) * rows * 2};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3-D fp32 tensor [n][rows][cp] (a residual source), box {32 channels, 128
+// frames, 1}, 128-byte swizzle.
+bool voc_map_f32(CUtensorMap* m, const void* base, int n, int rows, int cp) {
   auto fn = encode_fn();
   if (!fn || !base) return false;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(cp), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(n)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(cp) * 4,
                            static_cast<cuuint64_t>(cp) * rows * 4};
-  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(VC_BM), 1};
   cuuint32_t es[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 2-D fp32 weight [N][K], box {32, bn}.
+// 2-D fp16 weight [N][K], box {32, bn}, 64-byte swizzle.
 bool voc_map_w(CUtensorMap* m, const void* base, int N, int K, int bn) {
   auto fn = encode_fn();
   if (!fn || !base) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 4};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
   cuuint32_t box[2] = {32, static_cast<cuuint32_t>(bn)};
   cuuint32_t es[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -268,7 +287,8 @@ int voc_halo_bn(int N) {
 cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& amap, int n,
                      int rows_in, float* out, long long out_b, int out_rows, const float* res,
                      int accum, float div, uint32_t* err, cudaStream_t s,
-                     const CUtensorMap* halo_map = nullptr, const CUtensorMap* res_map = nullptr) {
+                     const CUtensorMap* halo_map = nullptr, const CUtensorMap* res_map = nullptr,
+                     __half* out16 = nullptr) {
   VcArgs p;
   p.tiles_t = rows_in / VC_BM;
   p.tiles_m = n * p.tiles_t;
@@ -287,30 +307,32 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
   p.res = res;
   p.accum = accum;
   p.div = div;
+  p.out16 = out16;
   if (halo_map && voc_halo(v)) {
     switch (voc_halo_bn(v.N)) {
-      case 128: return voc_halo_launch<128, 2, 3>(*halo_map, v.wmap, *halo_map, p, err, s);
-      case 96: return voc_halo_launch<96, 2, 4>(*halo_map, v.wmap, *halo_map, p, err, s);
-      case 64: return voc_halo_launch<64, 2, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 128: return voc_halo_launch<128, 3, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 96: return voc_halo_launch<96, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 64: return voc_halo_launch<64, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
       default:
-        if (res && res_map) return voc_halo_launch<32, 2, 6, 2>(*halo_map, v.wmap, *res_map, p, err, s);
-        return voc_halo_launch<32, 2, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
+        if (res && res_map) return voc_halo_launch<32, 3, 8, 2>(*halo_map, v.wmap, *res_map, p, err, s);
+        return voc_halo_launch<32, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
     }
   }
   switch (voc_bn(v.N)) {
-    case 256: return voc_conv_launch<256, 4>(amap, v.wmap, p, err, s);
+    case 256: return voc_conv_launch<256, 8>(amap, v.wmap, p, err, s);
     case 128: return voc_conv_launch<128, 6>(amap, v.wmap, p, err, s);
     case 96: return voc_conv_launch<96, 7>(amap, v.wmap, p, err, s);
-    case 64: return voc_conv_launch<64, 4>(amap, v.wmap, p, err, s);
-    default: return voc_conv_launch<32, 4>(amap, v.wmap, p, err, s);
+    case 64: return voc_conv_launch<64, 8>(amap, v.wmap, p, err, s);
+    default: return voc_conv_launch<32, 8>(amap, v.wmap, p, err, s);
   }
 }
 
-cudaError_t voc_act(const float* in, float* out, int n, int rows, int cp, const float* prm,
-                    int round_out, cudaStream_t s) {
+// half_out: the output is a convolution operand (fp16); else fp32.
+cudaError_t voc_act(const float* in, void* out, int n, int rows, int cp, const float* prm,
+                    int half_out, cudaStream_t s) {
   const int per_block = VA_R * VA_WARPS;
   const dim3 grid(cp / 32, (rows + per_block - 1) / per_block, n);
-  if (round_out)
+  if (half_out)
     return launch_pdl(voc_act_kernel<true>, grid, dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm);
   return launch_pdl(voc_act_kernel<false>, grid, dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm);
 }
@@ -424,7 +446,7 @@ int dvoc_create(const DvocConfig* cfg, const DvocWeights* w, void** out) {
   voc_layout(*h);
   for (VocConv& v : h->convs) {
     const int bn = voc_halo(v) ? voc_halo_bn(v.N) : voc_bn(v.N);
-    if (!voc_map_w(&v.wmap, w->conv_w + v.w_off, v.N, v.taps * v.cin_p, bn)) {
+    if (!voc_map_w(&v.wmap, static_cast<const __half*>(w->conv_w) + v.w_off, v.N, v.taps * v.cin_p, bn)) {
       delete h;
       return DFM_ERR_CUDA;
     }
@@ -482,11 +504,11 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
     bool ok = voc_map_act(&h->m_din, P(h->o_din), n, r.cpre, h->Lp);
     for (int i = 0; ok && i < h->ns; ++i) {
       const int cin_p = i ? vpad(h->ch[i - 1]) : c0p, rows_in = i ? r.cap[i - 1] : r.cpre;
-      ok = voc_map_act(&h->m_xin[i], P(h->o_x), n, rows_in, cin_p) &&
+      ok = voc_map_act(&h->m_xin[i], P(h->o_x16), n, rows_in, cin_p) &&
            voc_map_act(&h->m_act[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i])) &&
            voc_map_act(&h->m_act_h[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i]), VH_BOX) &&
-           voc_map_act(&h->m_u[i], P(h->o_u), n, r.cap[i], vpad(h->ch[i])) &&
-           voc_map_act(&h->m_h[i], P(h->o_h), n, r.cap[i], vpad(h->ch[i]));
+           voc_map_f32(&h->m_u[i], P(h->o_u), n, r.cap[i], vpad(h->ch[i])) &&
+           voc_map_f32(&h->m_h[i], P(h->o_h), n, r.cap[i], vpad(h->ch[i]));
     }
     if (!ok) {
       h->plan_ws = nullptr;
@@ -539,17 +561,19 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
   if (all)
     VCK(launch_pdl(voc_pack_kernel, dim3(grid_for(din)), dim3(256), 0, s,
                  static_cast<const float*>(P(h->o_z)), static_cast<const float*>(b->windows),
-                 b->valid, b->lengths, P(h->o_din), n, F, W, L, h->Lp, r.cpre));
+                 b->valid, b->lengths, reinterpret_cast<__half*>(P(h->o_din)),
+                 streaming ? P(h->o_din32) : nullptr, n, F, W, L, h->Lp, r.cpre));
   if (all && streaming && F > 0)
     VCK(launch_pdl(voc_window_store_kernel, dim3(grid_for(static_cast<size_t>(n) * W * L)), dim3(256),
-                   0, s, static_cast<const float*>(P(h->o_din)), b->windows, n, W, L, h->Lp, r.cpre));
+                   0, s, static_cast<const float*>(P(h->o_din32)), b->windows, n, W, L, h->Lp, r.cpre));
   // ---- decoder
   size_t li = 0, ai = 0;
   auto pick = [&](size_t i) { return all || static_cast<int>(i) == only; };
+  __half* X16 = reinterpret_cast<__half*>(P(h->o_x16));  // fp16 copy of each stage's output
   const VocConv& pre = h->convs[li];
   if (pick(li++))
     VCK(voc_conv(*h, pre, h->m_din, n, r.cpre, P(h->o_x), static_cast<long long>(r.cpre) * c0p,
-               r.cpre, nullptr, 0, 1.0f, err, s));
+               r.cpre, nullptr, 0, 1.0f, err, s, nullptr, nullptr, X16));
   for (int i = 0; i < h->ns; ++i) {
     const int cp = vpad(h->ch[i]), rows = r.cap[i], rows_in = i ? r.cap[i - 1] : r.cpre;
     const long long ob = static_cast<long long>(rows) * cp;
@@ -579,9 +603,11 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
           if (all) VCK(voc_act(C1, A, n, rows, cp, h->w.act + h->act_off[ai], 1, s));
           ++ai;
         }
+        // the stage's final sum also feeds the next stage's transposed conv (fp16)
+        __half* d16 = last && j == h->nk - 1 && i + 1 < h->ns ? X16 : nullptr;
         if (pick(li))
           VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, dst, ob, rows, src, acc, dv, err, s,
-                       &h->m_act_h[i], l == 0 ? &h->m_u[i] : &h->m_h[i]));
+                       &h->m_act_h[i], l == 0 ? &h->m_u[i] : &h->m_h[i], d16));
         ++li;
       }
     }

@@ -16,8 +16,8 @@ one call: the reference runs one request at a time.
 
 Every call goes through the C ABI (``include/dvoc.h``): the front (post_proj,
 Linear, LSTM, Linear) in fp32, every decoder convolution on the tcgen05 tensor
-cores with tf32 operands and fp32 accumulation, activations, conv_post and
-tanh in fp32.  There is no other path: without the library every call raises.
+cores with fp16 operands (the 10-bit mantissa of tf32) and fp32 accumulation,
+activations, conv_post and tanh in fp32.  There is no other path: without the library every call raises.
 """
 from __future__ import annotations
 
@@ -53,14 +53,6 @@ def dvoc_config(cfg: VocConfig, max_batch: int, max_frames: int) -> _lib.DvocCon
     c.max_batch = max_batch
     c.max_frames = max_frames
     return c
-
-
-def round_tf32(x: torch.Tensor) -> torch.Tensor:
-    """fp32 -> nearest tf32 value (10 mantissa bits, ties away from zero), as
-    ``cvt.rna.tf32.f32`` rounds; returned in fp32."""
-    b = x.float().contiguous().view(torch.int32)
-    b = (b + 0x1000) & ~0x1FFF
-    return b.view(torch.float32)
 
 
 def _act_block(sd: dict, name: str, c: int, activation: str) -> torch.Tensor:
@@ -142,7 +134,7 @@ def pack_voc_weights(sd: dict, cfg: VocConfig, device=None) -> dict[str, torch.T
                                        cfg.stage_channels(i), cfg.activation))
     cl = cfg.stage_channels(len(cfg.upsample_rates) - 1)
     acts.append(_act_block(sd, "decoder.activation_post", cl, cfg.activation))
-    w["conv_w"] = round_tf32(torch.cat(convs))
+    w["conv_w"] = torch.cat(convs).to(torch.float16)
     w["conv_b"] = torch.cat(biases)
     w["act"] = torch.cat(acts)
     pw = torch.zeros(7, _pad32(cl))

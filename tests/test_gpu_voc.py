@@ -2,10 +2,10 @@
 (``tests/golden/voc_golden.npz``, made by ``make_golden_voc.py``) and against
 the oracle at the full synthetic shape.
 
-Tolerance: the decoder's convolutions run with tf32 operands (10-bit
-mantissa, the precision PyTorch's cuDNN convolutions use on this GPU by
-default) and fp32 accumulation; the front, the activations and conv_post run
-in fp32.  Audio in [-1, 1] must match the fp32 reference with max-abs <= 2e-2
+Tolerance: the decoder's convolutions run with fp16 operands (a 10-bit
+mantissa: the precision of the tf32 operands PyTorch's cuDNN convolutions use
+on this GPU by default) and fp32 accumulation; the front, the activations and
+conv_post run in fp32.  Audio in [-1, 1] must match the fp32 reference with max-abs <= 2e-2
 and a signal-to-error ratio >= 40 dB per request (per emitted piece for
 streams)."""
 from __future__ import annotations
