@@ -81,7 +81,9 @@ typedef struct DvocConfig {
  *   act:    per activation [Cp] exp(alpha), [Cp] 1/(exp(beta)+1e-9),
  *           [Cp][12] upsampling filter, [Cp][12] downsampling filter; order:
  *           per stage per resblock activations 0..5 (type 1) or 0..1 (type 2),
- *           then activation_post.
+ *           then activation_post.  The resblock activations' filters are the
+ *           reference's fixed buffers, the same for every channel: only
+ *           channel 0's are read; activation_post's are per channel.
  * Padded channels hold zeros.  dvoc_conv_floats / dvoc_bias_floats /
  * dvoc_act_floats give the packed sizes. */
 typedef struct DvocWeights {

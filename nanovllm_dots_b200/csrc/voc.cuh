@@ -84,8 +84,8 @@ struct VcArgs {
   int nkb_c;          // 32-channel blocks of the input per tap
   int taps, off0, dil;  // tap j reads frame t + off0 + j * dil
   const float* bias;  // [N]
-  float* out;
-  long long out_b;    // floats between requests of out (and of res)
+  float* out;         // fp32 output, or null (out16 only)
+  long long out_b;    // elements between requests of out (and of res, out16)
   int out_ld;         // floats between frames t of out
   int u, cp_out;      // column col of frame t is output frame t*u + col / cp_out ...
   int out_rows;       // ... stored only below out_rows
@@ -175,8 +175,10 @@ DFM_DEV void voc_conv_epilogue(const VcArgs& p, uint32_t taddr, int b, int f, in
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = v[j] / p.div;
     }
+    if (p.out) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
     if (p.out16) {
       uint4* h4 = reinterpret_cast<uint4*>(p.out16 + rowoff + col);
 #pragma unroll
@@ -649,6 +651,91 @@ __global__ void __launch_bounds__(32 * VA_WARPS, 4)
       *of = o;
       of += cp;
     }
+  }
+}
+
+// The resblock activations (fixed filters, the same for every channel:
+// ``Activation1d(..., fixed_filter=True)``, ``bigvgan.py:339-346``), two
+// channels per thread on paired fp32 arithmetic (FFMA2): lanes 0-15 take the
+// 32-channel block's channel pairs for frames [m0, m0+16), lanes 16-31 the
+// same pairs for [m0+16, m0+32).  Same arithmetic as voc_act_kernel, with
+// the upsampling filter pre-scaled by 2 (exact).  Input fp32 (the residual
+// stream) or fp16 (a conv1 output); output fp16 (the next conv's operand).
+constexpr int VB_R = 16;
+
+DFM_DEV float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+DFM_DEV float2 ld2(const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p)); }
+
+template <typename Tin>
+__global__ void __launch_bounds__(32 * VA_WARPS, 4)
+    voc_act2_kernel(const Tin* __restrict__ in, __half* __restrict__ out, int rows, int cp,
+                    const float* __restrict__ prm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + 2 * (lane & 15);
+  const int m0 = ((blockIdx.y * VA_WARPS + warp) * 2 + (lane >> 4)) * VB_R;
+  const float2 a = ld2(prm + c), ib = ld2(prm + cp + c);
+  float fu[12], fd[12];
+  {
+    const float4* u4 = reinterpret_cast<const float4*>(prm + 2 * cp);   // channel 0's filters
+    const float4* d4 = reinterpret_cast<const float4*>(prm + 14 * cp);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const float4 uu = __ldg(u4 + q), dd = __ldg(d4 + q);
+      fu[4 * q] = 2.0f * uu.x; fu[4 * q + 1] = 2.0f * uu.y; fu[4 * q + 2] = 2.0f * uu.z; fu[4 * q + 3] = 2.0f * uu.w;
+      fd[4 * q] = dd.x; fd[4 * q + 1] = dd.y; fd[4 * q + 2] = dd.z; fd[4 * q + 3] = dd.w;
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (m0 >= rows) return;
+  const Tin* ip = in + static_cast<size_t>(blockIdx.z) * rows * cp + c;
+  float2 x[VB_R + 11];  // x[i] = in[m0 - 11 + i]
+  if (m0 >= 11) {
+    const Tin* p0 = ip + static_cast<size_t>(m0 - 11) * cp;
+#pragma unroll
+    for (int i = 0; i < VB_R + 11; ++i) {
+      x[i] = ld2(p0);
+      p0 += cp;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VB_R + 11; ++i) {
+      const int m = m0 - 11 + i;
+      x[i] = m >= 0 ? ld2(ip + static_cast<size_t>(m) * cp) : make_float2(0.f, 0.f);
+    }
+  }
+  float2 y[2 * VB_R + 11];
+  auto act = [&](int i) {
+    const int ph = (i + 1) & 1;
+    const int xi = (i - 11 - ph) / 2 + 11;
+    float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int qq = 0; qq < 6; ++qq) {
+      const float f = fu[2 * qq + ph];
+      s = __ffma2_rn(x[xi - qq], make_float2(f, f), s);
+    }
+    const float2 t = __fmul2_rn(s, a);
+    const float2 sn = make_float2(__sinf(t.x), __sinf(t.y));
+    return __ffma2_rn(ib, __fmul2_rn(sn, sn), s);
+  };
+#pragma unroll
+  for (int i = 0; i < 12; ++i) y[i] = act(i);
+  if (m0 == 0) {
+#pragma unroll
+    for (int i = 0; i < 11; ++i) y[i] = y[11];
+  }
+  __half* op = out + static_cast<size_t>(blockIdx.z) * rows * cp + c + static_cast<size_t>(m0) * cp;
+#pragma unroll
+  for (int k = 0; k < VB_R; ++k) {
+    if (k > 0) {
+      y[2 * k + 10] = act(2 * k + 10);
+      y[2 * k + 11] = act(2 * k + 11);
+    }
+    float2 o = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 12; ++j) o = __ffma2_rn(make_float2(fd[j], fd[j]), y[2 * k + j], o);
+    *reinterpret_cast<__half2*>(op) = __floats2half2_rn(o.x, o.y);
+    op += cp;
   }
 }
 

@@ -337,6 +337,15 @@ cudaError_t voc_act(const float* in, void* out, int n, int rows, int cp, const f
   return launch_pdl(voc_act_kernel<false>, grid, dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm);
 }
 
+// The resblock activations (shared fixed filters): fp32 or fp16 input, fp16 output.
+template <typename Tin>
+cudaError_t voc_act2(const Tin* in, __half* out, int n, int rows, int cp, const float* prm,
+                     cudaStream_t s) {
+  const int per_block = 2 * VB_R * VA_WARPS;
+  const dim3 grid(cp / 32, (rows + per_block - 1) / per_block, n);
+  return launch_pdl(voc_act2_kernel<Tin>, grid, dim3(32 * VA_WARPS), 0, s, in, out, rows, cp, prm);
+}
+
 cudaError_t voc_linear(const float* X, int ldx, const float* W, const float* b, float* Y, int ldy,
                        int M, int N, int K, cudaStream_t s) {
   return launch_pdl(voc_linear_kernel, dim3((N + VL_T - 1) / VL_T, (M + VL_T - 1) / VL_T),
@@ -580,8 +589,8 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
     float* X = P(h->o_x);
     float* U = P(h->o_u);
     float* H = P(h->o_h);
-    float* A = P(h->o_a);
-    float* C1 = P(h->o_c1);
+    __half* A = reinterpret_cast<__half*>(P(h->o_a));     // activation outputs (conv operands)
+    __half* C1 = reinterpret_cast<__half*>(P(h->o_c1));   // conv1 outputs (read only by act2)
     if (pick(li))
       VCK(voc_conv(*h, h->convs[li], h->m_xin[i], n, rows_in, U, ob, rows, nullptr, 0, 1.0f, err, s));
     ++li;
@@ -593,14 +602,14 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
         float* dst = last ? X : H;
         const int acc = last && j > 0;
         const float dv = last && j == h->nk - 1 ? static_cast<float>(h->nk) : 1.0f;
-        if (all) VCK(voc_act(src, A, n, rows, cp, h->w.act + h->act_off[ai], 1, s));
+        if (all) VCK(voc_act2(src, A, n, rows, cp, h->w.act + h->act_off[ai], s));
         ++ai;
         if (c.resblock_type == 1) {
           if (pick(li))
-            VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, C1, ob, rows, nullptr, 0, 1.0f, err, s,
-                         &h->m_act_h[i]));
+            VCK(voc_conv(*h, h->convs[li], h->m_act[i], n, rows, nullptr, ob, rows, nullptr, 0, 1.0f,
+                         err, s, &h->m_act_h[i], nullptr, C1));
           ++li;
-          if (all) VCK(voc_act(C1, A, n, rows, cp, h->w.act + h->act_off[ai], 1, s));
+          if (all) VCK(voc_act2(static_cast<const __half*>(C1), A, n, rows, cp, h->w.act + h->act_off[ai], s));
           ++ai;
         }
         // the stage's final sum also feeds the next stage's transposed conv (fp16)
