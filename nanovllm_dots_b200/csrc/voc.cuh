@@ -841,8 +841,10 @@ __global__ void __launch_bounds__(256)
 //   gates = (W_hh h_prev + b_hh) + gx[b][f]   (gx = W_ih x + b_ih)
 //   c = sig(f) c + sig(i) tanh(g);  h = sig(o) tanh(c)
 // h goes to h_next and to y[b][f] (plus skip[b][f] at the last layer).  A
-// block takes 8 hidden units (one per warp) for 32 requests (one per lane);
-// the 32 requests' h_prev sit transposed in shared memory.
+// block takes 8 hidden units (one per warp) for 32 requests (one per lane):
+// the 32 requests' h_prev sit transposed in shared memory, and the block's
+// 32 rows of W_hh (4 gates x 8 units) are staged there too, so the inner
+// loop reads only shared memory.
 constexpr int VS_J = 8;
 
 __global__ void __launch_bounds__(32 * VS_J)
@@ -850,10 +852,19 @@ __global__ void __launch_bounds__(32 * VS_J)
                          const float* __restrict__ bhh, const float* __restrict__ h_prev,
                          float* __restrict__ h_next, float* __restrict__ c, float* __restrict__ y,
                          const float* __restrict__ skip, int n, int Hm) {
-  extern __shared__ float hs[];  // [Hm][33]
+  extern __shared__ float sm[];
+  float* hs = sm;                  // [Hm][33]: h_prev of the block's 32 requests, transposed
+  float* ws = sm + Hm * 33;        // [4][VS_J][Hm]: this block's rows of W_hh
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int j = blockIdx.x * VS_J + warp;
+  const int j0 = blockIdx.x * VS_J, j = j0 + warp;
   const int b0 = blockIdx.y * 32, b = b0 + lane;
+  // the weights are constant: stage them before the dependency wait
+  for (int i = threadIdx.x * 4; i < 4 * VS_J * Hm; i += 32 * VS_J * 4) {
+    const int row = i / Hm, k = i - row * Hm;          // row = g * VS_J + u
+    const int g = row / VS_J, u = row - g * VS_J;
+    *reinterpret_cast<float4*>(ws + i) =
+        __ldg(reinterpret_cast<const float4*>(whh + (static_cast<size_t>(g) * Hm + j0 + u) * Hm + k));
+  }
   pdl_wait();
   pdl_trigger();
 #pragma unroll 1
@@ -863,16 +874,14 @@ __global__ void __launch_bounds__(32 * VS_J)
   }
   __syncthreads();
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const float* w0 = whh + static_cast<size_t>(j) * Hm;
-  const size_t gs = static_cast<size_t>(Hm) * Hm;
-#pragma unroll 1
+#pragma unroll 4
   for (int k = 0; k < Hm; k += 4) {
     float hv[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) hv[e] = hs[(k + e) * 33 + lane];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const float4 wv = __ldg(reinterpret_cast<const float4*>(w0 + g * gs + k));
+      const float4 wv = *reinterpret_cast<const float4*>(ws + (g * VS_J + warp) * Hm + k);
       acc[g] += wv.x * hv[0];
       acc[g] += wv.y * hv[1];
       acc[g] += wv.z * hv[2];

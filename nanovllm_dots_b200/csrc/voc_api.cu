@@ -9,8 +9,10 @@
 
 namespace {
 
-constexpr int kVocMaxLatent = 384;
-constexpr int kVocLstmSmem = 4 * kVocMaxLatent * 33 * 4;
+// The LSTM step keeps 32 requests' h (4L floats each, transposed) and its
+// block's 32 rows of W_hh (4L floats each) in shared memory.
+constexpr int kVocMaxLatent = 192;
+constexpr int kVocLstmSmem = 4 * kVocMaxLatent * (33 + 4 * VS_J) * 4;
 
 int vpad(int c) { return (c + 31) / 32 * 32; }
 size_t valign(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -51,7 +53,6 @@ struct VocHandle {
 };
 
 int voc_validate(const DvocConfig& c) {
-  // the LSTM step keeps 32 requests' states (4L floats each) in shared memory
   if (c.latent_dim < 2 || c.latent_dim > kVocMaxLatent || c.latent_dim % 2) return DFM_ERR_UNSUPPORTED;
   if (c.num_stages < 1 || c.num_stages > DVOC_MAX_STAGES) return DFM_ERR_UNSUPPORTED;
   if (c.num_kernels < 1 || c.num_kernels > DVOC_MAX_KERNELS) return DFM_ERR_UNSUPPORTED;
@@ -544,7 +545,7 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
       float* y = P(l & 1 ? h->o_y1 : h->o_y0);
       VCK(voc_linear(in, Hm, h->w.lstm_w_ih + l * gsz, h->w.lstm_b_ih + static_cast<size_t>(l) * 4 * Hm,
                      P(h->o_gx), 4 * Hm, M, 4 * Hm, Hm, s));
-      const int smem = Hm * 33 * 4;
+      const int smem = Hm * (33 + 4 * VS_J) * 4;
       static std::atomic<uint64_t> attr_done{0};
       VCK(smem_attr_once(attr_done, voc_lstm_step_kernel, kVocLstmSmem));
       for (int f = 0; f < F; ++f) {
