@@ -349,16 +349,23 @@ constexpr int VH_HALO = 64;
 constexpr int VH_ROWS = VC_BM + VH_HALO;   // frames staged per A tile
 constexpr int VH_BOX = 64;                 // frames per TMA box
 
-template <int BN, int SA, int SB, int SE = 0>
+// MT: 128-frame accumulators per tile (a tile is MT x 128 frames; every
+// barrier round of (channel block, tap) feeds MT x 2 MMAs from one A tile and
+// one W tile).
+template <int BN, int SA, int SB, int SE = 0, int MT = 1>
 struct VhShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "MMA N");
-  static constexpr int A_BYTES = VH_ROWS * VC_ROWB;  // 12 KB
+  static_assert(MT == 1 || MT == 2, "accumulators per tile");
+  static constexpr int ROWS = MT * VC_BM + VH_HALO;           // frames staged per A tile
+  static constexpr int A_BYTES = ROWS * VC_ROWB;               // 12 KB (MT 1) or 20 KB (MT 2)
   static constexpr int B_BYTES = BN * VC_ROWB;
-  static constexpr int E_BYTES = VC_BM * BN * 4;      // one tile's fp32 residual (128-byte swizzle)
+  static constexpr int E_BYTES = MT * VC_BM * BN * 4;          // one tile's fp32 residual (128-byte swizzle)
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms");
   static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + SE * E_BYTES + 1024 + 512;
   static_assert(SMEM <= 232448, "shared memory per CTA");
-  static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 256;
+  static constexpr int ACC_COLS = 2 * MT * BN;                 // double-buffered accumulators
+  static constexpr uint32_t TMEM_COLS = ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
+                                        : ACC_COLS <= 256 ? 256 : 512;
 };
 
 // A row-shifted operand descriptor keeps the base-offset field 0: the MMA
@@ -372,11 +379,12 @@ struct VhShape {
 // runs, and the epilogue reads them there instead of from global memory.
 // Tiles are ordered N fastest, so the N tiles of one M tile run on
 // neighbouring CTAs at the same time and share its A rows in L2.
-template <int BN, int SA, int SB, int SE>
+template <int BN, int SA, int SB, int SE, int MT>
 __global__ void __launch_bounds__(VC_THREADS, 2)
     voc_conv_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                          const __grid_constant__ CUtensorMap tmR, VcArgs p, uint32_t* err) {
-  using S = VhShape<BN, SA, SB, SE>;
+  using S = VhShape<BN, SA, SB, SE, MT>;
+  constexpr int TM = MT * VC_BM;        // frames per tile
   constexpr int SEN = SE > 0 ? SE : 1;  // residual buffers (1: none, never used)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -398,7 +406,7 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = p.N / BN;
   const int total = p.tiles_m * tiles_n;
-  const int nbox = (VC_BM + (p.taps - 1) * p.dil + VH_BOX - 1) / VH_BOX;
+  const int nbox = (TM + (p.taps - 1) * p.dil + VH_BOX - 1) / VH_BOX;
   const bool eres = SE > 0 && p.res != nullptr;
 
   if (threadIdx.x == 0) {
@@ -442,13 +450,15 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
 #pragma unroll 1
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++u) {
         const int m = t / tiles_n, n0 = (t - m * tiles_n) * BN;
-        const int b = m / p.tiles_t, f0 = (m - b * p.tiles_t) * VC_BM;
+        const int b = m / p.tiles_t, f0 = (m - b * p.tiles_t) * TM;
         if (eres) {
           const int eb = u % SEN;
           if (u >= SEN && !mbar_wait(&e_empty[eb], ((u / SEN) & 1) ^ 1, abort_flag, err)) break;
           mbar_arrive_expect_tx(&e_full[eb], S::E_BYTES);
-          for (int c = 0; c < BN / 32; ++c)
-            tma_load_3d(sE + eb * S::E_BYTES + c * VC_BM * 128, &tmR, &e_full[eb], n0 + 32 * c, f0, b);
+          for (int mt = 0; mt < MT; ++mt)
+            for (int c = 0; c < BN / 32; ++c)
+              tma_load_3d(sE + eb * S::E_BYTES + (mt * (BN / 32) + c) * VC_BM * 128, &tmR, &e_full[eb],
+                          n0 + 32 * c, f0 + mt * VC_BM, b);
         }
 #pragma unroll 1
         for (int cb = 0; ok && cb < p.nkb_c; ++cb, ++ga) {
@@ -484,7 +494,7 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
         const int buf = u & 1;
         if (u >= 2 && !mbar_wait(&tm_empty[buf], ((u >> 1) & 1) ^ 1, abort_flag, err)) break;
         tc_fence_after();
-        const uint32_t acc = tmem + buf * BN;
+        const uint32_t acc = tmem + buf * MT * BN;
 #pragma unroll 1
         for (int cb = 0; ok && cb < p.nkb_c; ++cb, ++ga) {
           const int sa = ga % SA;
@@ -501,12 +511,15 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
               break;
             }
             tc_fence_after();
-            const uint32_t a = a0 + static_cast<uint32_t>(j * p.dil) * VC_ROWB;
             const uint32_t bb = smem_u32(sB + sb * S::B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < VC_BK / 16; ++kk)
-              umma_bf16(acc, umma_desc_sw64(a + kk * 32), umma_desc_sw64(bb + kk * 32), idesc,
-                        (cb | j | kk) != 0);
+            for (int mt = 0; mt < MT; ++mt) {
+              const uint32_t a = a0 + static_cast<uint32_t>(mt * VC_BM + j * p.dil) * VC_ROWB;
+#pragma unroll
+              for (int kk = 0; kk < VC_BK / 16; ++kk)
+                umma_bf16(acc + mt * BN, umma_desc_sw64(a + kk * 32), umma_desc_sw64(bb + kk * 32), idesc,
+                          (cb | j | kk) != 0);
+            }
             umma_commit(&b_empty[sb]);
           }
           if (ok) umma_commit(&a_empty[sa]);
@@ -523,10 +536,9 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
       const int buf = u & 1;
       const int m = t / tiles_n, n0 = (t - m * tiles_n) * BN;
       const int b = m / p.tiles_t;
-      const int row = q * 32 + lane;
-      const int f = (m - b * p.tiles_t) * VC_BM + row;
+      const int f0 = (m - b * p.tiles_t) * TM;
       VcPre pre;
-      voc_conv_prefetch(p, b, f, n0, pre, !eres);
+      voc_conv_prefetch(p, b, f0 + q * 32 + lane, n0, pre, !eres);
       bool ready = mbar_wait(&tm_full[buf], (u >> 1) & 1, abort_flag, err);
       const uint8_t* ebuf = nullptr;
       if (eres) {
@@ -536,8 +548,14 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
       }
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
-      voc_conv_epilogue<BN>(p, tmem + buf * BN + (static_cast<uint32_t>(q * 32) << 16), b, f, n0, pre,
-                            ebuf, row);
+#pragma unroll 1
+      for (int mt = 0; mt < MT; ++mt) {
+        const int row = q * 32 + lane;
+        if (mt > 0) voc_conv_prefetch(p, b, f0 + mt * VC_BM + row, n0, pre, !eres);
+        voc_conv_epilogue<BN>(p, tmem + (buf * MT + mt) * BN + (static_cast<uint32_t>(q * 32) << 16), b,
+                              f0 + mt * VC_BM + row, n0, pre,
+                              ebuf ? ebuf + mt * (BN / 32) * VC_BM * 128 : nullptr, row);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

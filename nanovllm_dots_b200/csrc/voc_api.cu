@@ -17,6 +17,7 @@ constexpr int kVocLstmSmem = 4 * kVocMaxLatent * (33 + 4 * VS_J) * 4;
 int vpad(int c) { return (c + 31) / 32 * 32; }
 size_t valign(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 int round128(long long x) { return static_cast<int>((x + 127) / 128 * 128); }
+int round256(long long x) { return static_cast<int>((x + 255) / 256 * 256); }
 
 // One convolution of the decoder as the conv kernel sees it.
 struct VocConv {
@@ -135,7 +136,7 @@ void voc_tables(VocHandle& h) {
 struct VocRows {
   int tpre, cpre;                 // conv_pre: T, rounded to 128
   long long t[DVOC_MAX_STAGES];   // valid frames after stage i
-  int cap[DVOC_MAX_STAGES];       // rounded to 128
+  int cap[DVOC_MAX_STAGES];       // rounded to 256
 };
 
 VocRows voc_rows(const VocHandle& h, int T) {
@@ -146,7 +147,7 @@ VocRows voc_rows(const VocHandle& h, int T) {
   for (int i = 0; i < h.ns; ++i) {
     t *= h.c.upsample_rates[i];
     r.t[i] = t;
-    r.cap[i] = round128(t);
+    r.cap[i] = round256(t);   // whole 256-frame tiles of the narrow convolutions
   }
   return r;
 }
@@ -240,8 +241,11 @@ int voc_bn(int N) {
   return 32;
 }
 
-// Conv CTAs that fit on one SM by shared memory (the kernels allow 2).
-int voc_ctas_per_sm(int smem) { return 2 * (smem + 1024) <= 233472 ? 2 : 1; }
+// Conv CTAs that fit on one SM by shared memory and TMEM (the kernels allow 2;
+// a CTA that holds more than half of the 512 TMEM columns runs alone).
+int voc_ctas_per_sm(int smem, uint32_t tmem_cols) {
+  return 2 * (smem + 1024) <= 233472 && tmem_cols <= 256 ? 2 : 1;
+}
 
 template <int BN, int ST>
 cudaError_t voc_conv_launch(const CUtensorMap& a, const CUtensorMap& w, const VcArgs& p,
@@ -252,21 +256,24 @@ cudaError_t voc_conv_launch(const CUtensorMap& a, const CUtensorMap& w, const Vc
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
   const int tiles = p.tiles_m * (p.N / BN);
-  const int ctas = voc_ctas_per_sm(smem) * sm_count();
+  const int ctas = voc_ctas_per_sm(smem, VcShape<BN, ST>::TMEM_COLS) * sm_count();
   const int grid = tiles < ctas ? tiles : ctas;
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, p, err);
 }
 
-template <int BN, int SA, int SB, int SE = 0>
+template <int BN, int SA, int SB, int SE = 0, int MT = 1>
 cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& res,
-                            const VcArgs& p, uint32_t* err, cudaStream_t s) {
+                            VcArgs p, uint32_t* err, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
-  auto fn = voc_conv_halo_kernel<BN, SA, SB, SE>;
-  constexpr int smem = VhShape<BN, SA, SB, SE>::SMEM;
+  auto fn = voc_conv_halo_kernel<BN, SA, SB, SE, MT>;
+  using S = VhShape<BN, SA, SB, SE, MT>;
+  constexpr int smem = S::SMEM;
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
+  p.tiles_t /= MT;                  // tiles of MT x 128 frames (rows are multiples of 256)
+  p.tiles_m /= MT;
   const int tiles = p.tiles_m * (p.N / BN);
-  const int ctas = voc_ctas_per_sm(smem) * sm_count();
+  const int ctas = voc_ctas_per_sm(smem, S::TMEM_COLS) * sm_count();
   const int grid = tiles < ctas ? tiles : ctas;
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, res, p, err);
 }
@@ -313,10 +320,11 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
     switch (voc_halo_bn(v.N)) {
       case 128: return voc_halo_launch<128, 3, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 96: return voc_halo_launch<96, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
-      case 64: return voc_halo_launch<64, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 64: return voc_halo_launch<64, 2, 8, 0, 2>(*halo_map, v.wmap, *halo_map, p, err, s);
       default:
-        if (res && res_map) return voc_halo_launch<32, 3, 8, 2>(*halo_map, v.wmap, *res_map, p, err, s);
-        return voc_halo_launch<32, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
+        if (res && res_map)
+          return voc_halo_launch<32, 2, 8, 1, 2>(*halo_map, v.wmap, *res_map, p, err, s);
+        return voc_halo_launch<32, 2, 8, 0, 2>(*halo_map, v.wmap, *halo_map, p, err, s);
     }
   }
   switch (voc_bn(v.N)) {
