@@ -352,7 +352,9 @@ constexpr int VH_BOX = 64;                 // frames per TMA box
 // MT: 128-frame accumulators per tile (a tile is MT x 128 frames; every
 // barrier round of (channel block, tap) feeds MT x 2 MMAs from one A tile and
 // one W tile).
-template <int BN, int SA, int SB, int SE = 0, int MT = 1>
+// NB: accumulator buffers (2: the next tile's MMAs overlap this tile's
+// epilogue; 1: they wait for it, which halves TMEM so two CTAs per SM fit).
+template <int BN, int SA, int SB, int SE = 0, int MT = 1, int NB = 2>
 struct VhShape {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "MMA N");
   static_assert(MT == 1 || MT == 2, "accumulators per tile");
@@ -363,7 +365,8 @@ struct VhShape {
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms");
   static constexpr int SMEM = SA * A_BYTES + SB * B_BYTES + SE * E_BYTES + 1024 + 512;
   static_assert(SMEM <= 232448, "shared memory per CTA");
-  static constexpr int ACC_COLS = 2 * MT * BN;                 // double-buffered accumulators
+  static_assert(NB == 1 || NB == 2, "accumulator buffers");
+  static constexpr int ACC_COLS = NB * MT * BN;
   static constexpr uint32_t TMEM_COLS = ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
                                         : ACC_COLS <= 256 ? 256 : 512;
 };
@@ -379,11 +382,11 @@ struct VhShape {
 // runs, and the epilogue reads them there instead of from global memory.
 // Tiles are ordered N fastest, so the N tiles of one M tile run on
 // neighbouring CTAs at the same time and share its A rows in L2.
-template <int BN, int SA, int SB, int SE, int MT>
+template <int BN, int SA, int SB, int SE, int MT, int NB>
 __global__ void __launch_bounds__(VC_THREADS, 2)
     voc_conv_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                          const __grid_constant__ CUtensorMap tmR, VcArgs p, uint32_t* err) {
-  using S = VhShape<BN, SA, SB, SE, MT>;
+  using S = VhShape<BN, SA, SB, SE, MT, NB>;
   constexpr int TM = MT * VC_BM;        // frames per tile
   constexpr int SEN = SE > 0 ? SE : 1;  // residual buffers (1: none, never used)
   extern __shared__ uint8_t smem_raw[];
@@ -491,8 +494,8 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
       bool ok = true;
 #pragma unroll 1
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++u) {
-        const int buf = u & 1;
-        if (u >= 2 && !mbar_wait(&tm_empty[buf], ((u >> 1) & 1) ^ 1, abort_flag, err)) break;
+        const int buf = u % NB;
+        if (u >= NB && !mbar_wait(&tm_empty[buf], ((u / NB) & 1) ^ 1, abort_flag, err)) break;
         tc_fence_after();
         const uint32_t acc = tmem + buf * MT * BN;
 #pragma unroll 1
@@ -533,13 +536,13 @@ __global__ void __launch_bounds__(VC_THREADS, 2)
     int u = 0;
 #pragma unroll 1
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++u) {
-      const int buf = u & 1;
+      const int buf = u % NB;
       const int m = t / tiles_n, n0 = (t - m * tiles_n) * BN;
       const int b = m / p.tiles_t;
       const int f0 = (m - b * p.tiles_t) * TM;
       VcPre pre;
       voc_conv_prefetch(p, b, f0 + q * 32 + lane, n0, pre, !eres);
-      bool ready = mbar_wait(&tm_full[buf], (u >> 1) & 1, abort_flag, err);
+      bool ready = mbar_wait(&tm_full[buf], (u / NB) & 1, abort_flag, err);
       const uint8_t* ebuf = nullptr;
       if (eres) {
         const int eb = u % SEN;

@@ -261,12 +261,12 @@ cudaError_t voc_conv_launch(const CUtensorMap& a, const CUtensorMap& w, const Vc
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, p, err);
 }
 
-template <int BN, int SA, int SB, int SE = 0, int MT = 1>
+template <int BN, int SA, int SB, int SE = 0, int MT = 1, int NB = 2>
 cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& res,
                             VcArgs p, uint32_t* err, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
-  auto fn = voc_conv_halo_kernel<BN, SA, SB, SE, MT>;
-  using S = VhShape<BN, SA, SB, SE, MT>;
+  auto fn = voc_conv_halo_kernel<BN, SA, SB, SE, MT, NB>;
+  using S = VhShape<BN, SA, SB, SE, MT, NB>;
   constexpr int smem = S::SMEM;
   cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
