@@ -278,10 +278,11 @@ cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const CU
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, res, p, err);
 }
 
-// Narrow convolutions whose taps span at most VH_HALO frames run on the halo
-// kernel (one A tile per channel block for all taps).
+// The resblock convolutions (causal, taps spanning at most VH_HALO frames)
+// run on the halo kernel: one A tile per channel block for all taps.  conv_pre
+// (centred) and the transposed convs stay on voc_conv_kernel.
 bool voc_halo(const VocConv& v) {
-  return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.N <= 192 && v.u == 1;
+  return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.u == 1 && v.off0 == -(v.taps - 1) * v.dil;
 }
 
 // Tiles of the narrow convolutions: one tile of N = 32 or 64, else 96/128
