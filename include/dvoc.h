@@ -132,9 +132,11 @@ typedef struct DvocBatch {
 } DvocBatch;
 
 /* Handle.  Validates the configuration (DFM_ERR_UNSUPPORTED outside the
- * supported family: causal decoder, resblock type 1 or 2, every stage at
- * least 1 channel) and encodes the weights' TMA descriptors; copies no
- * weights (they must outlive the handle). */
+ * supported family: causal decoder, latent_dim even and at most 192,
+ * resblock type 1 or 2, every stage at least 1 channel) and encodes the
+ * weights' TMA descriptors; copies no weights (they must outlive the handle).
+ * conv_w, conv_b, act and lstm_w_hh must be 16-byte aligned.  A handle serves
+ * one call at a time (it keeps the tensor maps of the last call's shape). */
 int dvoc_create(const DvocConfig* cfg, const DvocWeights* w, void** handle);
 int dvoc_destroy(void* handle);
 

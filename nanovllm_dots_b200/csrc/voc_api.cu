@@ -449,8 +449,12 @@ int dvoc_create(const DvocConfig* cfg, const DvocWeights* w, void** out) {
                        w->act, w->post_conv_w};
   for (const void* p : req)
     if (!p) return DFM_ERR_INVALID_ARG;
+  // TMA reads the weights and the kernels read biases and activation
+  // parameters as 16-byte vectors
   if ((reinterpret_cast<uintptr_t>(w->conv_w) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(w->conv_b) & 15) != 0)
+      (reinterpret_cast<uintptr_t>(w->conv_b) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(w->act) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(w->lstm_w_hh) & 15) != 0)
     return DFM_ERR_INVALID_ARG;
   if (!encode_fn()) return DFM_ERR_CUDA;
   VocHandle* h = new (std::nothrow) VocHandle();

@@ -201,7 +201,6 @@ class B200Vocoder:
             self._h = h
             self.ws = torch.zeros(L.dvoc_workspace_size(h), dtype=torch.uint8, device=self.device)
         self.left_context = L.dvoc_stream_left_context(ctypes.byref(self._cfg))
-        self._zero_len = None
 
     # ------------------------------------------------------------------ core call
     def batch(self, n: int, frames: int, window: int, audio: torch.Tensor, latents=None,
