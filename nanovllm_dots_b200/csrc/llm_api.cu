@@ -141,10 +141,11 @@ int dllm_read_error(void* workspace, void* stream, uint32_t* err_word) {
 
 namespace {
 
-constexpr int kLlmQkvBN = 128, kLlmGuBN = 256;
-constexpr int kLlmOSplit = 4;     // O-projection split-K partials
-constexpr int kLlmQkvSplit = 4;   // QKV split-K partials (N = 2048 alone gives 16 work units)
-constexpr int kLlmSubPlanes = 5;  // the most partial planes a sublayer writes
+// Split-K partial planes of the decode projections (llm_swap_gemm_kernel:
+// 128 output features per work unit, so N = 1536-2048 alone gives 12-16 units)
+constexpr int kLlmOSplit = 8;      // O-projection
+constexpr int kLlmQkvSplit = 8;    // QKV
+constexpr int kLlmSubPlanes = 12;  // the most partial planes a sublayer writes (O, down)
 
 struct LlmStepWs {
   size_t err, h, xn, qkv, qr, kr, vr, ao, sub, gu, act, part_o, part_ml, total;
@@ -166,12 +167,16 @@ struct LlmHandle {
   const void** vc_ptr;
   int cache_blocks = 0;
   const void* plan_ws = nullptr;
-  CUtensorMap a_xn, a_ao, a_act, o_qkv, o_sub, o_gu;
+  CUtensorMap a_xn, a_ao, a_act;   // the GEMMs' activation operands (64-token boxes)
 };
 
-int llm_down_split(int inter) {
-  const int kb = inter / 64;
-  for (int s : {5, 4, 2}) if (kb % s == 0) return s;
+// K splits of the down-projection: the most (up to kLlmSubPlanes, among the
+// plane counts the RMSNorm kernel is built for) that divide its k-blocks and
+// keep its units (hidden / 128 per split) within one wave.
+int llm_down_split(int inter, int hidden, int sms) {
+  const int kb = inter / 64, tiles = hidden / LS_BM;
+  for (int s : {12, 10, 8, 7, 5, 4, 2})
+    if (kb % s == 0 && tiles * s <= sms) return s;
   return 1;
 }
 
@@ -207,12 +212,12 @@ int llm_validate(const DllmConfig& c) {
   if (c.head_dim != 128 || c.heads < 1 || c.kv_heads < 1 || c.heads % c.kv_heads ||
       c.heads / c.kv_heads > LA_MAXG)
     return DFM_ERR_UNSUPPORTED;
-  if (c.inter < 64 || c.inter % 128 || (2 * c.inter) % kLlmGuBN || c.hidden % kLlmQkvBN)
-    return DFM_ERR_UNSUPPORTED;
+  if (c.inter < 64 || c.inter % 128 || c.hidden % LS_BM) return DFM_ERR_UNSUPPORTED;
   if (c.block_size < LA_SUB || c.block_size % LA_SUB) return DFM_ERR_UNSUPPORTED;
   if (c.layers < 1 || c.max_blocks < 1 || c.max_batch < 1 || !(c.rms_eps > 0.f))
     return DFM_ERR_INVALID_ARG;
-  if ((c.heads * c.head_dim) / 64 % kLlmOSplit || (c.hidden / 64) % kLlmQkvSplit)
+  if ((c.heads * c.head_dim) / 64 % kLlmOSplit || (c.hidden / 64) % kLlmQkvSplit ||
+      ((c.heads + 2 * c.kv_heads) * c.head_dim) % LS_BM)
     return DFM_ERR_UNSUPPORTED;
   return DFM_OK;
 }
@@ -239,8 +244,35 @@ cudaError_t launch_rms_n(int nsub, int hidden, cudaStream_t s, int M, float* h,
     case 2: return launch_rms<2>(hidden, s, M, h, in, sub, plane, w, eps, out);
     case 4: return launch_rms<4>(hidden, s, M, h, in, sub, plane, w, eps, out);
     case 5: return launch_rms<5>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 7: return launch_rms<7>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 8: return launch_rms<8>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 10: return launch_rms<10>(hidden, s, M, h, in, sub, plane, w, eps, out);
+    case 12: return launch_rms<12>(hidden, s, M, h, in, sub, plane, w, eps, out);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// One decode projection on llm_swap_gemm_kernel: out = X W^T for n tokens,
+// as `splits` fp32 partial planes (kF32) or one bf16 result.
+template <bool kF32>
+cudaError_t llm_swap(const CUtensorMap& w, const CUtensorMap& x, int nout, int K, int n, int splits,
+                     void* out, size_t plane, uint32_t* err, cudaStream_t s) {
+  static std::atomic<uint64_t> attr_done{0};
+  auto fn = llm_swap_gemm_kernel<kF32>;
+  cudaError_t r = smem_attr_once(attr_done, fn, LsShape::SMEM);
+  if (r != cudaSuccess) return r;
+  LsArgs p;
+  p.tiles_m = nout / LS_BM;
+  p.tok_blocks = (n + LS_BN - 1) / LS_BN;
+  p.splits = splits;
+  p.nk = K / LS_BK / splits;
+  p.n = n;
+  p.nout = nout;
+  p.out = out;
+  p.plane = plane;
+  const int total = p.tiles_m * p.tok_blocks * splits;
+  const int grid = total < sm_count() ? total : sm_count();
+  return launch_pdl(fn, dim3(grid), dim3(LS_THREADS), LsShape::SMEM, s, w, x, p, err);
 }
 
 bool llm_plan(LlmHandle* h, void* ws) {
@@ -248,13 +280,9 @@ bool llm_plan(LlmHandle* h, void* ws) {
   const DllmConfig& c = h->c;
   uint8_t* b = static_cast<uint8_t*>(ws);
   const uint64_t NR = c.max_batch, Hd = c.hidden, HD = static_cast<uint64_t>(c.heads) * c.head_dim;
-  bool ok = map_2d(&h->a_xn, b + h->ws.xn, NR, Hd, Hd, 128) &&
-            map_2d(&h->a_ao, b + h->ws.ao, NR, HD, HD, 128) &&
-            map_2d(&h->a_act, b + h->ws.act, NR, c.inter, c.inter, 128) &&
-            map_out(&h->o_qkv, b + h->ws.qkv, true, NR, h->qkvw, kLlmQkvSplit, NR * h->qkvw * 4) &&
-            map_out(&h->o_sub, b + h->ws.sub, true, NR, Hd, kLlmSubPlanes, NR * Hd * 4) &&
-            map_out(&h->o_gu, b + h->ws.gu, false, NR, 2 * static_cast<uint64_t>(c.inter), 1,
-                    NR * 2 * static_cast<uint64_t>(c.inter) * 2);
+  bool ok = map_2d(&h->a_xn, b + h->ws.xn, NR, Hd, Hd, LS_BN) &&
+            map_2d(&h->a_ao, b + h->ws.ao, NR, HD, HD, LS_BN) &&
+            map_2d(&h->a_act, b + h->ws.act, NR, c.inter, c.inter, LS_BN);
   if (!ok) {
     h->plan_ws = nullptr;
     return false;
@@ -304,7 +332,7 @@ int dllm_create(const DllmConfig* cfg, const DllmWeights* w, void** out) {
   const DllmConfig& c = h->c;
   const int L = c.layers, Hd = c.hidden, HD = c.heads * c.head_dim;
   h->qkvw = (c.heads + 2 * c.kv_heads) * c.head_dim;
-  h->down_split = llm_down_split(c.inter);
+  h->down_split = llm_down_split(c.inter, c.hidden, sm_count());
   h->mc = llm_max_chunks(c.max_blocks, c.block_size);
   h->ws = llm_step_layout(c, h->qkvw, h->mc);
   h->m_qkv = new CUtensorMap[L];
@@ -319,13 +347,12 @@ int dllm_create(const DllmConfig* cfg, const DllmWeights* w, void** out) {
   bool ok = true;
   for (int l = 0; ok && l < L; ++l) {
     ok = map_2d(&h->m_qkv[l], bw(w->qkv_w) + static_cast<size_t>(l) * h->qkvw * Hd, h->qkvw, Hd,
-                Hd, kLlmQkvBN / 2) &&
-         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * Hd * HD, Hd, HD, HD,
-                kLlmQkvBN / 2) &&
+                Hd, LS_BM) &&
+         map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * Hd * HD, Hd, HD, HD, LS_BM) &&
          map_2d(&h->m_gu[l], bw(w->gate_up_w) + static_cast<size_t>(l) * 2 * c.inter * Hd,
-                2 * static_cast<uint64_t>(c.inter), Hd, Hd, kLlmGuBN / 2) &&
+                2 * static_cast<uint64_t>(c.inter), Hd, Hd, LS_BM) &&
          map_2d(&h->m_down[l], bw(w->down_w) + static_cast<size_t>(l) * Hd * c.inter, Hd, c.inter,
-                c.inter, kLlmQkvBN / 2);
+                c.inter, LS_BM);
   }
   if (!ok) {
     dllm_destroy(h);
@@ -405,8 +432,8 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
                   w.in_norm, c.rms_eps, xn));
   for (int l = 0; l < L; ++l) {
     const int qkvw = hd->qkvw;
-    CK((gemm2<kLlmQkvBN, 6>(hd->a_xn, hd->m_qkv[l], hd->o_qkv, n, qkvw, Hd, kLlmQkvSplit,
-                            store_t<true>(nullptr, kActNone), err, s)));
+    CK(llm_swap<true>(hd->m_qkv[l], hd->a_xn, qkvw, Hd, n, kLlmQkvSplit, f32(hd->ws.qkv),
+                      static_cast<size_t>(c.max_batch) * qkvw, err, s));
     const int cnt = n * (H + 2 * KVH) * (D / 2);
     CK(launch_pdl(llm_rope_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s,
                   static_cast<const float*>(f32(hd->ws.qkv)), kLlmQkvSplit,
@@ -422,17 +449,15 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
                   static_cast<__nv_bfloat16*>(const_cast<void*>(hd->vc_ptr[l])), st->slot_mapping, n,
                   row_elems, static_cast<long long>(st->num_blocks) * c.block_size, err));
     CK(launch_llm_decode<128>(hd->m_kc[l], hd->m_vc[l], ap, bf(hd->ws.ao), s));
-    CK((gemm2<kLlmQkvBN, 6>(hd->a_ao, hd->m_o[l], hd->o_sub, n, Hd, H * D, kLlmOSplit,
-                            store_t<true>(nullptr, kActNone), err, s)));
+    CK(llm_swap<true>(hd->m_o[l], hd->a_ao, Hd, H * D, n, kLlmOSplit, f32(hd->ws.sub), plane, err, s));
     CK(launch_rms_n(kLlmOSplit, Hd, s, n, h, nullptr, f32(hd->ws.sub), plane,
                     w.post_norm + static_cast<size_t>(l) * Hd, c.rms_eps, xn));
-    CK((gemm2<kLlmGuBN, 5>(hd->a_xn, hd->m_gu[l], hd->o_gu, n, 2 * I, Hd, 1,
-                           store_t<false>(nullptr, kActNone), err, s)));
+    CK(llm_swap<false>(hd->m_gu[l], hd->a_xn, 2 * I, Hd, n, 1, bf(hd->ws.gu), 0, err, s));
     const int acnt = n * (I / 8);
     CK(launch_pdl(llm_silu_mul_kernel, dim3((acnt + 255) / 256), dim3(256), 0, s,
                   static_cast<const __nv_bfloat16*>(bf(hd->ws.gu)), n, I, bf(hd->ws.act)));
-    CK((gemm2<kLlmQkvBN, 6>(hd->a_act, hd->m_down[l], hd->o_sub, n, Hd, I, hd->down_split,
-                            store_t<true>(nullptr, kActNone), err, s)));
+    CK(llm_swap<true>(hd->m_down[l], hd->a_act, Hd, I, n, hd->down_split, f32(hd->ws.sub), plane,
+                      err, s));
     // residual + the next layer's input norm, or the final norm into the output
     const bool last = l == L - 1;
     CK(launch_rms_n(hd->down_split, Hd, s, n, h, nullptr, f32(hd->ws.sub), plane,

@@ -137,3 +137,198 @@ __global__ void __launch_bounds__(256)
 }
 
 }  // namespace dfm
+
+namespace dfm {
+
+// ---------------------------------------------------------------- decode GEMM
+// The decode step's projections have M = n tokens (64) and stream their
+// weights: as an A operand of M = n they would fill a fraction of each MMA and
+// of each CTA pair.  Here the operands are swapped: the weight W [N_out][K]
+// (K-major, the nn.Linear layout) is the MMA's A operand, 128 output features
+// per tile, and the activations X [n][K] its B operand, 64 tokens per tile, so
+//   out_plane[s][t][j] = sum_{k in K-split s} W[j][k] X[t][k]
+// with every weight byte read once.  Work units (feature tile, token block,
+// K split) run on a persistent grid, feature tiles fastest so the CTAs at work
+// at once stream different weight rows; the first stages' weight tiles are
+// loaded before the dependency wait.  The epilogue reads one feature per
+// thread (TMEM lane) and writes the transpose: for each token the warp's 32
+// lanes store 32 consecutive features (coalesced).  Roles as gemm_bf16_tn.
+constexpr int LS_BM = 128, LS_BN = 64, LS_BK = 64, LS_ST = 8, LS_THREADS = 192;
+
+struct LsShape {
+  static constexpr int A_BYTES = LS_BM * LS_BK * 2;   // 16 KB of W
+  static constexpr int B_BYTES = LS_BN * LS_BK * 2;   // 8 KB of X
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM = LS_ST * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = 2 * LS_BN;    // double-buffered accumulators
+};
+
+struct LsArgs {
+  int tiles_m, tok_blocks, splits, nk;   // feature tiles, token blocks, K splits, k-blocks per split
+  int n, nout;                           // tokens, output features (row stride of out)
+  void* out;                             // fp32 planes [splits][rows][nout] or bf16 [rows][nout]
+  size_t plane;                          // elements between planes
+};
+
+template <bool kF32>
+__global__ void __launch_bounds__(LS_THREADS, 1)
+    llm_swap_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                         LsArgs p, uint32_t* err) {
+  using S = LsShape;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + LS_ST * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + LS_ST * S::STAGE_BYTES);
+  uint64_t* empty = full + LS_ST;
+  uint64_t* tm_full = empty + LS_ST;  // [2]
+  uint64_t* tm_empty = tm_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.tiles_m * p.tok_blocks * p.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < LS_ST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tm_full[b], 1);
+      mbar_init(&tm_empty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&tmW);
+    tma_prefetch(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  auto unit = [&](int t, int& m0, int& t0, int& kb0, int& s) {
+    const int mt = t % p.tiles_m, rest = t / p.tiles_m;
+    const int tb = rest % p.tok_blocks;
+    s = rest / p.tok_blocks;
+    m0 = mt * LS_BM;
+    t0 = tb * LS_BN;
+    kb0 = s * p.nk;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // the weights do not depend on the previous kernel: the first stages'
+      // W tiles go out before the dependency wait
+      int m0, t0, kb0, s;
+      unit(blockIdx.x, m0, t0, kb0, s);
+      const int pre = static_cast<int>(blockIdx.x) < total ? (p.nk < LS_ST ? p.nk : LS_ST) : 0;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], S::STAGE_BYTES);
+        tma_load_2d(sA + kb * S::A_BYTES, &tmW, &full[kb], (kb0 + kb) * LS_BK, m0);
+      }
+      pdl_wait();
+      int g = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        unit(t, m0, t0, kb0, s);
+#pragma unroll 1
+        for (int kb = 0; kb < p.nk; ++kb, ++g) {
+          const int st = g % LS_ST;
+          const uint32_t ph = (g / LS_ST) & 1;
+          if (g >= pre) {
+            if (g >= LS_ST && !mbar_wait(&empty[st], ph ^ 1, abort_flag, err)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
+            tma_load_2d(sA + st * S::A_BYTES, &tmW, &full[st], (kb0 + kb) * LS_BK, m0);
+          }
+          tma_load_2d(sB + st * S::B_BYTES, &tmX, &full[st], (kb0 + kb) * LS_BK, t0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(LS_BM, LS_BN);
+      int g = 0, u = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++u) {
+        const int b = u & 1;
+        if (u >= 2 && !mbar_wait(&tm_empty[b], ((u >> 1) & 1) ^ 1, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * LS_BN;
+#pragma unroll 1
+        for (int kb = 0; kb < p.nk; ++kb, ++g) {
+          const int st = g % LS_ST;
+          if (!mbar_wait(&full[st], (g / LS_ST) & 1, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + st * S::A_BYTES);
+          const uint32_t bb = smem_u32(sB + st * S::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < LS_BK / 16; ++kk)
+            umma_bf16(acc, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), idesc,
+                      (kb | kk) != 0);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&tm_full[b]);
+      }
+    }
+  } else {
+    pdl_wait();
+    const int q = warp & 3;
+    int u = 0;
+#pragma unroll 1
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++u) {
+      const int b = u & 1;
+      const bool ready =
+          __all_sync(0xffffffffu, mbar_wait(&tm_full[b], (u >> 1) & 1, abort_flag, err));
+      if (!ready) break;
+      tc_fence_after();
+      int m0, t0, kb0, s;
+      unit(t, m0, t0, kb0, s);
+      const int j = m0 + q * 32 + lane;   // this thread's output feature
+#pragma unroll 1
+      for (int c = 0; c < LS_BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + b * LS_BN + c + (static_cast<uint32_t>(q * 32) << 16), r);
+        tmem_wait_ld();
+        if (j >= p.nout) continue;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int tok = t0 + c + i;
+          if (tok < p.n) {
+            const size_t o = (kF32 ? static_cast<size_t>(s) * p.plane : 0) +
+                             static_cast<size_t>(tok) * p.nout + j;
+            if constexpr (kF32)
+              static_cast<float*>(p.out)[o] = __uint_as_float(r[i]);
+            else
+              static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(__uint_as_float(r[i]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+}  // namespace dfm
