@@ -148,7 +148,7 @@ constexpr int kLlmQkvSplit = 8;    // QKV
 constexpr int kLlmSubPlanes = 12;  // the most partial planes a sublayer writes (O, down)
 
 struct LlmStepWs {
-  size_t err, h, xn, qkv, qr, kr, vr, ao, sub, gu, act, part_o, part_ml, total;
+  size_t err, h, xn, qkv, qr, ao, sub, gu, act, part_o, part_ml, total;
 };
 
 struct LlmHandle {
@@ -195,8 +195,6 @@ LlmStepWs llm_step_layout(const DllmConfig& c, int qkvw, int mc) {
   L.xn = take(NR * Hd * 2);
   L.qkv = take(kLlmQkvSplit * NR * qkvw * 4);   // fp32 split-K planes
   L.qr = take(NR * HD * 2);
-  L.kr = take(NR * KD * 2);
-  L.vr = take(NR * KD * 2);
   L.ao = take(NR * HD * 2);
   L.sub = take(kLlmSubPlanes * NR * Hd * 4);
   L.gu = take(NR * 2 * static_cast<size_t>(c.inter) * 2);
@@ -439,15 +437,10 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
                   static_cast<const float*>(f32(hd->ws.qkv)), kLlmQkvSplit,
                   static_cast<size_t>(c.max_batch) * qkvw,
                   static_cast<const float*>(w.qkv_b + static_cast<size_t>(l) * qkvw), st->positions,
-                  w.inv_freq, n, H, KVH, D, bf(hd->ws.qr), bf(hd->ws.kr), bf(hd->ws.vr)));
-    const int row_elems = KVH * D;
-    const int scnt = 2 * n * (row_elems / 8);
-    CK(launch_pdl(llm_store_kv_kernel, dim3((scnt + 255) / 256), dim3(256), 0, s,
-                  static_cast<const __nv_bfloat16*>(bf(hd->ws.kr)),
-                  static_cast<const __nv_bfloat16*>(bf(hd->ws.vr)),
+                  w.inv_freq, n, H, KVH, D, bf(hd->ws.qr),
                   static_cast<__nv_bfloat16*>(const_cast<void*>(hd->kc_ptr[l])),
-                  static_cast<__nv_bfloat16*>(const_cast<void*>(hd->vc_ptr[l])), st->slot_mapping, n,
-                  row_elems, static_cast<long long>(st->num_blocks) * c.block_size, err));
+                  static_cast<__nv_bfloat16*>(const_cast<void*>(hd->vc_ptr[l])), st->slot_mapping,
+                  static_cast<long long>(st->num_blocks) * c.block_size, err));
     CK(launch_llm_decode<128>(hd->m_kc[l], hd->m_vc[l], ap, bf(hd->ws.ao), s));
     CK(llm_swap<true>(hd->m_o[l], hd->a_ao, Hd, H * D, n, kLlmOSplit, f32(hd->ws.sub), plane, err, s));
     CK(launch_rms_n(kLlmOSplit, Hd, s, n, h, nullptr, f32(hd->ws.sub), plane,

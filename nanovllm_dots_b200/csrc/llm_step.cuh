@@ -73,16 +73,19 @@ __global__ void __launch_bounds__(LR_THREADS)
 }
 
 // qkv = bias + sum of the QKV projection's nsplit fp32 split-K planes
-// [p][n][(H + 2 KVH) D] -> q [n][H][D], k [n][KVH][D] rotated at positions[i]
-// (NeoX halves: y1 = x1 cos - x2 sin, y2 = x2 cos + x1 sin, angle
-// pos * inv_freq[d], ``layers/rotary_embedding.py:6-47``) and v [n][KVH][D].
-// One thread per (row, head, rotary pair).
+// [p][n][(H + 2 KVH) D] -> q [n][H][D] and k rotated at positions[i] (NeoX
+// halves: y1 = x1 cos - x2 sin, y2 = x2 cos + x1 sin, angle pos * inv_freq[d],
+// ``layers/rotary_embedding.py:6-47``), v unrotated; k and v go straight into
+// the paged caches at the token's slot (``store_kvcache``,
+// ``layers/attention.py:10-47``: slot < 0 skips the token, a slot past the
+// cache is reported and skipped).  One thread per (row, head, rotary pair).
 __global__ void __launch_bounds__(256)
     llm_rope_kernel(const float* __restrict__ qkv, int nsplit, size_t plane,
                     const float* __restrict__ bias, const int* __restrict__ positions,
                     const float* __restrict__ inv_freq, int n, int H, int KVH, int D,
-                    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
-                    __nv_bfloat16* __restrict__ v) {
+                    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k_cache,
+                    __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ slot_mapping,
+                    long long num_slots, uint32_t* err) {
   const int half = D / 2, heads = H + 2 * KVH;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   pdl_trigger();
@@ -91,6 +94,19 @@ __global__ void __launch_bounds__(256)
   const int i = idx / (heads * half);
   const int rem = idx - i * heads * half;
   const int hd = rem / half, d = rem - hd * half;
+  __nv_bfloat16* dst;
+  if (hd < H) {
+    dst = q + (static_cast<size_t>(i) * H + hd) * D;
+  } else {
+    const int slot = slot_mapping[i];
+    if (slot < 0) return;
+    if (slot >= num_slots) {
+      if (d == 0) atomicOr(err, DFM_DEV_ERR_PAGE);
+      return;
+    }
+    const int kvh = hd < H + KVH ? hd - H : hd - H - KVH;
+    dst = (hd < H + KVH ? k_cache : v_cache) + (static_cast<size_t>(slot) * KVH + kvh) * D;
+  }
   const int c1 = hd * D + d, c2 = c1 + half;
   const float* src = qkv + static_cast<size_t>(i) * heads * D;
   float x1 = bias[c1], x2 = bias[c2];
@@ -99,15 +115,12 @@ __global__ void __launch_bounds__(256)
     x2 += src[p * plane + c2];
   }
   if (hd >= H + KVH) {   // v: no rotation
-    __nv_bfloat16* dst = v + (static_cast<size_t>(i) * KVH + (hd - H - KVH)) * D;
     dst[d] = __float2bfloat16(x1);
     dst[d + half] = __float2bfloat16(x2);
     return;
   }
   float s, c;
   sincosf(static_cast<float>(positions[i]) * inv_freq[d], &s, &c);
-  __nv_bfloat16* dst = hd < H ? q + (static_cast<size_t>(i) * H + hd) * D
-                              : k + (static_cast<size_t>(i) * KVH + (hd - H)) * D;
   dst[d] = __float2bfloat16(x1 * c - x2 * s);
   dst[d + half] = __float2bfloat16(x2 * c + x1 * s);
 }
