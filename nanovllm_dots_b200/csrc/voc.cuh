@@ -356,7 +356,7 @@ constexpr int VH_BOX = 64;                 // frames per TMA box
 // epilogue; 1: they wait for it, which halves TMEM so two CTAs per SM fit).
 template <int BN, int SA, int SB, int SE = 0, int MT = 1, int NB = 2>
 struct VhShape {
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "MMA N");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "MMA N");
   static_assert(MT == 1 || MT == 2, "accumulators per tile");
   static constexpr int ROWS = MT * VC_BM + VH_HALO;           // frames staged per A tile
   static constexpr int A_BYTES = ROWS * VC_ROWB;               // 12 KB (MT 1) or 20 KB (MT 2)

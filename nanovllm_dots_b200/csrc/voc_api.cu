@@ -290,7 +290,7 @@ bool voc_halo(const VocConv& v) {
 // per SM still fit); at 64 a single buffer measured slower than the direct
 // loads, which the wider tiles keep.
 int voc_halo_bn(int N) {
-  return N == 32 ? 32 : N == 64 ? 64 : N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : 32;
+  return N == 32 ? 32 : N == 64 ? 64 : N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : 32;
 }
 
 cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& amap, int n,
@@ -319,6 +319,7 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
   p.out16 = out16;
   if (halo_map && voc_halo(v)) {
     switch (voc_halo_bn(v.N)) {
+      case 256: return voc_halo_launch<256, 3, 4, 0, 1, 1>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 128: return voc_halo_launch<128, 3, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 96: return voc_halo_launch<96, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 64: return voc_halo_launch<64, 2, 8, 0, 2>(*halo_map, v.wmap, *halo_map, p, err, s);
