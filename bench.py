@@ -945,7 +945,7 @@ def run_llmdecode(args, rank, world):
                 "e2e": {"value": round(n * 1000.0 / e2e_ms, 1), "unit": "tokens/s",
                         "h2d_bytes_per_step": h_emb.numel() * 2, "d2h_bytes_per_step": h_out.numel() * 2,
                         "ms_per_step": round(e2e_ms, 4)},
-                "gpu_launches": (1 + 11 * cfg.layers) * args.steps,
+                "gpu_launches": (1 + 9 * cfg.layers) * args.steps,
                 "roofline": {"kernel": "whole decode step (weights + K/V streamed once)",
                              "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                              "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,

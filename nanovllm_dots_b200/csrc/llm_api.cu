@@ -148,7 +148,7 @@ constexpr int kLlmQkvSplit = 8;    // QKV
 constexpr int kLlmSubPlanes = 12;  // the most partial planes a sublayer writes (O, down)
 
 struct LlmStepWs {
-  size_t err, h, xn, qkv, qr, ao, sub, gu, act, part_o, part_ml, total;
+  size_t err, h, xn, qkv, qr, ao, sub, act, part_o, part_ml, total;
 };
 
 struct LlmHandle {
@@ -197,7 +197,6 @@ LlmStepWs llm_step_layout(const DllmConfig& c, int qkvw, int mc) {
   L.qr = take(NR * HD * 2);
   L.ao = take(NR * HD * 2);
   L.sub = take(kLlmSubPlanes * NR * Hd * 4);
-  L.gu = take(NR * 2 * static_cast<size_t>(c.inter) * 2);
   L.act = take(NR * static_cast<size_t>(c.inter) * 2);
   L.part_o = take(NR * c.heads * mc * static_cast<size_t>(c.head_dim) * 4);
   L.part_ml = take(NR * c.heads * mc * 2 * 4);
@@ -251,16 +250,19 @@ cudaError_t launch_rms_n(int nsub, int hidden, cudaStream_t s, int M, float* h,
 }
 
 // One decode projection on llm_swap_gemm_kernel: out = X W^T for n tokens,
-// as `splits` fp32 partial planes (kF32) or one bf16 result.
-template <bool kF32>
+// as `splits` fp32 partial planes (LS_F32), one bf16 result (LS_BF16), or
+// silu(gate) * up of a [gate; up] weight with nout = I (LS_SILU, W's tensor
+// map in 32-row boxes).
+template <int kMode>
 cudaError_t llm_swap(const CUtensorMap& w, const CUtensorMap& x, int nout, int K, int n, int splits,
                      void* out, size_t plane, uint32_t* err, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
-  auto fn = llm_swap_gemm_kernel<kF32>;
-  cudaError_t r = smem_attr_once(attr_done, fn, LsShape::SMEM);
+  auto fn = llm_swap_gemm_kernel<kMode>;
+  constexpr int smem = kMode == LS_SILU ? LsShape::SMEM_SILU : LsShape::SMEM;
+  cudaError_t r = smem_attr_once(attr_done, fn, smem);
   if (r != cudaSuccess) return r;
   LsArgs p;
-  p.tiles_m = nout / LS_BM;
+  p.tiles_m = (kMode == LS_SILU ? 2 * nout : nout) / LS_BM;
   p.tok_blocks = (n + LS_BN - 1) / LS_BN;
   p.splits = splits;
   p.nk = K / LS_BK / splits;
@@ -270,7 +272,7 @@ cudaError_t llm_swap(const CUtensorMap& w, const CUtensorMap& x, int nout, int K
   p.plane = plane;
   const int total = p.tiles_m * p.tok_blocks * splits;
   const int grid = total < sm_count() ? total : sm_count();
-  return launch_pdl(fn, dim3(grid), dim3(LS_THREADS), LsShape::SMEM, s, w, x, p, err);
+  return launch_pdl(fn, dim3(grid), dim3(LS_THREADS), smem, s, w, x, p, err);
 }
 
 bool llm_plan(LlmHandle* h, void* ws) {
@@ -348,7 +350,7 @@ int dllm_create(const DllmConfig* cfg, const DllmWeights* w, void** out) {
                 Hd, LS_BM) &&
          map_2d(&h->m_o[l], bw(w->o_w) + static_cast<size_t>(l) * Hd * HD, Hd, HD, HD, LS_BM) &&
          map_2d(&h->m_gu[l], bw(w->gate_up_w) + static_cast<size_t>(l) * 2 * c.inter * Hd,
-                2 * static_cast<uint64_t>(c.inter), Hd, Hd, LS_BM) &&
+                2 * static_cast<uint64_t>(c.inter), Hd, Hd, 32) &&
          map_2d(&h->m_down[l], bw(w->down_w) + static_cast<size_t>(l) * Hd * c.inter, Hd, c.inter,
                 c.inter, LS_BM);
   }
@@ -430,7 +432,7 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
                   w.in_norm, c.rms_eps, xn));
   for (int l = 0; l < L; ++l) {
     const int qkvw = hd->qkvw;
-    CK(llm_swap<true>(hd->m_qkv[l], hd->a_xn, qkvw, Hd, n, kLlmQkvSplit, f32(hd->ws.qkv),
+    CK(llm_swap<LS_F32>(hd->m_qkv[l], hd->a_xn, qkvw, Hd, n, kLlmQkvSplit, f32(hd->ws.qkv),
                       static_cast<size_t>(c.max_batch) * qkvw, err, s));
     const int cnt = n * (H + 2 * KVH) * (D / 2);
     CK(launch_pdl(llm_rope_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s,
@@ -442,14 +444,11 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
                   static_cast<__nv_bfloat16*>(const_cast<void*>(hd->vc_ptr[l])), st->slot_mapping,
                   static_cast<long long>(st->num_blocks) * c.block_size, err));
     CK(launch_llm_decode<128>(hd->m_kc[l], hd->m_vc[l], ap, bf(hd->ws.ao), s));
-    CK(llm_swap<true>(hd->m_o[l], hd->a_ao, Hd, H * D, n, kLlmOSplit, f32(hd->ws.sub), plane, err, s));
+    CK(llm_swap<LS_F32>(hd->m_o[l], hd->a_ao, Hd, H * D, n, kLlmOSplit, f32(hd->ws.sub), plane, err, s));
     CK(launch_rms_n(kLlmOSplit, Hd, s, n, h, nullptr, f32(hd->ws.sub), plane,
                     w.post_norm + static_cast<size_t>(l) * Hd, c.rms_eps, xn));
-    CK(llm_swap<false>(hd->m_gu[l], hd->a_xn, 2 * I, Hd, n, 1, bf(hd->ws.gu), 0, err, s));
-    const int acnt = n * (I / 8);
-    CK(launch_pdl(llm_silu_mul_kernel, dim3((acnt + 255) / 256), dim3(256), 0, s,
-                  static_cast<const __nv_bfloat16*>(bf(hd->ws.gu)), n, I, bf(hd->ws.act)));
-    CK(llm_swap<true>(hd->m_down[l], hd->a_act, Hd, I, n, hd->down_split, f32(hd->ws.sub), plane,
+    CK(llm_swap<LS_SILU>(hd->m_gu[l], hd->a_xn, I, Hd, n, 1, bf(hd->ws.act), 0, err, s));
+    CK(llm_swap<LS_F32>(hd->m_down[l], hd->a_act, Hd, I, n, hd->down_split, f32(hd->ws.sub), plane,
                       err, s));
     // residual + the next layer's input norm, or the final norm into the output
     const bool last = l == L - 1;

@@ -125,30 +125,6 @@ __global__ void __launch_bounds__(256)
   dst[d + half] = __float2bfloat16(x2 * c + x1 * s);
 }
 
-// gu [n][2 I] = [gate | up] -> act [n][I] = silu(gate) * up (``layers/activation.py:5-14``);
-// one thread per 8 outputs.
-__global__ void __launch_bounds__(256)
-    llm_silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int n, int I,
-                        __nv_bfloat16* __restrict__ act) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  pdl_trigger();
-  pdl_wait();
-  const int per = I / 8;
-  if (idx >= n * per) return;
-  const int i = idx / per, c = (idx - i * per) * 8;
-  const uint4 g4 = *reinterpret_cast<const uint4*>(gu + static_cast<size_t>(i) * 2 * I + c);
-  const uint4 u4 = *reinterpret_cast<const uint4*>(gu + static_cast<size_t>(i) * 2 * I + I + c);
-  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g4);
-  const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&u4);
-  uint32_t o[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 g = __bfloat1622float2(g2[e]), u = __bfloat1622float2(u2[e]);
-    o[e] = pack_bf16(silu(g.x) * u.x, silu(g.y) * u.y);
-  }
-  *reinterpret_cast<uint4*>(act + static_cast<size_t>(i) * I + c) = make_uint4(o[0], o[1], o[2], o[3]);
-}
-
 }  // namespace dfm
 
 namespace dfm {
@@ -166,24 +142,60 @@ namespace dfm {
 // loaded before the dependency wait.  The epilogue reads one feature per
 // thread (TMEM lane) and writes the transpose: for each token the warp's 32
 // lanes store 32 consecutive features (coalesced).  Roles as gemm_bf16_tn.
+//
+// Output modes:
+//   LS_BF16  one bf16 result [n][nout]
+//   LS_F32   `splits` fp32 partial planes [s][n][nout]
+//   LS_SILU  the MLP's gate|up projection with SiLU-and-mul in the epilogue
+//            (``layers/activation.py:5-14``): W = [gate; up] [2I][K] and
+//            act[t][f] = silu(gate_t[f]) * up_t[f] for f < I = nout.  Each
+//            128-row W tile is loaded as four 32-row boxes, gate rows
+//            64m..64m+31, up rows I+64m.., gate 64m+32.., up I+64m+32.., so
+//            TMEM lane quadrants 0/1 (and 2/3) hold the gate and up values of
+//            the same 32 features.  The two warps of a pair swap half of
+//            their (bf16-rounded, as the reference's bf16 linear output)
+//            values through shared memory and each writes act for half of
+//            the tokens.  The separate [n][2I] gate|up tensor never exists.
 constexpr int LS_BM = 128, LS_BN = 64, LS_BK = 64, LS_ST = 8, LS_THREADS = 192;
+constexpr int LS_BF16 = 0, LS_F32 = 1, LS_SILU = 2;
 
 struct LsShape {
   static constexpr int A_BYTES = LS_BM * LS_BK * 2;   // 16 KB of W
   static constexpr int B_BYTES = LS_BN * LS_BK * 2;   // 8 KB of X
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM = LS_ST * STAGE_BYTES + 1024 + 256;
+  static constexpr int XBUF_FLOATS = 2 * 2 * 32 * 32;  // LS_SILU: [pair][chunk parity][token][lane]
+  static constexpr int SMEM_SILU = SMEM + XBUF_FLOATS * 4;
   static constexpr uint32_t TMEM_COLS = 2 * LS_BN;    // double-buffered accumulators
 };
 
+// Named barrier over `nthreads` threads (whole warps) that also returns the
+// AND of every participant's predicate.
+DFM_DEV bool bar_red_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+DFM_DEV void bar_sync_n(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 struct LsArgs {
   int tiles_m, tok_blocks, splits, nk;   // feature tiles, token blocks, K splits, k-blocks per split
-  int n, nout;                           // tokens, output features (row stride of out)
+  int n, nout;                           // tokens, output features (row stride of out; I for LS_SILU)
   void* out;                             // fp32 planes [splits][rows][nout] or bf16 [rows][nout]
   size_t plane;                          // elements between planes
 };
 
-template <bool kF32>
+template <int kMode>
 __global__ void __launch_bounds__(LS_THREADS, 1)
     llm_swap_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                          LsArgs p, uint32_t* err) {
@@ -199,8 +211,20 @@ __global__ void __launch_bounds__(LS_THREADS, 1)
   uint64_t* tm_empty = tm_full + 2;   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xbuf = reinterpret_cast<float*>(smem + LS_ST * S::STAGE_BYTES + 256);   // LS_SILU only
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = p.tiles_m * p.tok_blocks * p.splits;
+  // one W tile: a 128-row box, or (LS_SILU) four 32-row boxes of gate and up rows
+  auto load_w = [&](uint8_t* dst, uint64_t* bar, int kx, int m0) {
+    if constexpr (kMode == LS_SILU) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        tma_load_2d(dst + q * (S::A_BYTES / 4), &tmW, bar, kx,
+                    (q & 1) * p.nout + (m0 >> 1) + 32 * (q >> 1));
+    } else {
+      tma_load_2d(dst, &tmW, bar, kx, m0);
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < LS_ST; ++s) {
@@ -244,7 +268,7 @@ __global__ void __launch_bounds__(LS_THREADS, 1)
       const int pre = static_cast<int>(blockIdx.x) < total ? (p.nk < LS_ST ? p.nk : LS_ST) : 0;
       for (int kb = 0; kb < pre; ++kb) {
         mbar_arrive_expect_tx(&full[kb], S::STAGE_BYTES);
-        tma_load_2d(sA + kb * S::A_BYTES, &tmW, &full[kb], (kb0 + kb) * LS_BK, m0);
+        load_w(sA + kb * S::A_BYTES, &full[kb], (kb0 + kb) * LS_BK, m0);
       }
       pdl_wait();
       int g = 0;
@@ -262,7 +286,7 @@ __global__ void __launch_bounds__(LS_THREADS, 1)
               break;
             }
             mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
-            tma_load_2d(sA + st * S::A_BYTES, &tmW, &full[st], (kb0 + kb) * LS_BK, m0);
+            load_w(sA + st * S::A_BYTES, &full[st], (kb0 + kb) * LS_BK, m0);
           }
           tma_load_2d(sB + st * S::B_BYTES, &tmX, &full[st], (kb0 + kb) * LS_BK, t0);
         }
@@ -301,30 +325,64 @@ __global__ void __launch_bounds__(LS_THREADS, 1)
   } else {
     pdl_wait();
     const int q = warp & 3;
-    int u = 0;
+    const int pair = q >> 1;           // LS_SILU: quadrants 0/1 and 2/3 hold gate/up of one feature set
+    const bool gate = (q & 1) == 0;
+    int u = 0, ch = 0;
 #pragma unroll 1
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++u) {
       const int b = u & 1;
-      const bool ready =
-          __all_sync(0xffffffffu, mbar_wait(&tm_full[b], (u >> 1) & 1, abort_flag, err));
+      bool ready = __all_sync(0xffffffffu, mbar_wait(&tm_full[b], (u >> 1) & 1, abort_flag, err));
+      // the two warps of a pair meet at named barriers below: both leave together
+      if constexpr (kMode == LS_SILU) ready = bar_red_and(1 + pair, 64, ready);
       if (!ready) break;
       tc_fence_after();
       int m0, t0, kb0, s;
       unit(t, m0, t0, kb0, s);
-      const int j = m0 + q * 32 + lane;   // this thread's output feature
+      const int j = kMode == LS_SILU ? (m0 >> 1) + 32 * pair + lane   // this thread's output feature
+                                     : m0 + q * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < LS_BN; c += 32) {
+      for (int c = 0; c < LS_BN; c += 32, ++ch) {
         uint32_t r[32];
         tmem_ld32(tmem + b * LS_BN + c + (static_cast<uint32_t>(q * 32) << 16), r);
         tmem_wait_ld();
+        if constexpr (kMode == LS_SILU) {
+          // the pair splits the chunk's 32 tokens: the gate warp finishes
+          // tokens 0-15 (with the up warp's values), the up warp 16-31
+          float* xb = xbuf + (pair * 2 + (ch & 1)) * 1024;   // [16 tokens][lane] from each warp
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(__float2bfloat16(__uint_as_float(r[i])));
+          if (gate) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xb[512 + i * 32 + lane] = v[16 + i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xb[i * 32 + lane] = v[i];
+          }
+          bar_sync_n(1 + pair, 64);
+          __nv_bfloat16* act = static_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(t0 + c) * p.nout + j;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float g, up;
+            int tok;
+            if (gate) {
+              g = v[i], up = xb[i * 32 + lane], tok = i;
+            } else {
+              g = xb[512 + i * 32 + lane], up = v[16 + i], tok = 16 + i;
+            }
+            if (t0 + c + tok < p.n)
+              act[static_cast<size_t>(tok) * p.nout] = __float2bfloat16(__fdividef(g, 1.0f + __expf(-g)) * up);
+          }
+          continue;
+        }
         if (j >= p.nout) continue;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int tok = t0 + c + i;
           if (tok < p.n) {
-            const size_t o = (kF32 ? static_cast<size_t>(s) * p.plane : 0) +
+            const size_t o = (kMode == LS_F32 ? static_cast<size_t>(s) * p.plane : 0) +
                              static_cast<size_t>(tok) * p.nout + j;
-            if constexpr (kF32)
+            if constexpr (kMode == LS_F32)
               static_cast<float*>(p.out)[o] = __uint_as_float(r[i]);
             else
               static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(__uint_as_float(r[i]));

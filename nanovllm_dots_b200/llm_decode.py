@@ -6,8 +6,9 @@ step through ``BatchedPagedLLM._decode_batch`` (``batched_llm.py:177-236``):
 ``QwenLLM.forward`` (``model_llm.py:113-171``) over torch linears, a Triton
 K/V store and flash-attn's paged decode.  ``B200QwenDecoder.step`` is that
 forward as one C call: per layer RMSNorm, the QKV / O / gate-up / down
-projections on the CTA-pair tcgen05 GEMM, rotary, the paged decode attention,
-SiLU-and-mul and the residual adds, on the caller's stream.  The caches stay
+projections on a swapped-operand tcgen05 GEMM (SiLU-and-mul in the gate-up
+epilogue), rotary with the K/V cache write, the paged decode attention and
+the residual adds, on the caller's stream.  The caches stay
 the engine's (``BatchedPagedLLM`` allocates one K and one V tensor per layer,
 ``batched_llm.py:57-66``).  There is no CPU path.
 """
