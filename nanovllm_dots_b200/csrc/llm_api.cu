@@ -223,11 +223,11 @@ template <int NSUB>
 cudaError_t launch_rms(int hidden, cudaStream_t s, int M, float* h, const __nv_bfloat16* in,
                        const float* sub, size_t plane, const float* w, float eps,
                        __nv_bfloat16* out) {
-  const dim3 grid((M + LR_ROWS_PER_BLOCK - 1) / LR_ROWS_PER_BLOCK), block(LR_THREADS);
+  const dim3 grid(M);
   switch (hidden) {
-    case 1024: return launch_pdl(llm_rms_kernel<1024, NSUB>, grid, block, 0, s, h, in, sub, plane, M, w, eps, out);
-    case 1536: return launch_pdl(llm_rms_kernel<1536, NSUB>, grid, block, 0, s, h, in, sub, plane, M, w, eps, out);
-    case 2048: return launch_pdl(llm_rms_kernel<2048, NSUB>, grid, block, 0, s, h, in, sub, plane, M, w, eps, out);
+    case 1024: return launch_pdl(llm_rms_kernel<1024, NSUB>, grid, dim3(256), 0, s, h, in, sub, plane, M, w, eps, out);
+    case 1536: return launch_pdl(llm_rms_kernel<1536, NSUB>, grid, dim3(384), 0, s, h, in, sub, plane, M, w, eps, out);
+    case 2048: return launch_pdl(llm_rms_kernel<2048, NSUB>, grid, dim3(512), 0, s, h, in, sub, plane, M, w, eps, out);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -291,12 +291,16 @@ __global__ void __launch_bounds__(LA_THREADS)
 }
 
 // out[i][h] = sum_c 2^(m_c - M) acc_c / sum_c 2^(m_c - M) l_c over the chunks
-// of sequence i; one block of D threads per (sequence, query head).
+// of sequence i; one block of D threads per (sequence, query head).  The
+// chunks' partials are read eight at a time, every load of a batch in flight
+// at once (one batch up to 1024 keys: the same sums, in the same order, as a
+// single pass with M the maximum over all chunks).
 template <int D>
 __global__ void __launch_bounds__(D)
     llm_attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                             const int* __restrict__ context_lens, int H, int max_chunks,
                             int max_keys, __nv_bfloat16* __restrict__ out) {
+  constexpr int CB = 8;
   const int row = blockIdx.x;            // i * H + h
   const int i = row / H;
   pdl_trigger();
@@ -304,13 +308,30 @@ __global__ void __launch_bounds__(D)
   const int ctx = context_lens[i];
   const int nch = (ctx < 1 || ctx > max_keys) ? 0 : (ctx + LA_CHUNK - 1) / LA_CHUNK;
   const float* ml = part_ml + static_cast<size_t>(row) * max_chunks * 2;
-  float M = -INFINITY;
-  for (int c = 0; c < nch; ++c) M = fmaxf(M, ml[2 * c]);
-  float L = 0.f, a = 0.f;
-  for (int c = 0; c < nch; ++c) {
-    const float w = fast_exp2(ml[2 * c] - M);
-    L += w * ml[2 * c + 1];
-    a += w * part_o[(static_cast<size_t>(row) * max_chunks + c) * D + threadIdx.x];
+  const float* po = part_o + static_cast<size_t>(row) * max_chunks * D + threadIdx.x;
+  float M = -INFINITY, L = 0.f, a = 0.f;
+  for (int c0 = 0; c0 < nch; c0 += CB) {
+    float m[CB], l[CB], o[CB];
+#pragma unroll
+    for (int j = 0; j < CB; ++j) {
+      const bool v = c0 + j < nch;
+      m[j] = v ? ml[2 * (c0 + j)] : -INFINITY;
+      l[j] = v ? ml[2 * (c0 + j) + 1] : 0.f;
+      o[j] = v ? po[static_cast<size_t>(c0 + j) * D] : 0.f;
+    }
+    float Mn = M;
+#pragma unroll
+    for (int j = 0; j < CB; ++j) Mn = fmaxf(Mn, m[j]);
+    const float sc = M == -INFINITY ? 0.f : fast_exp2(M - Mn);
+    L *= sc;
+    a *= sc;
+#pragma unroll
+    for (int j = 0; j < CB; ++j) {
+      const float w = fast_exp2(m[j] - Mn);
+      L += w * l[j];
+      a += w * o[j];
+    }
+    M = Mn;
   }
   out[static_cast<size_t>(row) * D + threadIdx.x] = __float2bfloat16(L > 0.f ? a / L : 0.f);
 }

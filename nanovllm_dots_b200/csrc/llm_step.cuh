@@ -9,67 +9,56 @@
 
 namespace dfm {
 
-constexpr int LR_ROWS_PER_BLOCK = 2;
-constexpr int LR_THREADS = 128 * LR_ROWS_PER_BLOCK;
-
-// One row per 128 threads (HD / 512 float4 column groups per thread):
+// One row per block, one float4 column group per thread (HD / 4 threads), so
+// every load of a row (residual, the NSUB partial planes, the weight) is in
+// flight at once:
 //   NSUB == 0: x = float(in[r])                 (the step's input embeddings)
 //   NSUB >  0: x = h[r] + sum_p sub[p][r]       (residual + the sublayer's partials)
 //   h[r] = x;  out[r] = bf16(x * rsqrt(mean(x^2) + eps) * w)
 // (``layers/layernorm.py:17-26``; the residual stream h is kept in fp32.)
+// The weight does not depend on the previous kernel and is read before the
+// dependency wait.
 template <int HD, int NSUB>
-__global__ void __launch_bounds__(LR_THREADS)
+__global__ void __launch_bounds__(HD / 4)
     llm_rms_kernel(float* __restrict__ h, const __nv_bfloat16* __restrict__ in,
                    const float* __restrict__ sub, size_t sub_plane, int M,
                    const float* __restrict__ w, float eps, __nv_bfloat16* __restrict__ out) {
-  static_assert(HD % 512 == 0, "width: a multiple of 512");
-  constexpr int V = HD / 512;   // float4 groups per thread
-  __shared__ float red[LR_ROWS_PER_BLOCK][4];
-  const int rb = threadIdx.x >> 7, t = threadIdx.x & 127;
-  const int wi = t >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * LR_ROWS_PER_BLOCK + rb;
+  static_assert(HD % 128 == 0 && HD / 4 <= 1024, "width");
+  constexpr int NW = HD / 128;   // warps per row
+  __shared__ float red[NW];
+  const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, col = t * 4;
+  const float4 wv = *reinterpret_cast<const float4*>(w + col);
   pdl_trigger();
   pdl_wait();
-  const bool valid = r < M;
-  float4 x[V], wv[V];
-  float ss = 0.f;
+  if (r >= M) return;
+  const size_t off = static_cast<size_t>(r) * HD + col;
+  float4 x;
+  if constexpr (NSUB == 0) {
+    const uint2 u = *reinterpret_cast<const uint2*>(in + off);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    x = make_float4(a.x, a.y, b.x, b.y);
+  } else {
+    float4 sp[NSUB];
+    x = *reinterpret_cast<const float4*>(h + off);
 #pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int col = j * 512 + t * 4;
-    x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    wv[j] = x[j];
-    if (!valid) continue;
-    wv[j] = *reinterpret_cast<const float4*>(w + col);
-    const size_t off = static_cast<size_t>(r) * HD + col;
-    if constexpr (NSUB == 0) {
-      const uint2 u = *reinterpret_cast<const uint2*>(in + off);
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-      x[j] = make_float4(a.x, a.y, b.x, b.y);
-    } else {
-      x[j] = *reinterpret_cast<const float4*>(h + off);
+    for (int p = 0; p < NSUB; ++p) sp[p] = *reinterpret_cast<const float4*>(sub + p * sub_plane + off);
 #pragma unroll
-      for (int p = 0; p < NSUB; ++p) {
-        const float4 s = *reinterpret_cast<const float4*>(sub + p * sub_plane + off);
-        x[j].x += s.x; x[j].y += s.y; x[j].z += s.z; x[j].w += s.w;
-      }
+    for (int p = 0; p < NSUB; ++p) {
+      x.x += sp[p].x; x.y += sp[p].y; x.z += sp[p].z; x.w += sp[p].w;
     }
-    *reinterpret_cast<float4*>(h + off) = x[j];
-    ss += x[j].x * x[j].x + x[j].y * x[j].y + x[j].z * x[j].z + x[j].w * x[j].w;
   }
+  *reinterpret_cast<float4*>(h + off) = x;
+  float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
   ss = warp_sum(ss);
-  if (lane == 0) red[rb][wi] = ss;
+  if (lane == 0) red[t >> 5] = ss;
   __syncthreads();
-  if (!valid) return;
-  const float ms = ((red[rb][0] + red[rb][1]) + (red[rb][2] + red[rb][3])) * (1.0f / HD);
-  const float rs = rsqrtf(ms + eps);
+  float tot = 0.f;
 #pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int col = j * 512 + t * 4;
-    *reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * HD + col) =
-        make_uint2(pack_bf16(x[j].x * rs * wv[j].x, x[j].y * rs * wv[j].y),
-                   pack_bf16(x[j].z * rs * wv[j].z, x[j].w * rs * wv[j].w));
-  }
+  for (int i = 0; i < NW; ++i) tot += red[i];
+  const float rs = rsqrtf(tot * (1.0f / HD) + eps);
+  *reinterpret_cast<uint2*>(out + off) =
+      make_uint2(pack_bf16(x.x * rs * wv.x, x.y * rs * wv.y), pack_bf16(x.z * rs * wv.z, x.w * rs * wv.w));
 }
 
 // qkv = bias + sum of the QKV projection's nsplit fp32 split-K planes
