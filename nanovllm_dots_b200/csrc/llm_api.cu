@@ -435,9 +435,8 @@ int dllm_decode_step(void* handle, const DllmStep* st, void* workspace, size_t w
     CK(llm_swap<LS_F32>(hd->m_qkv[l], hd->a_xn, qkvw, Hd, n, kLlmQkvSplit, f32(hd->ws.qkv),
                       static_cast<size_t>(c.max_batch) * qkvw, err, s));
     const int cnt = n * (H + 2 * KVH) * (D / 2);
-    CK(launch_pdl(llm_rope_kernel, dim3((cnt + 255) / 256), dim3(256), 0, s,
-                  static_cast<const float*>(f32(hd->ws.qkv)), kLlmQkvSplit,
-                  static_cast<size_t>(c.max_batch) * qkvw,
+    CK(launch_pdl(llm_rope_kernel<kLlmQkvSplit>, dim3((cnt + 255) / 256), dim3(256), 0, s,
+                  static_cast<const float*>(f32(hd->ws.qkv)), static_cast<size_t>(c.max_batch) * qkvw,
                   static_cast<const float*>(w.qkv_b + static_cast<size_t>(l) * qkvw), st->positions,
                   w.inv_freq, n, H, KVH, D, bf(hd->ws.qr),
                   static_cast<__nv_bfloat16*>(const_cast<void*>(hd->kc_ptr[l])),

@@ -67,9 +67,12 @@ __global__ void __launch_bounds__(HD / 4)
 // ``layers/rotary_embedding.py:6-47``), v unrotated; k and v go straight into
 // the paged caches at the token's slot (``store_kvcache``,
 // ``layers/attention.py:10-47``: slot < 0 skips the token, a slot past the
-// cache is reported and skipped).  One thread per (row, head, rotary pair).
+// cache is reported and skipped).  One thread per (row, head, rotary pair);
+// the plane count is a compile-time constant so every plane load is issued
+// before the first add.
+template <int NSPLIT>
 __global__ void __launch_bounds__(256)
-    llm_rope_kernel(const float* __restrict__ qkv, int nsplit, size_t plane,
+    llm_rope_kernel(const float* __restrict__ qkv, size_t plane,
                     const float* __restrict__ bias, const int* __restrict__ positions,
                     const float* __restrict__ inv_freq, int n, int H, int KVH, int D,
                     __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k_cache,
@@ -99,9 +102,16 @@ __global__ void __launch_bounds__(256)
   const int c1 = hd * D + d, c2 = c1 + half;
   const float* src = qkv + static_cast<size_t>(i) * heads * D;
   float x1 = bias[c1], x2 = bias[c2];
-  for (int p = 0; p < nsplit; ++p) {
-    x1 += src[p * plane + c1];
-    x2 += src[p * plane + c2];
+  float a1[NSPLIT], a2[NSPLIT];
+#pragma unroll
+  for (int p = 0; p < NSPLIT; ++p) {
+    a1[p] = src[p * plane + c1];
+    a2[p] = src[p * plane + c2];
+  }
+#pragma unroll
+  for (int p = 0; p < NSPLIT; ++p) {
+    x1 += a1[p];
+    x2 += a2[p];
   }
   if (hd >= H + KVH) {   // v: no rotation
     dst[d] = __float2bfloat16(x1);
