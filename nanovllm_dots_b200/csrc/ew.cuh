@@ -27,7 +27,7 @@ constexpr int LN_THREADS = 128 * LN_ROWS_PER_BLOCK;
 // Only LN_ADALN reads a gate; the others add sub with a gate of ones (the
 // encoder's plain residual, ``patch_encoder.py:82-86``).
 template <int NSUB, int MODE>
-__global__ void __launch_bounds__(LN_THREADS)
+__global__ void __launch_bounds__(LN_THREADS, NSUB <= 2 ? 8 : 5)
     ln_mod_kernel(float* __restrict__ h, const float* __restrict__ sub, size_t sub_plane,
                   const float* __restrict__ gate, int M, RowMap in_map,
                   const float* __restrict__ shift, const float* __restrict__ scale, int mod_ld,
@@ -35,8 +35,11 @@ __global__ void __launch_bounds__(LN_THREADS)
                   uint8_t* __restrict__ out8, float* __restrict__ out_scale) {
   // 128 threads (4 warps) per row, two rows per block: thread t of a row owns
   // the 16-byte column groups t and t + 128 (each warp's accesses are 512
-  // contiguous bytes), and the shift / scale vectors are loaded with the row.
-  // One warp per row left the kernel latency-bound (few warps per SM, each
+  // contiguous bytes).  The shift / scale vectors are read after the row
+  // statistics, which keeps the kernel at 32 registers: 8 blocks (16 rows)
+  // per SM, so config 2's 1088 blocks run in one wave (loaded with the row,
+  // 54 registers allowed 4 blocks per SM: 1.84 waves, measured slower).  One
+  // warp per row left the kernel latency-bound (few warps per SM, each
   // waiting on its own chain of loads).
   constexpr int H = 1024;
   __shared__ float red[LN_ROWS_PER_BLOCK][3][4];   // [row][sum | centred squares | absmax][warp]
@@ -57,10 +60,6 @@ __global__ void __launch_bounds__(LN_THREADS)
     for (int j = 0; j < 2; ++j) {
       const int col = j * 512 + t * 4;
       x[j] = *reinterpret_cast<const float4*>(hr + col);
-      if constexpr (norm) {   // the modulation / affine vectors, loaded before they are needed
-        a_sh[j] = *reinterpret_cast<const float4*>(shift + req * mod_ld + col);
-        b_sc[j] = *reinterpret_cast<const float4*>(scale + req * mod_ld + col);
-      }
     }
     if (sub) {
       const float* sr = sub + hrow;
@@ -112,6 +111,15 @@ __global__ void __launch_bounds__(LN_THREADS)
     const float var = ((red[rb][1][0] + red[rb][1][1]) + (red[rb][1][2] + red[rb][1][3])) * (1.0f / H);
     const float rstd = rsqrtf(var + eps);
     constexpr float one = MODE == LN_ADALN ? 1.f : 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int col = j * 512 + t * 4;
+      a_sh[j] = b_sc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid) {
+        a_sh[j] = *reinterpret_cast<const float4*>(shift + req * mod_ld + col);
+        b_sc[j] = *reinterpret_cast<const float4*>(scale + req * mod_ld + col);
+      }
+    }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       x[j].x = (x[j].x - mean) * rstd * (one + b_sc[j].x) + a_sh[j].x;
