@@ -285,12 +285,14 @@ bool voc_halo(const VocConv& v) {
   return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.u == 1 && v.off0 == -(v.taps - 1) * v.dil;
 }
 
-// Tiles of the narrow convolutions: one tile of N = 32 or 64, else 96/128
-// columns.  At N = 32 the residual is staged by TMA in two buffers (two CTAs
-// per SM still fit); at 64 a single buffer measured slower than the direct
-// loads, which the wider tiles keep.
+// Tiles of the resblock convolutions: one tile of N = 32 or 64, else 256 or
+// 192 columns with one accumulator buffer (256 TMEM columns, so two CTAs per
+// SM still fit), else 128/96 double-buffered.  At N = 32 the residual is
+// staged by TMA in two buffers; at 64 a single buffer measured slower than
+// the direct loads, which the wider tiles keep.
 int voc_halo_bn(int N) {
-  return N == 32 ? 32 : N == 64 ? 64 : N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : 32;
+  return N == 32 ? 32 : N == 64 ? 64 : N % 256 == 0 ? 256 : N % 192 == 0 ? 192 : N % 128 == 0 ? 128
+         : N % 96 == 0 ? 96 : 32;
 }
 
 cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& amap, int n,
@@ -320,6 +322,7 @@ cudaError_t voc_conv(const VocHandle& h, const VocConv& v, const CUtensorMap& am
   if (halo_map && voc_halo(v)) {
     switch (voc_halo_bn(v.N)) {
       case 256: return voc_halo_launch<256, 3, 4, 0, 1, 1>(*halo_map, v.wmap, *halo_map, p, err, s);
+      case 192: return voc_halo_launch<192, 3, 6, 0, 1, 1>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 128: return voc_halo_launch<128, 3, 6>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 96: return voc_halo_launch<96, 3, 8>(*halo_map, v.wmap, *halo_map, p, err, s);
       case 64: return voc_halo_launch<64, 2, 8, 0, 2>(*halo_map, v.wmap, *halo_map, p, err, s);
