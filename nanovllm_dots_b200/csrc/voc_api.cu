@@ -25,6 +25,7 @@ struct VocConv {
   int N;              // output columns
   int taps, off0, dil;
   int u, cp_out;      // transposed conv: u phases of cp_out columns; else u = 1
+  bool rows128 = false;  // input rows only a multiple of 128 (conv_pre's output)
   size_t w_off, b_off;
   CUtensorMap wmap;
 };
@@ -47,6 +48,7 @@ struct VocHandle {
   int plan_n = -1, plan_t = -1;
   CUtensorMap m_din;
   CUtensorMap m_xin[DVOC_MAX_STAGES];
+  CUtensorMap m_xin_h[DVOC_MAX_STAGES];  // 64-frame boxes (transposed convs on the halo kernel)
   CUtensorMap m_act[DVOC_MAX_STAGES];
   CUtensorMap m_act_h[DVOC_MAX_STAGES];  // 64-frame boxes (halo kernel)
   CUtensorMap m_u[DVOC_MAX_STAGES];      // residual sources of the resblock convs
@@ -108,6 +110,7 @@ void voc_tables(VocHandle& h) {
   for (int i = 0; i < h.ns; ++i) {
     const int cin_p = i ? vpad(h.ch[i - 1]) : c0p, cp = vpad(h.ch[i]), u = c.upsample_rates[i];
     add(cin_p, u * cp, 2, -1, 1, u, cp);
+    h.convs.back().rows128 = i == 0;
     for (int j = 0; j < h.nk; ++j) {
       const int k = c.resblock_kernel_sizes[j];
       const int nl = c.resblock_type == 1 ? 3 : 2;
@@ -278,11 +281,16 @@ cudaError_t voc_halo_launch(const CUtensorMap& a, const CUtensorMap& w, const CU
   return launch_pdl(fn, dim3(grid), dim3(VC_THREADS), smem, s, a, w, res, p, err);
 }
 
-// The resblock convolutions (causal, taps spanning at most VH_HALO frames)
-// run on the halo kernel: one A tile per channel block for all taps.  conv_pre
-// (centred) and the transposed convs stay on voc_conv_kernel.
+int voc_halo_bn(int N);
+
+// The resblock convolutions and the transposed convs (causal, taps spanning at
+// most VH_HALO frames) run on the halo kernel: one A tile per channel block
+// for all taps.  conv_pre (centred) stays on voc_conv_kernel, and so does a
+// transposed conv whose tile would be 256 frames (N <= 64) over conv_pre's
+// output, whose rows are only a multiple of 128.
 bool voc_halo(const VocConv& v) {
-  return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.u == 1 && v.off0 == -(v.taps - 1) * v.dil;
+  return v.taps > 1 && (v.taps - 1) * v.dil <= VH_HALO && v.off0 == -(v.taps - 1) * v.dil &&
+         !(v.rows128 && voc_halo_bn(v.N) <= 64);
 }
 
 // Tiles of the resblock convolutions: one tile of N = 32 or 64, else 256 or
@@ -532,6 +540,7 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
     for (int i = 0; ok && i < h->ns; ++i) {
       const int cin_p = i ? vpad(h->ch[i - 1]) : c0p, rows_in = i ? r.cap[i - 1] : r.cpre;
       ok = voc_map_act(&h->m_xin[i], P(h->o_x16), n, rows_in, cin_p) &&
+           voc_map_act(&h->m_xin_h[i], P(h->o_x16), n, rows_in, cin_p, VH_BOX) &&
            voc_map_act(&h->m_act[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i])) &&
            voc_map_act(&h->m_act_h[i], P(h->o_a), n, r.cap[i], vpad(h->ch[i]), VH_BOX) &&
            voc_map_f32(&h->m_u[i], P(h->o_u), n, r.cap[i], vpad(h->ch[i])) &&
@@ -610,7 +619,8 @@ static int voc_run(void* handle, const DvocBatch* b, void* workspace, size_t wor
     __half* A = reinterpret_cast<__half*>(P(h->o_a));     // activation outputs (conv operands)
     __half* C1 = reinterpret_cast<__half*>(P(h->o_c1));   // conv1 outputs (read only by act2)
     if (pick(li))
-      VCK(voc_conv(*h, h->convs[li], h->m_xin[i], n, rows_in, U, ob, rows, nullptr, 0, 1.0f, err, s));
+      VCK(voc_conv(*h, h->convs[li], h->m_xin[i], n, rows_in, U, ob, rows, nullptr, 0, 1.0f, err, s,
+                   &h->m_xin_h[i]));
     ++li;
     for (int j = 0; j < h->nk; ++j) {
       const int nl = c.resblock_type == 1 ? 3 : 2;
