@@ -1249,7 +1249,7 @@ def run_voc(args, rank, world, oneshot: bool, n: int = 64):
                         "ms_per_step": round(e2e_ms, 4), "api": "decode_batch" if oneshot else "stream_step_many"},
                 "eager_ms_per_step": round(eager_ms, 4),
                 "gpu_launches": voc_launches(cfg, F, oneshot, voc.num_convs) * args.steps,
-                "roofline": {"kernel": f"convolution #{heavy} (the call's largest; voc_conv_halo_kernel)",
+                "roofline": {"kernel": f"convolution #{heavy} (the call's largest)",
                              "bound": "tensor", "achieved": round(ach(flops[heavy], conv_us[heavy]), 1),
                              "peak": round(f16, 1), "unit": "TFLOP/s",
                              "frac": round(ach(flops[heavy], conv_us[heavy]) / f16, 4), "traffic": None,
