@@ -5,8 +5,8 @@ methods in a loop: the events (order, kinds, audio) and the per-request
 bookkeeping must be identical.  The script of steps covers streaming requests
 with one and several pending patches, a stream that finishes without a patch
 (no flush audio), one-shot requests finishing with and without latents, and
-``vocode=False``.  Needs the reference checkout (DFM_REFERENCE, default the
-sibling path used to make the golden fixtures); skipped without it."""
+``vocode=False``.  Needs the reference checkout (DFM_REFERENCE, default a
+``reference`` folder beside this repository); skipped without it."""
 from __future__ import annotations
 
 import os
@@ -18,7 +18,10 @@ import torch
 
 from nanovllm_dots_b200.vocoder import batched_step_stream, install_vocoder
 
-REF = os.environ.get("DFM_REFERENCE", "/root/reference")
+# the checkout named by DFM_REFERENCE, else a `reference` folder beside this
+# repository
+REF = os.environ.get("DFM_REFERENCE") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
 
 
 def _reference():
