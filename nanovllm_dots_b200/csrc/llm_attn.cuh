@@ -110,8 +110,19 @@ __global__ void __launch_bounds__(LA_THREADS)
   pdl_wait();
   const int c = blockIdx.x, g = blockIdx.y, i = blockIdx.z;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int ctx = p.context_lens[i];
   const int k0 = c * LA_CHUNK;
+  const int* bt = p.block_table + static_cast<size_t>(i) * p.max_blocks;
+  // the block ids of the first sub-tiles depend only on the chunk: read them
+  // together with the context length instead of after it
+  int blk0[LA_NBUF];
+  if (t == 0) {
+#pragma unroll
+    for (int j = 0; j < LA_NBUF; ++j) {
+      const int bi = (k0 + j * LA_SUB) / p.block_size;
+      blk0[j] = bi < p.max_blocks ? bt[bi] : -1;
+    }
+  }
+  const int ctx = p.context_lens[i];
   if (ctx < 1 || ctx > p.max_blocks * p.block_size) {
     if (c == 0 && g == 0 && t == 0) atomicOr(p.err, DFM_DEV_ERR_LEN);
     return;
@@ -135,12 +146,10 @@ __global__ void __launch_bounds__(LA_THREADS)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + LA_NBUF);
 
-  const int* bt = p.block_table + static_cast<size_t>(i) * p.max_blocks;
   // one sub-tile: D / 64 boxes of K and of V for keys [kk, kk + 64) of this chunk
-  auto issue = [&](int j) {
+  auto issue = [&](int j, int blk) {
     const int key = k0 + j * LA_SUB;
     const int bi = key / p.block_size;
-    int blk = bt[bi];
     if (blk < 0 || blk >= p.num_blocks) {
       atomicOr(p.err, DFM_DEV_ERR_PAGE);
       blk = p.num_blocks;   // out of range: TMA fills zeros
@@ -159,7 +168,9 @@ __global__ void __launch_bounds__(LA_THREADS)
     for (int b = 0; b < LA_NBUF; ++b) mbar_init(&full[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
-    for (int j = 0; j < LA_NBUF && j < nsub; ++j) issue(j);
+#pragma unroll
+    for (int j = 0; j < LA_NBUF; ++j)
+      if (j < nsub) issue(j, blk0[j]);
   }
   // the group's queries, pre-scaled into log2 units
   const __nv_bfloat16* qg = p.q + (static_cast<size_t>(i) * p.H + g * G) * D;
@@ -272,7 +283,8 @@ __global__ void __launch_bounds__(LA_THREADS)
       }
     }
     __syncthreads();   // buffer j % LA_NBUF, s_part and s_p are free again
-    if (t == 0 && j + LA_NBUF < nsub) issue(j + LA_NBUF);
+    if (t == 0 && j + LA_NBUF < nsub)
+      issue(j + LA_NBUF, bt[(k0 + (j + LA_NBUF) * LA_SUB) / p.block_size]);
   }
   if (!ok) return;
   // ---- unnormalised partial of this chunk
