@@ -888,10 +888,27 @@ __global__ void __launch_bounds__(32 * VS_J)
   }
   pdl_wait();
   pdl_trigger();
-#pragma unroll 1
-  for (int i = threadIdx.x; i < 32 * Hm; i += 32 * VS_J) {
-    const int bl = i / Hm, k = i - bl * Hm;
-    hs[k * 33 + bl] = (b0 + bl < n) ? h_prev[static_cast<size_t>(b0 + bl) * Hm + k] : 0.0f;
+  // h_prev of the 32 requests, 16 bytes per load and eight loads in flight
+  // per thread (Hm is a multiple of 4); a misaligned state pointer takes
+  // scalar loads
+  if ((reinterpret_cast<uintptr_t>(h_prev) & 15) == 0) {
+#pragma unroll 8
+    for (int i = threadIdx.x * 4; i < 32 * Hm; i += 32 * VS_J * 4) {
+      const int bl = i / Hm, k = i - bl * Hm;
+      const float4 v = (b0 + bl < n)
+                           ? __ldcg(reinterpret_cast<const float4*>(h_prev + static_cast<size_t>(b0 + bl) * Hm + k))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      hs[k * 33 + bl] = v.x;
+      hs[(k + 1) * 33 + bl] = v.y;
+      hs[(k + 2) * 33 + bl] = v.z;
+      hs[(k + 3) * 33 + bl] = v.w;
+    }
+  } else {
+#pragma unroll 8
+    for (int i = threadIdx.x; i < 32 * Hm; i += 32 * VS_J) {
+      const int bl = i / Hm, k = i - bl * Hm;
+      hs[k * 33 + bl] = (b0 + bl < n) ? h_prev[static_cast<size_t>(b0 + bl) * Hm + k] : 0.0f;
+    }
   }
   __syncthreads();
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
