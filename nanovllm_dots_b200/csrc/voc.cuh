@@ -781,7 +781,7 @@ __global__ void __launch_bounds__(VP_T)
 #pragma unroll 1
   for (int c0 = 0; c0 < cp; c0 += 32) {
     __syncthreads();
-#pragma unroll 1
+#pragma unroll 8   // independent loads: eight in flight per thread
     for (int i = threadIdx.x; i < (VP_T + 6) * 32; i += VP_T) {
       const int r = i >> 5, cc = i & 31;
       const int f = t0 - 6 + r;
