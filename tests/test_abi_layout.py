@@ -69,3 +69,13 @@ def test_headers_declare_no_field_the_mirror_lacks(c_layout):
         end = getattr(cls, field).offset + ctypes.sizeof(ftype)
         align = max(ctypes.alignment(t) for _, t in cls._fields_)
         assert c_layout[(name, "sizeof")] == (end + align - 1) // align * align, name
+
+
+def test_integration_guide_names_only_exported_functions():
+    """The C bindings INTEGRATION.md shows a maintainer call only functions
+    the library exports."""
+    import re
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    names = set(re.findall(r"\b((?:dfm|dpe|dllm|dvoc)_[a-z_0-9]+)", text))
+    assert names, "no C function named"
+    assert sorted(n for n in names if n not in _lib.EXPORTS) == []
