@@ -189,7 +189,6 @@ LlmStepWs llm_step_layout(const DllmConfig& c, int qkvw, int mc) {
     return o;
   };
   const size_t NR = c.max_batch, Hd = c.hidden, HD = static_cast<size_t>(c.heads) * c.head_dim;
-  const size_t KD = static_cast<size_t>(c.kv_heads) * c.head_dim;
   L.err = take(256);   // offset 0: dllm_read_error reads it
   L.h = take(NR * Hd * 4);
   L.xn = take(NR * Hd * 2);
