@@ -6,6 +6,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import pathlib
 import re
 
 import pytest
@@ -27,7 +28,7 @@ def declared_functions():
     names = set()
     for path, prefix in ((HEADER, "dfm_"), (PE_HEADER, "dpe_"), (LLM_HEADER, "dllm_"),
                          (VOC_HEADER, "dvoc_")):
-        src = open(path).read()
+        src = pathlib.Path(path).read_text()
         found = re.findall(rf"^\s*(?:int|int32_t|size_t|const char\*)\s+({prefix}\w+)\s*\(", src, re.M)
         assert found, f"no declarations parsed from {path}"
         names |= set(found)
@@ -44,7 +45,7 @@ def test_library_builds_and_exports_every_declared_symbol():
 
 
 def test_struct_layouts_match_header():
-    src = open(HEADER).read()
+    src = pathlib.Path(HEADER).read_text()
     body = src[src.index("typedef struct DfmWeights"):src.index("} DfmWeights;")]
     n_ptr = len(re.findall(r"const (?:void|float)\*\s+\w+", body))
     assert n_ptr == len(_lib.WEIGHT_FIELDS)
@@ -120,7 +121,7 @@ def test_pack_weights_fp8_rowwise(weights):
 
 
 def test_pe_struct_layouts_and_pool_bytes():
-    src = open(PE_HEADER).read()
+    src = pathlib.Path(PE_HEADER).read_text()
     body = src[src.index("typedef struct DpeWeights"):src.index("} DpeWeights;")]
     assert len(re.findall(r"const (?:void|float)\*\s+\w+", body)) == len(_lib.PE_WEIGHT_FIELDS)
     assert ctypes.sizeof(_lib.DpeConfig) == 12 * 4

@@ -75,7 +75,8 @@ def test_integration_guide_names_only_exported_functions():
     """The C bindings INTEGRATION.md shows a maintainer call only functions
     the library exports."""
     import re
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+        text = f.read()
     names = set(re.findall(r"\b((?:dfm|dpe|dllm|dvoc)_[a-z_0-9]+)", text))
     assert names, "no C function named"
     assert sorted(n for n in names if n not in _lib.EXPORTS) == []
