@@ -1170,7 +1170,10 @@ def run_voc(args, rank, world, oneshot: bool, n: int = 64):
         conv_us.append(c0.elapsed_time(c1) * 1000 / reps)
     voc.check_errors()
     hbm, bf16, peak_kind = load_peaks()
-    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if peak_kind == "measured" else {}
+    peaks = {}
+    if peak_kind == "measured":
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
     f16 = peaks.get("bf16_tflops_sustained", 1400.0)   # kind::f16 runs fp16 at the bf16 rate
     conv_total_us = sum(conv_us)
     top = max(range(len(conv_us)), key=lambda i: conv_us[i] * 1.0)
